@@ -1,0 +1,265 @@
+/* maya3_b200.h -- C ABI of the B200-native Maya3 decode tick.
+ *
+ * One shared library (libm3b200.so, sm_100a) exports the per-tick hot path of Maya3's streaming TTS engine: the
+ * Qwen3 backbone decode over a static per-seat KV cache, the cb0 sampler with controlled stop, the depth
+ * transformer's RVQ level loop with top-k sampling, and the one-frame Mimi decoder.  It replaces the reference's
+ * serve-side components (serve/fast_backbone.py, serve/fast_depth.py, serve/fast_depth_kernels.py,
+ * serve/fast_codec.py and Engine._cb0 in maya3/engine.py) behind the same seat interface.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Every tensor argument is a DEVICE pointer unless marked "host".
+ *   - Weights and per-seat state (KV caches, lengths, sampler state, codec state) are owned by the caller and must
+ *     outlive the handle; a handle owns only its scratch memory, allocated once by *_create.
+ *   - Every call that does device work takes a cudaStream_t (passed as void*) and only enqueues work: no host
+ *     synchronisation and no allocation, so a step can be captured into a CUDA graph by the caller.
+ *   - Functions return M3_OK (0) or a negative M3_ERR_*; m3_last_error() describes the last failure on the calling
+ *     thread.  Problems seen inside kernels (slot or position out of range, a timed-out wait) are recorded in the
+ *     handle's device status word and read back with *_status() after the caller's own synchronisation.
+ *   - Row arrays (slots, offsets, real, codes) are int64, as the reference's torch.long tensors.
+ *   - Slot `max_slots` is the padding ("dummy") slot, as in the reference: bucket padding rows point at it.
+ */
+#ifndef MAYA3_B200_H
+#define MAYA3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  M3_OK = 0,
+  M3_ERR_ARG = -1,         /* bad argument: shape, size, pointer (reference raises ValueError) */
+  M3_ERR_CUDA = -2,        /* a CUDA or cuBLAS call failed */
+  M3_ERR_RANGE = -3,       /* slot / bucket out of range (reference raises IndexError / ValueError) */
+  M3_ERR_UNSUPPORTED = -4  /* geometry this build does not implement */
+};
+
+enum { /* device status word values */
+  M3_DEV_OK = 0,
+  M3_DEV_BAD_SLOT = 1,     /* a row named a slot outside [0, max_slots]; it was redirected to the dummy slot */
+  M3_DEV_BAD_POS = 2,      /* a position reached the KV capacity; the row was clamped */
+  M3_DEV_BAD_CODE = 3,     /* a code outside [0, n_codes) reached an embedding table; it was clamped */
+  M3_DEV_TIMEOUT = 4       /* a bounded wait inside a kernel gave up */
+};
+
+typedef void* m3_stream; /* cudaStream_t */
+
+#if defined(__GNUC__)
+#define M3_API __attribute__((visibility("default")))
+#else
+#define M3_API
+#endif
+
+M3_API const char* m3_last_error(void);
+M3_API int m3_version(void);
+
+/* ---------------------------------------------------------------------------------------------- utilities */
+/* Y[M,N] = X[M,K] . W[N,K]^T, bf16 inputs, fp32 accumulation, Y bf16 (y_f32 = 0) or fp32 (y_f32 = 1).
+ * Row-major with leading dimensions ldx, ldw, ldy (elements).  Replaces F.linear on the serving path
+ * (serve/fast_backbone.py:193,200-202; serve/fast_depth.py:150,167,185-191; serve/fast_codec.py:140,168-181). */
+M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
+                 int32_t n, int32_t k, int32_t y_f32, m3_stream stream);
+
+/* ---------------------------------------------------------------------------------------------- backbone */
+/* Replaces StaticBackbone (serve/fast_backbone.py:111-362): the static-KV Qwen3 decode with per-seat positions. */
+typedef struct m3_backbone m3_backbone;
+
+typedef struct {
+  int32_t layers, hidden, heads, kv_heads, head_dim, ffn;
+  int32_t max_slots;  /* real seats; slot max_slots is the dummy */
+  int32_t capacity;   /* KV positions per seat */
+  int32_t max_rows;   /* largest row bucket a step may use (decode rows + inline prefill rows) */
+  float eps;          /* RMSNorm epsilon */
+} m3_backbone_config;
+
+typedef struct {
+  /* host arrays of `layers` device pointers; all tensors bf16 row-major */
+  const void* const* in_norm;   /* [hidden]                                  input_layernorm.weight */
+  const void* const* wqkv;      /* [(heads + 2 kv_heads) head_dim, hidden]   q|k|v proj rows (fast_backbone.py:135) */
+  const void* const* q_norm;    /* [head_dim] */
+  const void* const* k_norm;    /* [head_dim] */
+  const void* const* wo;        /* [hidden, heads head_dim] */
+  const void* const* post_norm; /* [hidden] */
+  const void* const* wgu;       /* [2 ffn, hidden]  gate rows then up rows (fast_backbone.py:139) */
+  const void* const* wdown;     /* [hidden, ffn] */
+  const void* final_norm;       /* [hidden] */
+  const void* cos;              /* [capacity, head_dim] RoPE tables in the model dtype (fast_backbone.py:152-153) */
+  const void* sin;
+  void* const* k_cache;         /* per layer [max_slots + 1, kv_heads, capacity, head_dim] (fast_backbone.py:146-148) */
+  void* const* v_cache;
+  int64_t* lengths;             /* [max_slots + 1] tokens held per slot (fast_backbone.py:149) */
+} m3_backbone_weights;
+
+M3_API int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbone_weights* w, m3_backbone** out);
+M3_API int m3_backbone_destroy(m3_backbone* bb);
+/* One graphed step of StaticBackbone._forward (serve/fast_backbone.py:176-234) over `rows` rows.
+ * slots [rows]: the slot of each row (inline-prefill rows repeat their slot, padding rows use the dummy);
+ * offsets [rows] or NULL: position offset of each prefill row (0 for decode rows); real [rows] or NULL: 1 for
+ * rows that advance their slot's length (NULL = all rows); x [rows, hidden] bf16 input; out [rows, hidden] bf16
+ * final-normed hidden state.  ctx: context bucket, at least max(lengths[slot] + offset) + 1 over the rows.
+ * Each row attends over keys 0..pos of its slot, pos = lengths[slot] + offset; every row's K/V is written before
+ * any row attends, so prefill rows form an exact causal prefill (fast_backbone.py:326-333). */
+M3_API int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* offsets, const int64_t* real,
+                     const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream);
+/* Read (and optionally clear) the device status word; synchronises with the device. */
+M3_API int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clear);
+
+/* ---------------------------------------------------------------------------------------------- cb0 sampler */
+/* Replaces Engine._cb0 + Backbone.cb0_logits + row_exponential (maya3/engine.py:652-694,
+ * tts/model/backbone.py:97, serve/fast_depth_kernels.py:339-355): per-seat temperature, top-k, top-p, presence
+ * penalty, controlled stop and the per-request Philox stream. */
+typedef struct m3_cb0 m3_cb0;
+
+typedef struct {
+  int32_t hidden;
+  int32_t n_cls;      /* 2049 = 2048 codes + AEOS */
+  int32_t max_slots;
+  int32_t max_rows;
+  int32_t rep_win;    /* presence-penalty window (frames of cb0 history) */
+} m3_cb0_config;
+
+typedef struct {         /* per-slot state tensors of maya3/engine.py:210-223, each [max_slots + 1] */
+  const void* head;      /* bf16 [n_cls, hidden]  cb0_head.weight */
+  int64_t* frames;       /* frames generated by the seat */
+  const int64_t* min_frames;
+  float* hazard;
+  const float* aeos_bias;
+  const float* temp;
+  const int64_t* top_k;
+  const float* top_p;
+  const float* rep;
+  const int32_t* seed;
+  int32_t* ctr;
+  int64_t* hist;         /* [max_slots + 1, rep_win] last cb0 codes, -1 = empty */
+} m3_cb0_state;
+
+M3_API int m3_cb0_create(const m3_cb0_config* cfg, const m3_cb0_state* st, m3_cb0** out);
+M3_API int m3_cb0_destroy(m3_cb0* s);
+/* h [rows, hidden] bf16, idx [rows] slot per row -> stop code [rows] (0 or REASONS 2/3/4, maya3/engine.py:46) and
+ * cb0 [rows] in [0, 2047]; advances the per-slot state.  apply_rep / apply_top_p mirror the engine's host flags
+ * (`cb0_rep_win > 0 and (cb0_rep > 0 or any_rep)`, `_any_top_p`). */
+M3_API int m3_cb0_step(m3_cb0* s, const void* h, const int64_t* idx, int64_t* code, int64_t* cb0, int32_t rows,
+                int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
+/* The sampler alone on given fp32 logits [rows, n_cls] (the cb0 head output as fp32). */
+M3_API int m3_cb0_sample_logits(m3_cb0* s, const float* logits, const int64_t* idx, int64_t* code, int64_t* cb0,
+                         int32_t rows, int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
+
+/* ---------------------------------------------------------------------------------------------- depth */
+/* Replaces FastDepth (serve/fast_depth.py:32-257) with its fused kernels (serve/fast_depth_kernels.py). */
+typedef struct m3_depth m3_depth;
+
+typedef struct {
+  int32_t layers, d, heads, ffn;
+  int32_t n_q;            /* codebooks per frame: cb0 + n_q - 1 depth levels */
+  int32_t n_codes;
+  int32_t d_backbone;
+  int32_t n_groups;
+  int32_t group_of_level[64];  /* level -> weight group; entry 0 unused (tts/model/depth_v2.py:45) */
+  int32_t max_slots, max_rows;
+  float ln_eps;
+  float inv_temp;         /* 1 / sampler temperature, computed in double and rounded once (Triton's fp32 argument) */
+  int32_t top_k;
+  int32_t greedy;         /* argmax instead of sampling */
+} m3_depth_config;
+
+typedef struct {
+  const void* in_proj;    /* [d, d_backbone] */
+  const void* embed;      /* [n_q - 1, n_codes, d] prefix table code_up(code_lo) + level_emb[1:] (fast_depth.py:49-50) */
+  const void* level0;     /* [d] level_emb[0] */
+  /* host arrays of n_groups * layers device pointers, index group * layers + layer */
+  const void* const* n1_w; const void* const* n1_b;
+  const void* const* n2_w; const void* const* n2_b;
+  const void* const* qkv;  /* [3d, d] */
+  const void* const* o;    /* [d, d] */
+  const void* const* f1;   /* [ffn, d] */
+  const void* const* f2;   /* [d, ffn] */
+  const void* norm_w; const void* norm_b;
+  const void* const* heads;   /* host array of n_q - 1 pointers, each [n_codes, d] */
+  const void* const* cross_kv; /* host array of `layers` pointers, each [2d, d] (speaker cross-attn kv) */
+  const void* const* cross_o;  /* host array of `layers` pointers, each [d, d] */
+  const void* audio_table;     /* [n_q n_codes, d_backbone] AudioInputEmbed.table */
+  const void* audio_norm;      /* [d_backbone] AudioInputEmbed.norm.weight */
+  void* cross_const;           /* [max_slots + 1, layers, d] per-slot speaker constants (fast_depth.py:56) */
+  int32_t* row_seed;           /* [max_slots + 1] per-slot Philox seed (fast_depth.py:66) */
+  int32_t* row_ctr;            /* [max_slots + 1] per-slot frame counter */
+} m3_depth_weights;
+
+M3_API int m3_depth_create(const m3_depth_config* cfg, const m3_depth_weights* w, m3_depth** out);
+M3_API int m3_depth_destroy(m3_depth* d);
+/* FastDepth.set_speaker (serve/fast_depth.py:72-82): mem [d] bf16, keep = the reference mask (0 or 1). */
+M3_API int m3_depth_set_speaker(m3_depth* d, int32_t slot, const void* mem, float keep, m3_stream stream);
+/* FastDepth.__call__ (serve/fast_depth.py:241-257): h [rows, d_backbone] bf16, cb0 [rows] -> codes [rows, n_q]
+ * int64 and feedback [rows, d_backbone] bf16 (the next backbone input); advances row_ctr of each row's slot. */
+M3_API int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, const int64_t* cb0, int64_t* codes,
+                  void* feedback, int32_t rows, m3_stream stream);
+/* The level sampler alone (serve/fast_depth_kernels.py:305-336): logits [rows, n] (bf16 if logits_bf16 else
+ * fp32), per-row seed/counter -> codes [rows].  inv_temp = 1 / temperature. */
+M3_API int m3_topk_sample(const void* logits, int32_t logits_bf16, int32_t rows, int32_t n, const int32_t* seed,
+                   const int32_t* ctr, int32_t level, float inv_temp, int32_t top_k, int32_t greedy, int64_t* codes,
+                   m3_stream stream);
+M3_API int m3_depth_status(m3_depth* d, int32_t* status, int32_t clear);
+
+/* ---------------------------------------------------------------------------------------------- mimi */
+/* Replaces StaticMimi (serve/fast_codec.py:32-277): one 80 ms frame per seat with per-slot streaming state. */
+typedef struct m3_mimi m3_mimi;
+
+typedef struct {
+  int32_t hidden, n_q, n_semantic, codebook_size, codebook_dim;
+  int32_t layers, heads, ffn, window, ring;
+  int32_t n_ratios, ratios[8];
+  int32_t num_filters, kernel, last_kernel, res_kernel, compress, upsample_stride;
+  int32_t max_slots, max_rows;
+  float norm_eps;
+} m3_mimi_config;
+
+typedef struct {
+  const void* codebooks;     /* [n_q, codebook_size, codebook_dim] decoded embeddings (embed_sum / usage) */
+  const void* proj_sem;      /* [hidden, codebook_dim] semantic output_proj */
+  const void* proj_ac;       /* [hidden, codebook_dim] acoustic output_proj */
+  const void* upsample;      /* [hidden, 2 upsample_stride] depthwise ConvTranspose1d weight */
+  /* transformer, host arrays of `layers` pointers */
+  const void* const* ln1_w; const void* const* ln1_b;
+  const void* const* wqkv;   /* [3 hidden, hidden] q|k|v proj rows */
+  const void* const* wo;     /* [hidden, hidden] */
+  const void* const* ln2_w; const void* const* ln2_b;
+  const void* const* fc1;    /* [ffn, hidden] */
+  const void* const* fc2;    /* [hidden, ffn] */
+  const void* const* ls1;    /* [hidden] self_attn_layer_scale */
+  const void* const* ls2;    /* [hidden] mlp_layer_scale */
+  const float* inv_freq;     /* [head_dim / 2] fp32 RoPE frequencies, as the model holds them */
+  /* SEANet decoder, host arrays; conv weights repacked tap-major: [c_out, k * c_in] with element (o, j c_in + i) =
+   * W[o, i, j]; transposed-conv weights [2r c_out, c_in] with element (j c_out + o, i) = W[i, o, j] */
+  const void* conv0_w; const void* conv0_b;
+  const void* const* convt_w; const void* const* convt_b;     /* n_ratios */
+  const void* const* res1_w; const void* const* res1_b;       /* n_ratios: k res_kernel, c -> c / compress */
+  const void* const* res2_w; const void* const* res2_b;       /* n_ratios: k 1, c / compress -> c */
+  const void* final_w; const void* final_b;                   /* [1, last_kernel num_filters] */
+  /* per-slot state, caller-owned (rows = max_slots + 1) */
+  void* conv_state;          /* bf16 [rows, m3_mimi_state_elems()] histories and overlap tails, channels-last */
+  void* kv;                  /* bf16 [layers, 2, rows, heads, ring, head_dim] keys post-RoPE (fast_codec.py:68) */
+  int64_t* key_pos;          /* [rows, ring] absolute key positions, empty = -(1 << 40) */
+  int64_t* tokens;           /* [rows] transformer tokens consumed */
+} m3_mimi_weights;
+
+/* Elements of one slot's conv_state row for a geometry. */
+M3_API int64_t m3_mimi_state_elems(const m3_mimi_config* cfg);
+M3_API int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* w, m3_mimi** out);
+M3_API int m3_mimi_destroy(m3_mimi* m);
+/* StaticMimi.reset (serve/fast_codec.py:236-244). */
+M3_API int m3_mimi_reset(m3_mimi* m, int32_t slot, int32_t zero_kv, m3_stream stream);
+/* StaticMimi.decode (serve/fast_codec.py:246-277): codes [rows, n_q] -> pcm [rows, samples_per_frame] fp32. */
+M3_API int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* codes, float* pcm, int32_t rows,
+                   m3_stream stream);
+M3_API int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear);
+
+/* ---------------------------------------------------------------------------------------------- readout */
+/* The engine's per-tick readout (maya3/engine.py:557-561): packed [rows, 2 + spf / 4] int64 rows holding
+ * (stop code, cb0, PCM as int16 = round(clamp(pcm, -1, 1) * 32767)). */
+M3_API int m3_pack_readout(const int64_t* code, const int64_t* cb0, const float* pcm, int64_t* packed, int32_t rows,
+                    int32_t spf, m3_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MAYA3_B200_H */

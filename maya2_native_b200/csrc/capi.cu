@@ -1,0 +1,60 @@
+// Library-wide C ABI pieces: error reporting, version, and the engine's per-tick readout packing.
+#include <cstdarg>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace m3 {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+const char* last_error() { return g_err; }
+
+// One row per seat: [stop code, cb0, pcm16 packed four samples per int64] (maya3/engine.py:557-561):
+// pcm16 = round(clamp(pcm, -1, 1) * 32767) with round-half-to-even, as torch.round.
+__global__ void pack_readout_kernel(const int64_t* __restrict__ code, const int64_t* __restrict__ cb0,
+                                    const float* __restrict__ pcm, int64_t* __restrict__ packed, int spf) {
+  const int row = blockIdx.x;
+  const int words = spf / 4;
+  int64_t* out = packed + (int64_t)row * (2 + words);
+  if (threadIdx.x == 0) {
+    out[0] = code[row];
+    out[1] = cb0[row];
+  }
+  const float4* src = reinterpret_cast<const float4*>(pcm + (int64_t)row * spf);
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    const float4 v = src[w];
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    uint64_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = fminf(fmaxf(f[e], -1.f), 1.f) * 32767.f;
+      const int16_t q = (int16_t)__float2int_rn(c);
+      word |= (uint64_t)(uint16_t)q << (16 * e);
+    }
+    out[2 + w] = (int64_t)word;
+  }
+}
+
+}  // namespace m3
+
+extern "C" const char* m3_last_error(void) { return m3::last_error(); }
+
+extern "C" int m3_version(void) { return 1; }
+
+extern "C" int m3_pack_readout(const int64_t* code, const int64_t* cb0, const float* pcm, int64_t* packed,
+                               int32_t rows, int32_t spf, m3_stream stream) {
+  M3_REQUIRE(code && cb0 && pcm && packed, M3_ERR_ARG, "m3_pack_readout: null argument");
+  M3_REQUIRE(spf % 4 == 0 && rows >= 0, M3_ERR_ARG, "m3_pack_readout: spf %d not a multiple of 4", spf);
+  if (rows == 0) return M3_OK;
+  m3::pack_readout_kernel<<<rows, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(code, cb0, pcm, packed, spf);
+  M3_LAUNCHED();
+  return M3_OK;
+}

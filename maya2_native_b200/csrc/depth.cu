@@ -1,0 +1,495 @@
+// Depth transformer: the per-frame RVQ level loop (replaces serve/fast_depth.py FastDepth with its fused kernels
+// serve/fast_depth_kernels.py) plus the backbone feedback embed (tts/model/audio_io.py:27-35).
+//
+// For each level l (1..n_q-1) the level's weight group runs its 4 pre-norm layers over the prefix [proj(h)+lvl0,
+// emb(cb0), ..., emb(cb_{l-1})] (or, inside a shared group, incrementally over the one new position against the
+// group's stored K/V), the last layer only for the final position; then LayerNorm, the level head and the top-k
+// sampler, whose kernel also writes the next prefix row.  All rows of the seat batch go through each linear layer
+// together, so the weights are read once per level for every seat.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "ops.cuh"
+#include "sampler.cuh"
+
+namespace m3 {
+
+// ------------------------------------------------------------------------------------------------ row setup
+__global__ void depth_prep_kernel(const int64_t* __restrict__ slots, const int64_t* __restrict__ cb0, int rows,
+                                  int max_slots, int n_codes, int* __restrict__ slot32, int* __restrict__ cb032,
+                                  int64_t* __restrict__ codes, int n_q, int* status) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int64_t s = slots[r];
+  if (s < 0 || s > max_slots) {
+    report(status, M3_DEV_BAD_SLOT);
+    s = max_slots;
+  }
+  int64_t c = cb0[r];
+  if (c < 0 || c >= n_codes) {
+    report(status, M3_DEV_BAD_CODE);
+    c = c < 0 ? 0 : n_codes - 1;
+  }
+  slot32[r] = (int)s;
+  cb032[r] = (int)c;
+  codes[(int64_t)r * n_q] = cb0[r];
+}
+
+// prefix[:, 0] = bf16(in_proj(h) + level0); prefix[:, 1] = embed[0][cb0]   (serve/fast_depth.py:149-151)
+__global__ void prefix_init_kernel(const bf16* __restrict__ proj, const bf16* __restrict__ level0,
+                                   const bf16* __restrict__ embed0, const int* __restrict__ cb032,
+                                   bf16* __restrict__ prefix, int NL, int D) {
+  const int r = blockIdx.x;
+  bf16* p = prefix + (int64_t)r * NL * D;
+  const uint4* e = reinterpret_cast<const uint4*>(embed0 + (int64_t)cb032[r] * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) {
+    float a[8], b[8];
+    unpack8(reinterpret_cast<const uint4*>(proj + (int64_t)r * D)[i], a);
+    unpack8(reinterpret_cast<const uint4*>(level0)[i], b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = a[k] + b[k];
+    reinterpret_cast<uint4*>(p)[i] = pack8(a);
+    reinterpret_cast<uint4*>(p + D)[i] = e[i];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ LayerNorm
+// Row r of the input lives at src + (r / T) * sb + (r % T) * st (elements); optional residual add(s):
+// x' = bf16(x + a) then x' = bf16(x' + c[slot]) (serve/fast_depth_kernels.py:280-283), stored to xout (contiguous);
+// y = bf16((x' - mean) / sqrt(var + eps) * w + b) with fp32 statistics (:284-289).
+__global__ void add_ln_kernel(const bf16* __restrict__ src, int T, int64_t sb, int64_t st,
+                              const bf16* __restrict__ a, const bf16* __restrict__ c, int64_t c_slot_stride,
+                              const int* __restrict__ slot32, bf16* __restrict__ xout, bf16* __restrict__ y,
+                              const bf16* __restrict__ w, const bf16* __restrict__ bias, float eps, int D) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int nv = D / 8;
+  const bf16* xr = src + (int64_t)(r / T) * sb + (int64_t)(r % T) * st;
+  constexpr int kMaxPer = 4;
+  float v[kMaxPer][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+      unpack8(reinterpret_cast<const uint4*>(xr)[i], v[it]);
+      if (a) {
+        float av[8];
+        unpack8(reinterpret_cast<const uint4*>(a + (int64_t)r * D)[i], av);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[it][e] = rbf(v[it][e] + av[e]);
+      }
+      if (c) {
+        float cv[8];
+        unpack8(reinterpret_cast<const uint4*>(c + (int64_t)slot32[r / T] * c_slot_stride)[i], cv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[it][e] = rbf(v[it][e] + cv[e]);
+      }
+      if (xout) reinterpret_cast<uint4*>(xout + (int64_t)r * D)[i] = pack8(v[it]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[it][e];
+    }
+  }
+  const float mean = block_sum(sum, red) / (float)D;
+  float sq = 0.f;
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[it][e] - mean;
+        sq = fmaf(d, d, sq);
+      }
+  }
+  const float var = block_sum(sq, red) / (float)D;
+  const float den = sqrtf(var + eps);
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+      float wv[8], bv[8], o[8];
+      unpack8(reinterpret_cast<const uint4*>(w)[i], wv);
+      unpack8(reinterpret_cast<const uint4*>(bias)[i], bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = (v[it][e] - mean) / den * wv[e] + bv[e];
+      reinterpret_cast<uint4*>(y + (int64_t)r * D)[i] = pack8(o);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+// Tiny attention over at most kMaxKeys positions: query i of row b sits at absolute position q0 + i and sees keys
+// 0..q0+i (causal; the last-position and incremental forms are q0 = n-1 with one query).  One warp per query, lanes
+// split the head dim; fp32 scores and softmax, output rounded once (F.scaled_dot_product_attention).
+constexpr int kMaxKeys = 64;
+
+struct KeySrc {
+  const bf16* k;  // key of (b, j, head h) at k + b*sb + j*sj + h*hd
+  const bf16* v;
+  int64_t sb, sj;
+};
+
+__global__ void depth_attn_kernel(const bf16* __restrict__ qkv, int T, int q0, int Tq, KeySrc ks, int H, int HD,
+                                  float scale, bf16* __restrict__ out) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int D = H * HD;
+  for (int i = warp; i < Tq; i += nw) {
+    const int qp = q0 + i;  // absolute position of this query
+    // the queries are the last Tq of the T qkv rows of seat b
+    const bf16* q = qkv + ((int64_t)b * T + (T - Tq) + i) * 3 * D + (int64_t)h * HD;
+    float qv[4];
+    const int per = HD / 32;
+    for (int e = 0; e < per; ++e) qv[e] = to_f(q[lane * per + e]);
+    float s[kMaxKeys];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxKeys; ++j) {
+      if (j > qp) break;
+      const bf16* kr = ks.k + (int64_t)b * ks.sb + (int64_t)j * ks.sj + (int64_t)h * HD;
+      float d = 0.f;
+      for (int e = 0; e < per; ++e) d = fmaf(qv[e], to_f(kr[lane * per + e]), d);
+      d = warp_sum(d) * scale;
+      s[j] = d;
+      mx = fmaxf(mx, d);
+    }
+    float den = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxKeys; ++j) {
+      if (j > qp) break;
+      s[j] = expf(s[j] - mx);
+      den += s[j];
+    }
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kMaxKeys; ++j) {
+      if (j > qp) break;
+      const bf16* vr = ks.v + (int64_t)b * ks.sb + (int64_t)j * ks.sj + (int64_t)h * HD;
+      for (int e = 0; e < per; ++e) o[e] = fmaf(s[j], to_f(vr[lane * per + e]), o[e]);
+    }
+    bf16* dst = out + ((int64_t)b * Tq + i) * D + (int64_t)h * HD;
+    for (int e = 0; e < per; ++e) dst[lane * per + e] = to_bf(o[e] / den);
+  }
+}
+
+// kvbuf[b, p0 + t] = (k, v) of qkv rows t of b  (serve/fast_depth.py:170,176)
+__global__ void kv_store_kernel(const bf16* __restrict__ qkv, int T, bf16* __restrict__ kv, int NL, int p0, int D) {
+  const int b = blockIdx.x, t = blockIdx.y;
+  const uint4* src = reinterpret_cast<const uint4*>(qkv + ((int64_t)b * T + t) * 3 * D + D);
+  uint4* dst = reinterpret_cast<uint4*>(kv + ((int64_t)b * NL + p0 + t) * 2 * D);
+  for (int i = threadIdx.x; i < 2 * D / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// keep only the last position of each row block: out[b] = x[b*T + T-1]  (x = x[:, -1:], serve/fast_depth.py:181)
+__global__ void take_last_kernel(const bf16* __restrict__ x, int T, bf16* __restrict__ out, int D) {
+  const int b = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(x + ((int64_t)b * T + T - 1) * D);
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)b * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// act = bf16(gelu_erf(f))   (F.gelu on the depth dtype)
+__global__ void gelu_kernel(bf16* __restrict__ f, int64_t n8) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float v[8];
+  unpack8(reinterpret_cast<const uint4*>(f)[i], v);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = 0.5f * v[e] * (1.f + erff(v[e] * 0.70710678118654752f));
+  reinterpret_cast<uint4*>(f)[i] = pack8(v);
+}
+
+__global__ void ctr_advance_kernel(const int* __restrict__ slot32, int rows, int32_t* __restrict__ ctr) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) atomicAdd(reinterpret_cast<int*>(ctr + slot32[r]), 1);
+}
+
+// feedback = RMSNorm(bf16(bf16(sum_k table[code_k + k n_codes]) / sqrt(n_q))), fp32 epsilon (nn.RMSNorm eps=None)
+// (tts/model/audio_io.py:33-35 as inlined at serve/fast_depth.py:200-202).
+__global__ void feedback_kernel(const int64_t* __restrict__ codes, int NL, int n_codes,
+                                const bf16* __restrict__ table, const bf16* __restrict__ w, int D, float inv_scale_div,
+                                bf16* __restrict__ out, int* status) {
+  __shared__ float red[32];
+  __shared__ int cs[64];
+  const int r = blockIdx.x;
+  for (int k = threadIdx.x; k < NL; k += blockDim.x) {
+    int64_t c = codes[(int64_t)r * NL + k];
+    if (c < 0 || c >= n_codes) {
+      report(status, M3_DEV_BAD_CODE);
+      c = c < 0 ? 0 : n_codes - 1;
+    }
+    cs[k] = (int)c + k * n_codes;
+  }
+  __syncthreads();
+  constexpr int kMaxPer = 4;
+  float v[kMaxPer][8];
+  float ss = 0.f;
+  const int nv = D / 8;
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[it][e] = 0.f;
+      for (int k = 0; k < NL; ++k) {
+        float t[8];
+        unpack8(reinterpret_cast<const uint4*>(table + (int64_t)cs[k] * D)[i], t);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[it][e] += t[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[it][e] = rbf(rbf(v[it][e]) / inv_scale_div);
+        ss = fmaf(v[it][e], v[it][e], ss);
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.f / sqrtf(ss / (float)D + 1.1920928955078125e-07f);
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+      float wv[8], o[8];
+      unpack8(reinterpret_cast<const uint4*>(w)[i], wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[it][e] * inv * wv[e];
+      reinterpret_cast<uint4*>(out + (int64_t)r * D)[i] = pack8(o);
+    }
+  }
+}
+
+}  // namespace m3
+
+// ================================================================================================ handle
+using namespace m3;
+
+struct m3_depth {
+  m3_depth_config c{};
+  const bf16 *in_proj = nullptr, *embed = nullptr, *level0 = nullptr, *norm_w = nullptr, *norm_b = nullptr;
+  std::vector<const bf16*> n1_w, n1_b, n2_w, n2_b, qkv, o, f1, f2, heads, cross_kv, cross_o;
+  const bf16 *audio_table = nullptr, *audio_norm = nullptr;
+  bf16* cross_const = nullptr;
+  int32_t *row_seed = nullptr, *row_ctr = nullptr;
+  void* ws = nullptr;
+  int *slot32 = nullptr, *cb032 = nullptr, *status = nullptr;
+  bf16 *prefix = nullptr, *x = nullptr, *x2 = nullptr, *y = nullptr, *qkvb = nullptr, *a = nullptr, *ob = nullptr,
+       *ff = nullptr, *logits = nullptr, *proj = nullptr, *kvbuf = nullptr, *spk = nullptr;
+};
+
+namespace {
+template <class T>
+T* carve(char*& p, size_t count) {
+  T* r = reinterpret_cast<T*>(p);
+  p += (count * sizeof(T) + 255) / 256 * 256;
+  return r;
+}
+int norm_threads(int D) { return std::min(1024, std::max(32, (D / 8 + 31) / 32 * 32)); }
+}  // namespace
+
+extern "C" int m3_depth_create(const m3_depth_config* cfg, const m3_depth_weights* w, m3_depth** out) {
+  M3_REQUIRE(cfg && w && out, M3_ERR_ARG, "m3_depth_create: null argument");
+  const m3_depth_config& c = *cfg;
+  M3_REQUIRE(c.n_q >= 2 && c.n_q <= 64 && c.n_q <= kMaxKeys, M3_ERR_UNSUPPORTED, "n_q %d", c.n_q);
+  M3_REQUIRE(c.d % c.heads == 0 && (c.d / c.heads) % 32 == 0 && c.d / c.heads <= 128, M3_ERR_UNSUPPORTED,
+             "depth head dim must be 32, 64, 96 or 128");
+  M3_REQUIRE(c.d % 8 == 0 && c.ffn % 8 == 0 && c.d_backbone % 8 == 0 && c.d <= 8192, M3_ERR_UNSUPPORTED, "sizes");
+  auto* d = new m3_depth();
+  d->c = c;
+  d->in_proj = (const bf16*)w->in_proj;
+  d->embed = (const bf16*)w->embed;
+  d->level0 = (const bf16*)w->level0;
+  d->norm_w = (const bf16*)w->norm_w;
+  d->norm_b = (const bf16*)w->norm_b;
+  const int GL = c.n_groups * c.layers;
+  for (int i = 0; i < GL; ++i) {
+    d->n1_w.push_back((const bf16*)w->n1_w[i]);
+    d->n1_b.push_back((const bf16*)w->n1_b[i]);
+    d->n2_w.push_back((const bf16*)w->n2_w[i]);
+    d->n2_b.push_back((const bf16*)w->n2_b[i]);
+    d->qkv.push_back((const bf16*)w->qkv[i]);
+    d->o.push_back((const bf16*)w->o[i]);
+    d->f1.push_back((const bf16*)w->f1[i]);
+    d->f2.push_back((const bf16*)w->f2[i]);
+  }
+  for (int i = 0; i < c.n_q - 1; ++i) d->heads.push_back((const bf16*)w->heads[i]);
+  for (int i = 0; i < c.layers; ++i) {
+    d->cross_kv.push_back((const bf16*)w->cross_kv[i]);
+    d->cross_o.push_back((const bf16*)w->cross_o[i]);
+  }
+  d->audio_table = (const bf16*)w->audio_table;
+  d->audio_norm = (const bf16*)w->audio_norm;
+  d->cross_const = (bf16*)w->cross_const;
+  d->row_seed = w->row_seed;
+  d->row_ctr = w->row_ctr;
+  const size_t R = c.max_rows, NL = c.n_q, D = c.d;
+  size_t bytes = 0;
+  auto add = [&](size_t n) { bytes += (n + 255) / 256 * 256; };
+  add(R * 4); add(R * 4); add(256);
+  add(R * NL * D * 2);          // prefix
+  add(R * NL * D * 2);          // x
+  add(R * NL * D * 2);          // x2
+  add(R * NL * D * 2);          // y
+  add(R * NL * 3 * D * 2);      // qkv
+  add(R * NL * D * 2);          // a
+  add(R * NL * D * 2);          // o
+  add(R * NL * c.ffn * 2);      // ff
+  add(R * c.n_codes * 2);       // logits
+  add(R * D * 2);               // proj
+  add((size_t)c.layers * R * NL * 2 * D * 2);  // kvbuf
+  add(4 * D * 2);               // speaker scratch
+  cudaError_t e = cudaMalloc(&d->ws, bytes);
+  if (e != cudaSuccess) {
+    delete d;
+    set_error("m3_depth_create: cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    return M3_ERR_CUDA;
+  }
+  char* p = (char*)d->ws;
+  d->slot32 = carve<int>(p, R);
+  d->cb032 = carve<int>(p, R);
+  d->status = carve<int>(p, 64);
+  d->prefix = carve<bf16>(p, R * NL * D);
+  d->x = carve<bf16>(p, R * NL * D);
+  d->x2 = carve<bf16>(p, R * NL * D);
+  d->y = carve<bf16>(p, R * NL * D);
+  d->qkvb = carve<bf16>(p, R * NL * 3 * D);
+  d->a = carve<bf16>(p, R * NL * D);
+  d->ob = carve<bf16>(p, R * NL * D);
+  d->ff = carve<bf16>(p, R * NL * c.ffn);
+  d->logits = carve<bf16>(p, R * c.n_codes);
+  d->proj = carve<bf16>(p, R * D);
+  d->kvbuf = carve<bf16>(p, (size_t)c.layers * R * NL * 2 * D);
+  d->spk = carve<bf16>(p, 4 * D);
+  cudaMemset(d->status, 0, 256);
+  *out = d;
+  return M3_OK;
+}
+
+extern "C" int m3_depth_destroy(m3_depth* d) {
+  if (!d) return M3_OK;
+  cudaFree(d->ws);
+  delete d;
+  return M3_OK;
+}
+
+extern "C" int m3_depth_status(m3_depth* d, int32_t* status, int32_t clear) {
+  M3_REQUIRE(d && status, M3_ERR_ARG, "m3_depth_status: null argument");
+  M3_CUDA(cudaMemcpy(status, d->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (clear) M3_CUDA(cudaMemset(d->status, 0, sizeof(int32_t)));
+  return M3_OK;
+}
+
+extern "C" int m3_depth_set_speaker(m3_depth* d, int32_t slot, const void* mem, float keep, m3_stream stream) {
+  M3_REQUIRE(d && mem, M3_ERR_ARG, "m3_depth_set_speaker: null argument");
+  M3_REQUIRE(slot >= 0 && slot <= d->c.max_slots, M3_ERR_RANGE, "slot %d outside [0, %d]", slot, d->c.max_slots);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int D = d->c.d;
+  for (int li = 0; li < d->c.layers; ++li) {
+    bf16* dst = d->cross_const + ((int64_t)slot * d->c.layers + li) * D;
+    if (keep == 0.f) {  // o(v * 0) = 0: the layers are bias-free
+      M3_CUDA(cudaMemsetAsync(dst, 0, (size_t)D * 2, s));
+      continue;
+    }
+    // kv = kv(mem) (bf16), v = second half; cross = o(v)   (serve/fast_depth.py:80-82)
+    M3_TRY(gemm({(const bf16*)mem, D, d->cross_kv[li], D, d->spk, 2 * D, 1, 2 * D, D, false}, s));
+    M3_TRY(gemm({d->spk + D, D, d->cross_o[li], D, dst, D, 1, D, D, false}, s));
+  }
+  return M3_OK;
+}
+
+extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, const int64_t* cb0, int64_t* codes,
+                             void* feedback, int32_t rows, m3_stream stream) {
+  M3_REQUIRE(d && slots && h && cb0 && codes && feedback, M3_ERR_ARG, "m3_depth_step: null argument");
+  const m3_depth_config& c = d->c;
+  M3_REQUIRE(rows >= 0 && rows <= c.max_rows, M3_ERR_RANGE, "rows %d > max_rows %d", rows, c.max_rows);
+  if (rows == 0) return M3_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int R = rows, NL = c.n_q, D = c.d, H = c.heads, HD = D / H, L = c.layers;
+  const int nt = norm_threads(D);
+  const float scale = 1.f / sqrtf((float)HD);
+  depth_prep_kernel<<<cdiv(R, 128), 128, 0, s>>>(slots, cb0, R, c.max_slots, c.n_codes, d->slot32, d->cb032, codes,
+                                                 NL, d->status);
+  M3_LAUNCHED();
+  M3_TRY(gemm({(const bf16*)h, c.d_backbone, d->in_proj, c.d_backbone, d->proj, D, R, D, c.d_backbone, false}, s));
+  prefix_init_kernel<<<R, 128, 0, s>>>(d->proj, d->level0, d->embed, d->cb032, d->prefix, NL, D);
+  M3_LAUNCHED();
+  const int64_t kv_layer = (int64_t)R * NL * 2 * D;
+  int previous = -1;
+  for (int level = 1; level < NL; ++level) {
+    const int group = c.group_of_level[level];
+    const int n = level + 1;
+    const bool incremental = group == previous;
+    const bool reused_later = level + 1 < NL && c.group_of_level[level + 1] == group;
+    const int T = incremental ? 1 : n;
+    const int start = incremental ? level : 0;
+    const int gl = group * L;
+    // y = n1(x); x (the residual stream) becomes a contiguous copy of the prefix slice
+    add_ln_kernel<<<R * T, nt, 0, s>>>(d->prefix + (int64_t)start * D, T, (int64_t)NL * D, D, nullptr, nullptr, 0,
+                                       nullptr, d->x, d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D);
+    M3_LAUNCHED();
+    int Tr = T;  // rows per seat in the residual stream
+    for (int li = 0; li < L; ++li) {
+      M3_TRY(gemm({d->y, D, d->qkv[gl + li], D, d->qkvb, 3 * D, R * Tr, 3 * D, D, false}, s));
+      bf16* kvl = d->kvbuf + li * kv_layer;
+      int Tq = Tr, q0 = start;
+      KeySrc ks;
+      if (incremental) {
+        kv_store_kernel<<<dim3(R, 1), 128, 0, s>>>(d->qkvb, 1, kvl, NL, level, D);
+        ks = {kvl, kvl + D, (int64_t)NL * 2 * D, 2 * D};
+        q0 = level;
+      } else {
+        if (reused_later) kv_store_kernel<<<dim3(R, n), 128, 0, s>>>(d->qkvb, n, kvl, NL, 0, D);
+        ks = {d->qkvb + D, d->qkvb + 2 * D, (int64_t)n * 3 * D, 3 * D};
+        if (li == L - 1) {
+          Tq = 1;
+          q0 = n - 1;
+        }
+      }
+      M3_LAUNCHED();
+      depth_attn_kernel<<<dim3(R, H), 128, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, HD, scale, d->a);
+      M3_LAUNCHED();
+      if (Tq != Tr) {  // the last layer keeps only each seat's final position
+        take_last_kernel<<<R, 128, 0, s>>>(d->x, Tr, d->x2, D);
+        M3_LAUNCHED();
+        std::swap(d->x, d->x2);
+        Tr = Tq;
+      }
+      M3_TRY(gemm({d->a, D, d->o[gl + li], D, d->ob, D, R * Tr, D, D, false}, s));
+      // x, y2 = add_ln(x, o(a), n2)
+      add_ln_kernel<<<R * Tr, nt, 0, s>>>(d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
+                                          d->n2_b[gl + li], c.ln_eps, D);
+      M3_LAUNCHED();
+      M3_TRY(gemm({d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
+      const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
+      gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);
+      M3_LAUNCHED();
+      M3_TRY(gemm({d->ff, c.ffn, d->f2[gl + li], c.ffn, d->ob, D, R * Tr, D, c.ffn, false}, s));
+      // x, y = add_ln(x, f, next n1 (or the final norm), cross[slot][li])
+      const bf16* nw = li + 1 < L ? d->n1_w[gl + li + 1] : d->norm_w;
+      const bf16* nb = li + 1 < L ? d->n1_b[gl + li + 1] : d->norm_b;
+      add_ln_kernel<<<R * Tr, nt, 0, s>>>(d->x, Tr, (int64_t)Tr * D, D, d->ob, d->cross_const + (int64_t)li * D,
+                                          (int64_t)L * D, d->slot32, d->x, d->y, nw, nb, c.ln_eps, D);
+      M3_LAUNCHED();
+    }
+    // level head on the final position, then sample and write the next prefix row
+    M3_TRY(gemm({d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, d->logits, c.n_codes, R,
+                 c.n_codes, D, false},
+                s));
+    const bool more = n < NL;
+    M3_TRY(launch_topk_sample(d->logits, true, c.n_codes, R, c.n_codes, d->row_seed, d->row_ctr, d->slot32, level,
+                              c.inv_temp, c.top_k, c.greedy, codes + level, NL,
+                              more ? d->embed + (int64_t)level * c.n_codes * D : nullptr, D,
+                              more ? d->prefix + (int64_t)n * D : nullptr, (int64_t)NL * D, s));
+    previous = group;
+  }
+  ctr_advance_kernel<<<cdiv(R, 128), 128, 0, s>>>(d->slot32, R, d->row_ctr);
+  M3_LAUNCHED();
+  feedback_kernel<<<R, norm_threads(c.d_backbone), 0, s>>>(codes, NL, c.n_codes, d->audio_table, d->audio_norm,
+                                                           c.d_backbone, sqrtf((float)NL), (bf16*)feedback,
+                                                           d->status);
+  M3_LAUNCHED();
+  return M3_OK;
+}

@@ -1,0 +1,173 @@
+// Linear layers: Y[M,N] = X[M,K] . W[N,K]^T with bf16 operands and fp32 accumulation.
+//
+// Small M (a handful of seats) is weight-bandwidth bound: a GEMV kernel streams each weight row once with 16-byte
+// loads and keeps the few activation rows in shared memory.  Larger M goes to cuBLAS (a plain library GEMM).
+#include <cublas_v2.h>
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace m3 {
+
+// ------------------------------------------------------------------------------------------------ GEMV
+// One warp produces kCols consecutive output columns for all MT rows.  Lanes split K in 8-element (16 B) chunks.
+constexpr int kGemvWarps = 8;
+constexpr int kCols = 4;
+
+template <int MT, bool OUT_F32>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __restrict__ X, int64_t ldx,
+                                                               const bf16* __restrict__ W, int64_t ldw,
+                                                               void* __restrict__ Y, int64_t ldy, int M, int N,
+                                                               int K) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MT, K]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kv = K / 8;
+  for (int i = tid; i < MT * kv; i += blockDim.x) {
+    const int r = i / kv, c = i % kv;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < M) v = *reinterpret_cast<const uint4*>(X + r * ldx + c * 8);
+    reinterpret_cast<uint4*>(xs)[i] = v;
+  }
+  __syncthreads();
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * kCols;
+  if (n0 >= N) return;
+  float acc[MT][kCols];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) acc[m][c] = 0.f;
+  for (int k = lane; k < kv; k += 32) {
+    uint4 wv[kCols];
+#pragma unroll
+    for (int c = 0; c < kCols; ++c)
+      wv[c] = (n0 + c < N) ? __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + c) * ldw) + k)
+                           : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      float xf[8];
+      unpack8(reinterpret_cast<const uint4*>(xs)[m * kv + k], xf);
+#pragma unroll
+      for (int c = 0; c < kCols; ++c) {
+        float wf[8];
+        unpack8(wv[c], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m][c] = fmaf(xf[e], wf[e], acc[m][c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) acc[m][c] = warp_sum(acc[m][c]);
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m >= M) break;
+#pragma unroll
+      for (int c = 0; c < kCols; ++c) {
+        if (n0 + c >= N) break;
+        if (OUT_F32)
+          reinterpret_cast<float*>(Y)[m * ldy + n0 + c] = acc[m][c];
+        else
+          reinterpret_cast<bf16*>(Y)[m * ldy + n0 + c] = to_bf(acc[m][c]);
+      }
+    }
+  }
+}
+
+template <int MT>
+static int launch_gemv(const GemmDesc& g, cudaStream_t s) {
+  const int cols_per_block = kGemvWarps * kCols;
+  dim3 grid(cdiv(g.N, cols_per_block));
+  size_t smem = (size_t)MT * g.K * sizeof(bf16);
+  if (g.y_f32) {
+    if (smem > 48 * 1024)
+      M3_CUDA(cudaFuncSetAttribute(gemv_kernel<MT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    gemv_kernel<MT, true><<<grid, kGemvWarps * 32, smem, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+  } else {
+    if (smem > 48 * 1024)
+      M3_CUDA(cudaFuncSetAttribute(gemv_kernel<MT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    gemv_kernel<MT, false><<<grid, kGemvWarps * 32, smem, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+  }
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ cuBLAS
+namespace {
+struct Blas {
+  cublasHandle_t h = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+std::mutex g_blas_mu;
+std::vector<Blas> g_blas;  // one per device
+
+int blas_for_current_device(Blas** out) {
+  int dev = 0;
+  M3_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_blas_mu);
+  if ((int)g_blas.size() <= dev) g_blas.resize(dev + 1);
+  Blas& b = g_blas[dev];
+  if (!b.h) {
+    if (cublasCreate(&b.h) != CUBLAS_STATUS_SUCCESS) {
+      set_error("cublasCreate failed");
+      return M3_ERR_CUDA;
+    }
+    // A fixed workspace lets cuBLAS calls be captured into CUDA graphs (no allocation at launch).
+    b.ws_bytes = 32u << 20;
+    M3_CUDA(cudaMalloc(&b.ws, b.ws_bytes));
+    cublasSetMathMode(b.h, CUBLAS_DEFAULT_MATH);
+  }
+  *out = &b;
+  return M3_OK;
+}
+}  // namespace
+
+static int launch_cublas(const GemmDesc& g, cudaStream_t s) {
+  Blas* b = nullptr;
+  M3_TRY(blas_for_current_device(&b));
+  if (cublasSetStream(b->h, s) != CUBLAS_STATUS_SUCCESS ||
+      cublasSetWorkspace(b->h, b->ws, b->ws_bytes) != CUBLAS_STATUS_SUCCESS) {
+    set_error("cublasSetStream/Workspace failed");
+    return M3_ERR_CUDA;
+  }
+  const float alpha = 1.f, beta = 0.f;
+  // Row-major Y[M,N] = X W^T  <=>  column-major Y^T[N,M] = W^T(op T of col-major [K,N]) . X^T (col-major [K,M]).
+  cublasStatus_t st = cublasGemmEx(b->h, CUBLAS_OP_T, CUBLAS_OP_N, g.N, g.M, g.K, &alpha, g.W, CUDA_R_16BF,
+                                   (int)g.ldw, g.X, CUDA_R_16BF, (int)g.ldx, &beta, g.Y,
+                                   g.y_f32 ? CUDA_R_32F : CUDA_R_16BF, (int)g.ldy, CUBLAS_COMPUTE_32F,
+                                   CUBLAS_GEMM_DEFAULT);
+  if (st != CUBLAS_STATUS_SUCCESS) {
+    set_error("cublasGemmEx failed (status %d) M=%d N=%d K=%d", (int)st, g.M, g.N, g.K);
+    return M3_ERR_CUDA;
+  }
+  return M3_OK;
+}
+
+int gemm(const GemmDesc& g, cudaStream_t s) {
+  M3_REQUIRE(g.M >= 0 && g.N > 0 && g.K > 0, M3_ERR_ARG, "gemm: bad shape M=%d N=%d K=%d", g.M, g.N, g.K);
+  if (g.M == 0) return M3_OK;
+  const bool vec_ok = g.K % 8 == 0 && g.ldx % 8 == 0 && g.ldw % 8 == 0 &&
+                      (reinterpret_cast<uintptr_t>(g.X) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.W) & 15) == 0;
+  if (vec_ok && g.M <= 8 && (size_t)8 * g.K * 2 <= 200 * 1024) {
+    if (g.M <= 1) return launch_gemv<1>(g, s);
+    if (g.M <= 2) return launch_gemv<2>(g, s);
+    if (g.M <= 4) return launch_gemv<4>(g, s);
+    return launch_gemv<8>(g, s);
+  }
+  return launch_cublas(g, s);
+}
+
+}  // namespace m3
+
+extern "C" int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                            int32_t m, int32_t n, int32_t k, int32_t y_f32, m3_stream stream) {
+  m3::GemmDesc g{reinterpret_cast<const m3::bf16*>(x), ldx, reinterpret_cast<const m3::bf16*>(w), ldw, y, ldy,
+                 m, n, k, y_f32 != 0};
+  return m3::gemm(g, reinterpret_cast<cudaStream_t>(stream));
+}

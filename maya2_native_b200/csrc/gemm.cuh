@@ -1,0 +1,20 @@
+#pragma once
+#include "common.cuh"
+
+namespace m3 {
+
+// Y[M,N] = X[M,K] . W[N,K]^T (row-major, leading dimensions in elements), fp32 accumulation.
+struct GemmDesc {
+  const bf16* X;
+  int64_t ldx;
+  const bf16* W;
+  int64_t ldw;
+  void* Y;
+  int64_t ldy;
+  int M, N, K;
+  bool y_f32;  // Y stored as fp32 instead of bf16
+};
+
+int gemm(const GemmDesc& g, cudaStream_t s);
+
+}  // namespace m3

@@ -1,0 +1,661 @@
+// One-frame streaming Mimi decoder with per-slot state (replaces serve/fast_codec.py StaticMimi).
+//
+// Layout: activations are channels-last [row, time, channel] so every convolution is a GEMM over (row, time) rows:
+// a causal conv of k taps reads its k shifted input rows (the first k-1 come from the slot's history), a
+// transposed conv of stride r is X . W^T producing 2r output columns per input step, folded back with the previous
+// step's overlap (and the slot's stored tail for the first r outputs).  Rounding follows the reference (HF
+// MimiModel modules in the model dtype): each conv output is bias-added and rounded once, the stored convT tail is
+// bf16(y - bias), the resnet sum and the transformer residuals round after each add.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "ops.cuh"
+
+namespace m3 {
+
+constexpr int64_t kNever = -(1ll << 40);  // key_pos of an empty ring entry (serve/fast_codec.py:25)
+
+struct StageDims {  // one upsampling stage of the SEANet decoder
+  int cin, cout, r, L;  // L = input steps per frame
+  int64_t tail_off, hist_off;  // offsets (elements) in the slot's state row: convT tail [r, cout], k3 history
+};
+
+// ------------------------------------------------------------------------------------------------ RVQ + upsample
+// A_sem[b] = sum of semantic codebook rows, A_ac[b] = sum of acoustic rows (bf16 after each add,
+// serve/fast_codec.py:134-140).
+__global__ void rvq_gather_kernel(const int64_t* __restrict__ codes, int n_q, int n_sem, int cb_size, int cbd,
+                                  const bf16* __restrict__ books, bf16* __restrict__ a_sem, bf16* __restrict__ a_ac,
+                                  int* status) {
+  const int b = blockIdx.x;
+  for (int d = threadIdx.x; d < cbd; d += blockDim.x) {
+    float sem = 0.f, ac = 0.f;
+    for (int k = 0; k < n_q; ++k) {
+      int64_t c = codes[(int64_t)b * n_q + k];
+      if (c < 0 || c >= cb_size) {
+        report(status, M3_DEV_BAD_CODE);
+        c = c < 0 ? 0 : cb_size - 1;
+      }
+      const float e = to_f(books[((int64_t)k * cb_size + c) * cbd + d]);
+      if (k < n_sem)
+        sem = k == 0 ? e : rbf(sem + e);
+      else
+        ac = k == n_sem ? e : rbf(ac + e);
+    }
+    a_sem[(int64_t)b * cbd + d] = to_bf(sem);
+    a_ac[(int64_t)b * cbd + d] = to_bf(ac);
+  }
+}
+
+// x = bf16(P_sem + P_ac) (one 12.5 Hz token), then the depthwise ConvTranspose1d(k = 2s, stride s, no bias) with
+// its overlap tail: out[t] = bf16(y[t] + tail[t]) for t < s, new tail = y[s..2s)   (serve/fast_codec.py:112-126).
+__global__ void upsample_kernel(const bf16* __restrict__ p_sem, const bf16* __restrict__ p_ac,
+                                const bf16* __restrict__ w, int s, const int* __restrict__ slot32,
+                                bf16* __restrict__ state, int64_t state_row, bf16* __restrict__ out, int H) {
+  const int b = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  bf16* tail = state + (int64_t)slot32[b] * state_row;  // [s, H]
+  const float x = rbf(to_f(p_sem[(int64_t)b * H + c]) + to_f(p_ac[(int64_t)b * H + c]));
+  float y[16];
+  for (int j = 0; j < 2 * s; ++j) y[j] = rbf(x * to_f(w[(int64_t)c * 2 * s + j]));
+  for (int t = 0; t < s; ++t) {
+    const float prev = to_f(tail[(int64_t)t * H + c]);
+    out[((int64_t)b * s + t) * H + c] = to_bf(y[t] + prev);
+    tail[(int64_t)t * H + c] = to_bf(y[s + t]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ transformer
+// Absolute positions of this frame's tokens and their ring entries (serve/fast_codec.py:153-157).
+__global__ void tpos_kernel(const int* __restrict__ slot32, int rows, int T, int ring, const int64_t* __restrict__ tokens,
+                            int64_t* __restrict__ key_pos, int64_t* __restrict__ pos_out) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= rows) return;
+  const int s = slot32[b];
+  const int64_t start = tokens[s];
+  for (int t = 0; t < T; ++t) {
+    const int64_t p = start + t;
+    key_pos[(int64_t)s * ring + (p % ring)] = p;
+    pos_out[(int64_t)b * T + t] = p;
+  }
+}
+
+// q, k <- apply_rotary_pos_emb in the model dtype (each product and the sum rounded); k and v written to the slot's
+// ring at pos % ring (keys post-RoPE, serve/fast_codec.py:171-175).  One warp per (row, token, head).
+__global__ void mimi_rope_kernel(const bf16* __restrict__ qkv, const int64_t* __restrict__ pos,
+                                 const float* __restrict__ inv_freq, const int* __restrict__ slot32, int T, int heads,
+                                 int hd, int ring, bf16* __restrict__ q_out, bf16* __restrict__ kring,
+                                 bf16* __restrict__ vring, int64_t slot_stride) {
+  const int bt = blockIdx.x;  // row * T + t
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (h >= heads) return;
+  const int b = bt / T;
+  const int H = heads * hd, half = hd / 2;
+  const int64_t p = pos[bt];
+  const bf16* row = qkv + (int64_t)bt * 3 * H;
+  const int64_t roff = (int64_t)slot32[b] * slot_stride + ((int64_t)h * ring + (p % ring)) * hd;
+  for (int i = lane; i < half; i += 32) {
+    const float f = (float)p * inv_freq[i];
+    const float cs = rbf(cosf(f)), sn = rbf(sinf(f));  // emb = [f, f]: both halves share cos/sin
+    const int d1 = h * hd + i, d2 = d1 + half;
+    const float q1 = to_f(row[d1]), q2 = to_f(row[d2]);
+    const float k1 = to_f(row[H + d1]), k2 = to_f(row[H + d2]);
+    // rotate_half(x) = [-x2, x1]
+    q_out[(int64_t)bt * H + d1] = to_bf(rbf(q1 * cs) + rbf(-q2 * sn));
+    q_out[(int64_t)bt * H + d2] = to_bf(rbf(q2 * cs) + rbf(q1 * sn));
+    kring[roff + i] = to_bf(rbf(k1 * cs) + rbf(-k2 * sn));
+    kring[roff + i + half] = to_bf(rbf(k2 * cs) + rbf(k1 * sn));
+    vring[roff + i] = row[2 * H + d1];
+    vring[roff + i + half] = row[2 * H + d2];
+  }
+}
+
+// Sliding-window attention of the frame's T queries over the slot's ring: key r is visible to the query at
+// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head); one
+// thread per ring entry for the scores, one thread per (query, dim) for the weighted sum.
+constexpr int kRingMax = 512;
+
+__global__ void ring_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kring,
+                                 const bf16* __restrict__ vring, const int64_t* __restrict__ key_pos,
+                                 const int64_t* __restrict__ pos, const int* __restrict__ slot32, int T, int heads,
+                                 int hd, int ring, int window, int64_t slot_stride, float scale,
+                                 bf16* __restrict__ out) {
+  __shared__ float sc[4][kRingMax];
+  __shared__ float qs[4][128];
+  __shared__ float red[32];
+  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int H = heads * hd;
+  const int s = slot32[b];
+  const bf16* K = kring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
+  const bf16* V = vring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
+  for (int i = tid; i < T * hd; i += blockDim.x) qs[i / hd][i % hd] = to_f(q[((int64_t)b * T + i / hd) * H + h * hd + i % hd]);
+  __syncthreads();
+  for (int r = tid; r < ring; r += blockDim.x) {
+    const int64_t kp = key_pos[(int64_t)s * ring + r];
+    const uint4* kr = reinterpret_cast<const uint4*>(K + (int64_t)r * hd);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < hd / 8; ++c) {
+      float kf[8];
+      unpack8(kr[c], kf);
+      for (int t = 0; t < T; ++t)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[t] = fmaf(qs[t][c * 8 + e], kf[e], acc[t]);
+    }
+    for (int t = 0; t < T; ++t) {
+      const int64_t p = pos[(int64_t)b * T + t];
+      const bool vis = kp <= p && kp > p - window;
+      sc[t][r] = vis ? acc[t] * scale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  for (int t = 0; t < T; ++t) {
+    float mx = -INFINITY;
+    for (int r = tid; r < ring; r += blockDim.x) mx = fmaxf(mx, sc[t][r]);
+    mx = block_max(mx, red);
+    float sum = 0.f;
+    __syncthreads();
+    for (int r = tid; r < ring; r += blockDim.x) {
+      const float e = sc[t][r] == -INFINITY ? 0.f : expf(sc[t][r] - mx);
+      sc[t][r] = e;
+      sum += e;
+    }
+    sum = block_sum(sum, red);
+    __syncthreads();
+    for (int r = tid; r < ring; r += blockDim.x) sc[t][r] /= sum;
+  }
+  __syncthreads();
+  for (int i = tid; i < T * hd; i += blockDim.x) {
+    const int t = i / hd, d = i % hd;
+    float o = 0.f;
+    for (int r = 0; r < ring; ++r) o = fmaf(sc[t][r], to_f(V[(int64_t)r * hd + d]), o);
+    out[((int64_t)b * T + t) * H + h * hd + d] = to_bf(o);
+  }
+}
+
+// h' = bf16(h + bf16(scale * a)) (MimiLayerScale + residual), stored; y = LayerNorm(h') if w != nullptr.
+__global__ void scale_add_ln_kernel(bf16* __restrict__ h, const bf16* __restrict__ a, const bf16* __restrict__ ls,
+                                    bf16* __restrict__ y, const bf16* __restrict__ w, const bf16* __restrict__ bias,
+                                    float eps, int D) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  constexpr int kMaxPer = 4;
+  float v[kMaxPer][8];
+  float sum = 0.f;
+  const int nv = D / 8;
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+      float hv[8], av[8], sv[8];
+      unpack8(reinterpret_cast<const uint4*>(h + (int64_t)r * D)[i], hv);
+      unpack8(reinterpret_cast<const uint4*>(a + (int64_t)r * D)[i], av);
+      unpack8(reinterpret_cast<const uint4*>(ls)[i], sv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[it][e] = rbf(hv[e] + rbf(sv[e] * av[e]));
+        sum += v[it][e];
+      }
+      reinterpret_cast<uint4*>(h + (int64_t)r * D)[i] = pack8(v[it]);
+    }
+  }
+  if (!w) return;
+  const float mean = block_sum(sum, red) / (float)D;
+  float sq = 0.f;
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sq = fmaf(v[it][e] - mean, v[it][e] - mean, sq);
+  }
+  const float den = sqrtf(block_sum(sq, red) / (float)D + eps);
+#pragma unroll
+  for (int it = 0; it < kMaxPer; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i < nv) {
+      float wv[8], bv[8], o[8];
+      unpack8(reinterpret_cast<const uint4*>(w)[i], wv);
+      unpack8(reinterpret_cast<const uint4*>(bias)[i], bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = (v[it][e] - mean) / den * wv[e] + bv[e];
+      reinterpret_cast<uint4*>(y + (int64_t)r * D)[i] = pack8(o);
+    }
+  }
+}
+
+__global__ void tokens_advance_kernel(const int* __restrict__ slot32, int rows, int T, int dummy,
+                                      int64_t* __restrict__ tokens) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < rows && slot32[b] != dummy) tokens[slot32[b]] += T;
+  if (b == 0) tokens[dummy] = 0;  // serve/fast_codec.py:182-183
+}
+
+// ------------------------------------------------------------------------------------------------ SEANet
+__device__ __forceinline__ float elu(float x) { return x > 0.f ? x : expm1f(x); }
+
+// im2col of a causal stride-1 conv with k taps over [history (k-1 rows, stored), new rows]:
+// A[b*L + t, j*C + c] = joined[t + j][c], joined = [hist; act(x)] with act = ELU (rounded) when elu_in.
+// The slot's history becomes the last k-1 rows of joined.  One CTA per (row, channel chunk): every read of the
+// history happens before the CTA's own write of it.
+__global__ void im2col_hist_kernel(const bf16* __restrict__ x, int L, int C, int k, int elu_in,
+                                   const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
+                                   int64_t hist_off, bf16* __restrict__ A) {
+  const int b = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  const bool on = c < C;
+  bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;  // [k-1, C]
+  const int P = k - 1;
+  float hv[8];
+  for (int j = 0; j < P && on; ++j) hv[j] = to_f(hist[(int64_t)j * C + c]);
+  __syncthreads();
+  if (!on) return;
+  auto joined = [&](int i) -> float {
+    if (i < P) return hv[i];
+    const float v = to_f(x[((int64_t)b * L + (i - P)) * C + c]);
+    return elu_in ? rbf(elu(v)) : v;
+  };
+  for (int t = 0; t < L; ++t)
+    for (int j = 0; j < k; ++j) A[((int64_t)b * L + t) * k * C + (int64_t)j * C + c] = to_bf(joined(t + j));
+  for (int j = 0; j < P; ++j) hist[(int64_t)j * C + c] = to_bf(joined(L + j));
+}
+
+// y = bf16(z + bias); mode 1: y = bf16(elu(y)); mode 2: y = bf16(res + y)
+__global__ void bias_epilogue_kernel(const float* __restrict__ z, const bf16* __restrict__ bias, int64_t M, int N,
+                                     int mode, const bf16* __restrict__ res, bf16* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * N) return;
+  float v = rbf(z[i] + to_f(bias[i % N]));
+  if (mode == 1) v = rbf(elu(v));
+  if (mode == 2) v = rbf(to_f(res[i]) + v);
+  y[i] = to_bf(v);
+}
+
+// In place y = bf16(elu(y)).
+__global__ void elu_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = to_bf(elu(to_f(x[i])));
+}
+
+// Transposed conv fold: Z[b*L + t, j*Co + o] (fp32, j < 2r) are the per-step contributions.  Output step
+// s = t*r + jj gets Z[t, jj] + Z[t-1, jj + r]; conv output = bf16(sum + bias); the first r outputs add the slot's
+// stored tail; the new tail = bf16(bf16(Z[L-1, r + jj] + bias) - bias)   (serve/fast_codec.py:112-126).
+__global__ void convt_fold_kernel(const float* __restrict__ Z, const bf16* __restrict__ bias, int L, int r, int Co,
+                                  const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
+                                  int64_t tail_off, bf16* __restrict__ y) {
+  const int b = blockIdx.x;
+  const int o = blockIdx.y * blockDim.x + threadIdx.x;
+  if (o >= Co) return;
+  bf16* tail = state + (int64_t)slot32[b] * state_row + tail_off;  // [r, Co]
+  const float bo = to_f(bias[o]);
+  const int64_t zr = (int64_t)2 * r * Co;
+  const float* zb = Z + (int64_t)b * L * zr;
+  for (int t = 0; t < L; ++t)
+    for (int jj = 0; jj < r; ++jj) {
+      float v = zb[(int64_t)t * zr + (int64_t)jj * Co + o];
+      if (t > 0) v += zb[(int64_t)(t - 1) * zr + (int64_t)(jj + r) * Co + o];
+      v = rbf(v + bo);
+      if (t == 0) v = rbf(v + to_f(tail[(int64_t)jj * Co + o]));
+      y[((int64_t)b * L * r + (int64_t)t * r + jj) * Co + o] = to_bf(v);
+    }
+  for (int jj = 0; jj < r; ++jj) {
+    const float v = rbf(zb[(int64_t)(L - 1) * zr + (int64_t)(jj + r) * Co + o] + bo);
+    tail[(int64_t)jj * Co + o] = to_bf(v - bo);
+  }
+}
+
+// Final ELU + conv (C -> 1 channel, k taps, history k-1 rows of ELU(x)) -> fp32 PCM.  One CTA per row.
+__global__ void final_conv_kernel(const bf16* __restrict__ x, int L, int C, int k, const bf16* __restrict__ w,
+                                  const bf16* __restrict__ bias, const int* __restrict__ slot32,
+                                  bf16* __restrict__ state, int64_t state_row, int64_t hist_off,
+                                  float* __restrict__ pcm) {
+  extern __shared__ float fsm[];  // [(k-1) * C] history, then w [k * C]
+  const int b = blockIdx.x;
+  bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;
+  const int P = k - 1;
+  float* hs = fsm;
+  float* ws = fsm + P * C;
+  for (int i = threadIdx.x; i < P * C; i += blockDim.x) hs[i] = to_f(hist[i]);
+  for (int i = threadIdx.x; i < k * C; i += blockDim.x) ws[i] = to_f(w[i]);
+  __syncthreads();
+  const float bo = to_f(bias[0]);
+  for (int t = threadIdx.x; t < L; t += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int i = t + j;  // index into joined
+      for (int c = 0; c < C; ++c) {
+        const float v = i < P ? hs[i * C + c] : rbf(elu(to_f(x[((int64_t)b * L + i - P) * C + c])));
+        acc = fmaf(ws[j * C + c], v, acc);
+      }
+    }
+    pcm[(int64_t)b * L + t] = rbf(acc + bo);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < P * C; i += blockDim.x) {
+    const int row = L - P + i / C;  // last P rows of joined are new rows L-P .. L-1 (L >= P)
+    hist[i] = to_bf(elu(to_f(x[((int64_t)b * L + row) * C + i % C])));
+  }
+}
+
+}  // namespace m3
+
+// ================================================================================================ handle
+using namespace m3;
+
+struct m3_mimi {
+  m3_mimi_config c{};
+  const bf16 *books = nullptr, *proj_sem = nullptr, *proj_ac = nullptr, *upw = nullptr;
+  std::vector<const bf16*> ln1_w, ln1_b, wqkv, wo, ln2_w, ln2_b, fc1, fc2, ls1, ls2;
+  const float* inv_freq = nullptr;
+  const bf16 *conv0_w = nullptr, *conv0_b = nullptr, *final_w = nullptr, *final_b = nullptr;
+  std::vector<const bf16*> convt_w, convt_b, res1_w, res1_b, res2_w, res2_b;
+  bf16* state = nullptr;
+  bf16* kv = nullptr;
+  int64_t *key_pos = nullptr, *tokens = nullptr;
+  int64_t state_row = 0, up_off = 0, conv0_off = 0, final_off = 0;
+  std::vector<StageDims> stages;
+  void* ws = nullptr;
+  int *slot32 = nullptr, *status = nullptr;
+  int64_t* pos = nullptr;
+  bf16 *a_sem = nullptr, *a_ac = nullptr, *p_sem = nullptr, *p_ac = nullptr, *h = nullptr, *y = nullptr,
+       *qkv = nullptr, *q = nullptr, *att = nullptr, *ob = nullptr, *ff = nullptr, *act0 = nullptr, *act1 = nullptr,
+       *col = nullptr, *tmp = nullptr;
+  float* z = nullptr;
+};
+
+namespace {
+template <class T>
+T* carve(char*& p, size_t count) {
+  T* r = reinterpret_cast<T*>(p);
+  p += (count * sizeof(T) + 255) / 256 * 256;
+  return r;
+}
+
+// State row layout (elements, channels-last): upsample tail [s, H]; conv0 history [k-1, H]; per stage: convT tail
+// [r, cout], resnet k3 history [res_kernel-1, cout]; final conv history [last_kernel-1, num_filters].
+int64_t plan(const m3_mimi_config& c, std::vector<StageDims>* st, int64_t* up, int64_t* c0, int64_t* fin) {
+  int64_t off = 0;
+  *up = off;
+  off += (int64_t)c.upsample_stride * c.hidden;
+  *c0 = off;
+  off += (int64_t)(c.kernel - 1) * c.hidden;
+  int ch = (1 << c.n_ratios) * c.num_filters;
+  int L = c.upsample_stride;
+  for (int i = 0; i < c.n_ratios; ++i) {
+    StageDims s{ch, ch / 2, c.ratios[i], L, 0, 0};
+    s.tail_off = off;
+    off += (int64_t)s.r * s.cout;
+    s.hist_off = off;
+    off += (int64_t)(c.res_kernel - 1) * s.cout;
+    if (st) st->push_back(s);
+    L *= s.r;
+    ch /= 2;
+  }
+  *fin = off;
+  off += (int64_t)(c.last_kernel - 1) * c.num_filters;
+  return off;
+}
+}  // namespace
+
+extern "C" int64_t m3_mimi_state_elems(const m3_mimi_config* cfg) {
+  if (!cfg || cfg->n_ratios < 1 || cfg->n_ratios > 8) return -1;
+  int64_t a, b, c;
+  return plan(*cfg, nullptr, &a, &b, &c);
+}
+
+extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* w, m3_mimi** out) {
+  M3_REQUIRE(cfg && w && out, M3_ERR_ARG, "m3_mimi_create: null argument");
+  const m3_mimi_config& c = *cfg;
+  M3_REQUIRE(c.n_ratios >= 1 && c.n_ratios <= 8, M3_ERR_ARG, "n_ratios %d", c.n_ratios);
+  const int hd = c.hidden / c.heads;
+  M3_REQUIRE(c.hidden % c.heads == 0 && hd % 8 == 0 && hd <= 128 && c.heads <= 32, M3_ERR_UNSUPPORTED, "head dim");
+  M3_REQUIRE(c.ring <= kRingMax && c.ring >= c.window + c.upsample_stride, M3_ERR_ARG, "ring %d", c.ring);
+  M3_REQUIRE(c.upsample_stride <= 4 && c.upsample_stride <= 8 && c.kernel - 1 <= 8 && c.res_kernel - 1 <= 8 &&
+                 c.last_kernel - 1 <= 8,
+             M3_ERR_UNSUPPORTED, "kernel sizes");
+  M3_REQUIRE(c.hidden % 8 == 0 && c.ffn % 8 == 0, M3_ERR_UNSUPPORTED, "sizes must be multiples of 8");
+  auto* m = new m3_mimi();
+  m->c = c;
+  m->books = (const bf16*)w->codebooks;
+  m->proj_sem = (const bf16*)w->proj_sem;
+  m->proj_ac = (const bf16*)w->proj_ac;
+  m->upw = (const bf16*)w->upsample;
+  for (int i = 0; i < c.layers; ++i) {
+    m->ln1_w.push_back((const bf16*)w->ln1_w[i]);
+    m->ln1_b.push_back((const bf16*)w->ln1_b[i]);
+    m->wqkv.push_back((const bf16*)w->wqkv[i]);
+    m->wo.push_back((const bf16*)w->wo[i]);
+    m->ln2_w.push_back((const bf16*)w->ln2_w[i]);
+    m->ln2_b.push_back((const bf16*)w->ln2_b[i]);
+    m->fc1.push_back((const bf16*)w->fc1[i]);
+    m->fc2.push_back((const bf16*)w->fc2[i]);
+    m->ls1.push_back((const bf16*)w->ls1[i]);
+    m->ls2.push_back((const bf16*)w->ls2[i]);
+  }
+  m->inv_freq = w->inv_freq;
+  m->conv0_w = (const bf16*)w->conv0_w;
+  m->conv0_b = (const bf16*)w->conv0_b;
+  m->final_w = (const bf16*)w->final_w;
+  m->final_b = (const bf16*)w->final_b;
+  for (int i = 0; i < c.n_ratios; ++i) {
+    m->convt_w.push_back((const bf16*)w->convt_w[i]);
+    m->convt_b.push_back((const bf16*)w->convt_b[i]);
+    m->res1_w.push_back((const bf16*)w->res1_w[i]);
+    m->res1_b.push_back((const bf16*)w->res1_b[i]);
+    m->res2_w.push_back((const bf16*)w->res2_w[i]);
+    m->res2_b.push_back((const bf16*)w->res2_b[i]);
+  }
+  m->state = (bf16*)w->conv_state;
+  m->kv = (bf16*)w->kv;
+  m->key_pos = w->key_pos;
+  m->tokens = w->tokens;
+  m->state_row = plan(c, &m->stages, &m->up_off, &m->conv0_off, &m->final_off);
+  // scratch sized for max_rows
+  const size_t R = c.max_rows, T = c.upsample_stride, H = c.hidden;
+  size_t act = R * T * H, col = R * T * c.kernel * H, zf = R * T * H * 2;
+  for (const StageDims& s : m->stages) {
+    act = std::max(act, R * s.L * s.r * (size_t)s.cout);
+    col = std::max(col, R * s.L * s.r * (size_t)c.res_kernel * s.cout);
+    zf = std::max(zf, R * s.L * (size_t)2 * s.r * s.cout);
+    zf = std::max(zf, R * s.L * s.r * (size_t)s.cout);
+  }
+  zf = std::max(zf, R * T * (size_t)(1 << c.n_ratios) * c.num_filters);
+  act = std::max(act, R * T * (size_t)(1 << c.n_ratios) * c.num_filters);  // conv0 output
+  size_t bytes = 0;
+  auto add = [&](size_t n) { bytes += (n + 255) / 256 * 256; };
+  add(R * 4); add(256); add(R * T * 8);
+  add(R * c.codebook_dim * 2); add(R * c.codebook_dim * 2); add(R * H * 2); add(R * H * 2);
+  add(R * T * H * 2); add(R * T * H * 2); add(R * T * 3 * H * 2); add(R * T * H * 2); add(R * T * H * 2);
+  add(R * T * H * 2); add(R * T * c.ffn * 2);
+  add(act * 2); add(act * 2); add(col * 2); add(act * 2); add(zf * 4);
+  cudaError_t e = cudaMalloc(&m->ws, bytes);
+  if (e != cudaSuccess) {
+    delete m;
+    set_error("m3_mimi_create: cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    return M3_ERR_CUDA;
+  }
+  char* p = (char*)m->ws;
+  m->slot32 = carve<int>(p, R);
+  m->status = carve<int>(p, 64);
+  m->pos = carve<int64_t>(p, R * T);
+  m->a_sem = carve<bf16>(p, R * c.codebook_dim);
+  m->a_ac = carve<bf16>(p, R * c.codebook_dim);
+  m->p_sem = carve<bf16>(p, R * H);
+  m->p_ac = carve<bf16>(p, R * H);
+  m->h = carve<bf16>(p, R * T * H);
+  m->y = carve<bf16>(p, R * T * H);
+  m->qkv = carve<bf16>(p, R * T * 3 * H);
+  m->q = carve<bf16>(p, R * T * H);
+  m->att = carve<bf16>(p, R * T * H);
+  m->ob = carve<bf16>(p, R * T * H);
+  m->ff = carve<bf16>(p, R * T * c.ffn);
+  m->act0 = carve<bf16>(p, act);
+  m->act1 = carve<bf16>(p, act);
+  m->col = carve<bf16>(p, col);
+  m->tmp = carve<bf16>(p, act);
+  m->z = carve<float>(p, zf);
+  cudaMemset(m->status, 0, 256);
+  *out = m;
+  return M3_OK;
+}
+
+extern "C" int m3_mimi_destroy(m3_mimi* m) {
+  if (!m) return M3_OK;
+  cudaFree(m->ws);
+  delete m;
+  return M3_OK;
+}
+
+extern "C" int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear) {
+  M3_REQUIRE(m && status, M3_ERR_ARG, "m3_mimi_status: null argument");
+  M3_CUDA(cudaMemcpy(status, m->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (clear) M3_CUDA(cudaMemset(m->status, 0, sizeof(int32_t)));
+  return M3_OK;
+}
+
+__global__ void mimi_reset_kernel(bf16* state, int64_t state_row, int64_t* key_pos, int ring, int64_t* tokens,
+                                  int slot) {
+  for (int64_t i = threadIdx.x; i < state_row; i += blockDim.x) state[(int64_t)slot * state_row + i] = to_bf(0.f);
+  for (int i = threadIdx.x; i < ring; i += blockDim.x) key_pos[(int64_t)slot * ring + i] = kNever;
+  if (threadIdx.x == 0) tokens[slot] = 0;
+}
+
+extern "C" int m3_mimi_reset(m3_mimi* m, int32_t slot, int32_t zero_kv, m3_stream stream) {
+  M3_REQUIRE(m, M3_ERR_ARG, "m3_mimi_reset: null handle");
+  M3_REQUIRE(slot >= 0 && slot <= m->c.max_slots, M3_ERR_RANGE, "slot %d outside [0, %d]", slot, m->c.max_slots);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  mimi_reset_kernel<<<1, 256, 0, s>>>(m->state, m->state_row, m->key_pos, m->c.ring, m->tokens, slot);
+  M3_LAUNCHED();
+  if (zero_kv) {  // [layers, 2, rows, heads, ring, hd]: one strided block per (layer, k/v)
+    const int hd = m->c.hidden / m->c.heads;
+    const size_t blk = (size_t)m->c.heads * m->c.ring * hd;
+    const size_t rows = m->c.max_slots + 1;
+    for (int l = 0; l < 2 * m->c.layers; ++l)
+      M3_CUDA(cudaMemsetAsync(m->kv + ((size_t)l * rows + slot) * blk, 0, blk * 2, s));
+  }
+  return M3_OK;
+}
+
+__global__ void mimi_prep_kernel(const int64_t* __restrict__ slots, int rows, int max_slots, int* __restrict__ slot32,
+                                 int* status) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int64_t s = slots[r];
+  if (s < 0 || s > max_slots) {
+    report(status, M3_DEV_BAD_SLOT);
+    s = max_slots;
+  }
+  slot32[r] = (int)s;
+}
+
+extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* codes, float* pcm, int32_t rows,
+                              m3_stream stream) {
+  M3_REQUIRE(m && slots && codes && pcm, M3_ERR_ARG, "m3_mimi_decode: null argument");
+  const m3_mimi_config& c = m->c;
+  M3_REQUIRE(rows >= 0 && rows <= c.max_rows, M3_ERR_RANGE, "rows %d > max_rows %d", rows, c.max_rows);
+  if (rows == 0) return M3_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int R = rows, H = c.hidden, T = c.upsample_stride, hd = H / c.heads;
+  const int nb = norm_block(H);
+  mimi_prep_kernel<<<cdiv(R, 128), 128, 0, s>>>(slots, R, c.max_slots, m->slot32, m->status);
+  M3_LAUNCHED();
+  // RVQ decode -> two output projections (1x1 convs, bf16 outputs)
+  rvq_gather_kernel<<<R, 128, 0, s>>>(codes, c.n_q, c.n_semantic, c.codebook_size, c.codebook_dim, m->books,
+                                      m->a_sem, m->a_ac, m->status);
+  M3_LAUNCHED();
+  M3_TRY(gemm({m->a_sem, c.codebook_dim, m->proj_sem, c.codebook_dim, m->p_sem, H, R, H, c.codebook_dim, false}, s));
+  M3_TRY(gemm({m->a_ac, c.codebook_dim, m->proj_ac, c.codebook_dim, m->p_ac, H, R, H, c.codebook_dim, false}, s));
+  upsample_kernel<<<dim3(R, cdiv(H, 128)), 128, 0, s>>>(m->p_sem, m->p_ac, m->upw, T, m->slot32,
+                                                         m->state + m->up_off, m->state_row, m->h, H);
+  M3_LAUNCHED();
+  // decoder transformer over the frame's T tokens
+  tpos_kernel<<<cdiv(R, 128), 128, 0, s>>>(m->slot32, R, T, c.ring, m->tokens, m->key_pos, m->pos);
+  M3_LAUNCHED();
+  const int64_t rows_all = c.max_slots + 1;
+  const int64_t slot_stride = (int64_t)c.heads * c.ring * hd;  // one slot's block inside kv[layer][k|v]
+  const int64_t kv_half = rows_all * slot_stride;
+  add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, 1, H, 0, nullptr, nullptr, 0, nullptr, nullptr, m->y, m->ln1_w[0],
+                                     m->ln1_b[0], c.norm_eps, H);
+  M3_LAUNCHED();
+  for (int li = 0; li < c.layers; ++li) {
+    M3_TRY(gemm({m->y, H, m->wqkv[li], H, m->qkv, 3 * H, R * T, 3 * H, H, false}, s));
+    bf16* kr = m->kv + (int64_t)li * 2 * kv_half;
+    mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
+                                                   m->q, kr, kr + kv_half, slot_stride);
+    M3_LAUNCHED();
+    ring_attn_kernel<<<dim3(R, c.heads), 128, 0, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32, T,
+                                                       c.heads, hd, c.ring, c.window, slot_stride,
+                                                       1.f / sqrtf((float)hd), m->att);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->att, H, m->wo[li], H, m->ob, H, R * T, H, H, false}, s));
+    scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls1[li], m->y, m->ln2_w[li], m->ln2_b[li], c.norm_eps,
+                                             H);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->y, H, m->fc1[li], H, m->ff, c.ffn, R * T, c.ffn, H, false}, s));
+    const int64_t n8 = (int64_t)R * T * c.ffn / 8;
+    gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(m->ff, n8);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->ff, c.ffn, m->fc2[li], c.ffn, m->ob, H, R * T, H, c.ffn, false}, s));
+    const bool last = li + 1 == c.layers;
+    scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls2[li], m->y, last ? nullptr : m->ln1_w[li + 1],
+                                             last ? nullptr : m->ln1_b[li + 1], c.norm_eps, H);
+    M3_LAUNCHED();
+  }
+  tokens_advance_kernel<<<cdiv(R, 128), 128, 0, s>>>(m->slot32, R, T, c.max_slots, m->tokens);
+  M3_LAUNCHED();
+  // SEANet: conv0 (k taps, hidden -> C0)
+  const int C0 = (1 << c.n_ratios) * c.num_filters;
+  im2col_hist_kernel<<<dim3(R, cdiv(H, 128)), 128, 0, s>>>(m->h, T, H, c.kernel, 0, m->slot32, m->state,
+                                                            m->state_row, m->conv0_off, m->col);
+  M3_LAUNCHED();
+  M3_TRY(gemm({m->col, (int64_t)c.kernel * H, m->conv0_w, (int64_t)c.kernel * H, m->z, C0, R * T, C0, c.kernel * H,
+               true},
+              s));
+  int64_t n = (int64_t)R * T * C0;
+  bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->conv0_b, (int64_t)R * T, C0, 0, nullptr,
+                                                                   m->act0);
+  M3_LAUNCHED();
+  bf16* x = m->act0;
+  bf16* other = m->act1;
+  for (int i = 0; i < c.n_ratios; ++i) {
+    const StageDims& sd = m->stages[i];
+    const int64_t Min = (int64_t)R * sd.L, Mout = Min * sd.r;
+    // ELU -> ConvTranspose1d as X . Wt^T (fp32 contributions) -> fold with the overlap tail
+    elu_kernel<<<(unsigned)((Min * sd.cin + 255) / 256), 256, 0, s>>>(x, m->tmp, Min * sd.cin);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->tmp, sd.cin, m->convt_w[i], sd.cin, m->z, 2 * sd.r * sd.cout, (int)Min, 2 * sd.r * sd.cout, sd.cin,
+                 true},
+                s));
+    convt_fold_kernel<<<dim3(R, cdiv(sd.cout, 128)), 128, 0, s>>>(m->z, m->convt_b[i], sd.L, sd.r, sd.cout,
+                                                                   m->slot32, m->state, m->state_row, sd.tail_off,
+                                                                   other);
+    M3_LAUNCHED();
+    std::swap(x, other);  // x = stage output y (residual)
+    // resnet: ELU -> conv k3 (history) -> ELU -> conv k1 -> + y
+    const int hid = sd.cout / c.compress;
+    im2col_hist_kernel<<<dim3(R, cdiv(sd.cout, 128)), 128, 0, s>>>(x, sd.L * sd.r, sd.cout, c.res_kernel, 1,
+                                                                    m->slot32, m->state, m->state_row, sd.hist_off,
+                                                                    m->col);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->col, (int64_t)c.res_kernel * sd.cout, m->res1_w[i], (int64_t)c.res_kernel * sd.cout, m->z, hid,
+                 (int)Mout, hid, c.res_kernel * sd.cout, true},
+                s));
+    n = Mout * hid;
+    bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res1_b[i], Mout, hid, 1, nullptr,
+                                                                     m->tmp);
+    M3_LAUNCHED();
+    M3_TRY(gemm({m->tmp, hid, m->res2_w[i], hid, m->z, sd.cout, (int)Mout, sd.cout, hid, true}, s));
+    n = Mout * sd.cout;
+    bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res2_b[i], Mout, sd.cout, 2, x, other);
+    M3_LAUNCHED();
+    std::swap(x, other);
+  }
+  const StageDims& last = m->stages.back();
+  const int Lf = last.L * last.r;
+  const size_t fsmem = (size_t)(2 * c.last_kernel) * c.num_filters * sizeof(float);
+  final_conv_kernel<<<R, 256, fsmem, s>>>(x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32,
+                                          m->state, m->state_row, m->final_off, pcm);
+  M3_LAUNCHED();
+  return M3_OK;
+}

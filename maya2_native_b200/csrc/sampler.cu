@@ -1,0 +1,484 @@
+// Sampling kernels: the depth level sampler (replaces _topk_sample, serve/fast_depth_kernels.py:305-336) and the
+// cb0 sampler with controlled stop (replaces Engine._cb0 + row_exponential, maya3/engine.py:652-694,
+// serve/fast_depth_kernels.py:339-355).  One CTA per row; the top-k threshold is found by a bitwise search over
+// order-preserving integer keys (exact k-th largest, no sort); noise is counter-based Philox, bit-identical to the
+// reference's tl.rand stream for the same (seed, counter, level, code).
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "sampler.cuh"
+
+namespace m3 {
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as easy as 1, 2, 3", SC'11) on the counter
+// (offset, 0, 0, 0) with key (seed_lo, seed_hi); the first word as a uniform float in [0, 1) the way Triton's
+// uint_to_uniform_float folds it: int32 x -> (x < 0 ? -x - 1 : x) * 4.6566127342e-10.
+__device__ __forceinline__ float philox_uniform(int32_t seed, uint32_t offset) {
+  uint32_t c0 = offset, c1 = 0, c2 = 0, c3 = 0;
+  uint32_t k0 = (uint32_t)seed, k1 = seed < 0 ? 0xffffffffu : 0u;  // int32 seed widened to 64 bits
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hb = __umulhi(0xCD9E8D57u, c2), lb = 0xCD9E8D57u * c2;
+    const uint32_t ha = __umulhi(0xD2511F53u, c0), la = 0xD2511F53u * c0;
+    const uint32_t n0 = hb ^ c1 ^ k0, n2 = ha ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lb;
+    c2 = n2;
+    c3 = la;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  int32_t x = (int32_t)c0;
+  x = x < 0 ? -x - 1 : x;
+  return __fmul_rn((float)x, 4.6566127342e-10f);
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+constexpr int kSampThreads = 256;
+constexpr int kMaxPer = 16;  // up to 4096 entries per row
+
+// Largest key T with #(key >= T) >= k, i.e. the k-th largest key (1 <= k <= n).
+__device__ uint32_t kth_largest_key(const uint32_t (&key)[kMaxPer], int per, int k, int* red) {
+  uint32_t T = 0;
+  for (int b = 31; b >= 0; --b) {
+    const uint32_t cand = T | (1u << b);
+    int cnt = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
+      if (i < per) cnt += key[i] >= cand;
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = cnt;
+    __syncthreads();
+    int tot = 0;
+#pragma unroll
+    for (int w = 0; w < kSampThreads / 32; ++w) tot += red[w];
+    if (tot >= k) T = cand;
+  }
+  return T;
+}
+
+// Block argmax with the smallest index among equal maxima (torch / Triton argmax).
+__device__ int block_argmax(float v, int idx, float* redv, int* redi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) v = ov, idx = oi;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) redv[threadIdx.x >> 5] = v, redi[threadIdx.x >> 5] = idx;
+  __syncthreads();
+  v = redv[0];
+  idx = redi[0];
+#pragma unroll
+  for (int w = 1; w < kSampThreads / 32; ++w)
+    if (redv[w] > v || (redv[w] == v && redi[w] < idx)) v = redv[w], idx = redi[w];
+  return idx;
+}
+
+// ------------------------------------------------------------------------------------------------ depth sampler
+// x = logits * (1/temp); kth = k-th largest (0 when k is outside [1, V], as the reference's masked sum yields);
+// keep x >= kth; greedy -> argmax, else argmax(x - log(-log u)), u = tl.rand(seed, (ctr*32 + level)*V + c).
+// Optionally writes the next prefix row embed[code] (serve/fast_depth.py:195-196).
+template <typename TL>
+__global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
+    const TL* __restrict__ logits, int64_t ld, int V, const int32_t* __restrict__ seed,
+    const int32_t* __restrict__ ctr, const int* __restrict__ slot32, int level, float inv_temp, int k, int greedy,
+    int64_t* __restrict__ codes, int64_t code_stride, const bf16* __restrict__ embed, int D,
+    bf16* __restrict__ next_row, int64_t next_stride) {
+  __shared__ int red[32];
+  __shared__ float redv[32];
+  __shared__ int redi[32];
+  __shared__ int s_code;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int per = cdiv(V, kSampThreads);
+  const int sl = slot32 ? slot32[row] : row;
+  float x[kMaxPer];
+  uint32_t key[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    x[i] = -INFINITY;
+    key[i] = 0;
+    if (i < per && c < V) {
+      x[i] = to_f(logits[row * ld + c]) * inv_temp;
+      key[i] = order_key(x[i]);
+    }
+  }
+  float kth = 0.f;
+  if (k >= 1 && k <= V) kth = key_value(kth_largest_key(key, per, k, red));
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  const int32_t sd = greedy ? 0 : seed[sl];
+  const uint32_t base = greedy ? 0u : ((uint32_t)ctr[sl] * 32u + (uint32_t)level) * (uint32_t)V;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    if (i < per && c < V) {
+      float sc = x[i] >= kth ? x[i] : -INFINITY;
+      if (!greedy) {
+        const float u = fmaxf(philox_uniform(sd, base + (uint32_t)c), 1e-12f);
+        sc = sc - logf(-logf(u));
+      }
+      if (sc > best || bidx == 0x7fffffff) best = sc, bidx = c;
+    }
+  }
+  const int code = block_argmax(best, bidx, redv, redi);
+  if (tid == 0) {
+    codes[row * code_stride] = code;
+    s_code = code;
+  }
+  if (next_row) {
+    __syncthreads();
+    const uint4* src = reinterpret_cast<const uint4*>(embed + (int64_t)s_code * D);
+    uint4* dst = reinterpret_cast<uint4*>(next_row + row * next_stride);
+    for (int i = tid; i < D / 8; i += kSampThreads) dst[i] = src[i];
+  }
+}
+
+int launch_topk_sample(const void* logits, bool bf, int64_t ld, int rows, int V, const int32_t* seed,
+                       const int32_t* ctr, const int* slot32, int level, float inv_temp, int k, int greedy,
+                       int64_t* codes, int64_t code_stride, const bf16* embed, int D, bf16* next_row,
+                       int64_t next_stride, cudaStream_t s) {
+  M3_REQUIRE(V > 0 && V <= kSampThreads * kMaxPer, M3_ERR_UNSUPPORTED, "sampler width %d unsupported", V);
+  if (rows == 0) return M3_OK;
+  if (bf)
+    topk_sample_kernel<bf16><<<rows, kSampThreads, 0, s>>>((const bf16*)logits, ld, V, seed, ctr, slot32, level,
+                                                            inv_temp, k, greedy, codes, code_stride, embed, D,
+                                                            next_row, next_stride);
+  else
+    topk_sample_kernel<float><<<rows, kSampThreads, 0, s>>>((const float*)logits, ld, V, seed, ctr, slot32, level,
+                                                             inv_temp, k, greedy, codes, code_stride, embed, D,
+                                                             next_row, next_stride);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ cb0 sampler
+constexpr int kAeos = 2048;
+constexpr int kSortN = 4096;
+
+struct Cb0Dev {
+  int64_t* frames;
+  const int64_t* min_frames;
+  float* hazard;
+  const float* aeos_bias;
+  const float* temp;
+  const int64_t* top_k;
+  const float* top_p;
+  const float* rep;
+  const int32_t* seed;
+  int32_t* ctr;
+  int64_t* hist;
+  int rep_win;
+  int max_slots;
+};
+
+// Descending bitonic sort of (value, index) pairs in shared memory (kSortN entries, padding = -inf).
+__device__ void bitonic_sort_desc(float* v, short* ix) {
+  for (int size = 2; size <= kSortN; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < kSortN / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = ((lo & size) == 0);
+        const float a = v[lo], b = v[hi];
+        const bool swap = desc ? (a < b) : (a > b);
+        if (swap) {
+          v[lo] = b;
+          v[hi] = a;
+          const short t = ix[lo];
+          ix[lo] = ix[hi];
+          ix[hi] = t;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <typename TL>
+__global__ void __launch_bounds__(kSampThreads) cb0_sample_kernel(const TL* __restrict__ logits, int64_t ld, int V,
+                                                                  const int64_t* __restrict__ idx, Cb0Dev st,
+                                                                  int apply_rep, int apply_top_p,
+                                                                  int64_t* __restrict__ code_out,
+                                                                  int64_t* __restrict__ cb0_out, int* status) {
+  __shared__ float redf[32];
+  __shared__ int red[32];
+  __shared__ float redv[32];
+  __shared__ int redi[32];
+  __shared__ unsigned char pen[kSortN];
+  __shared__ float sv[kSortN];
+  __shared__ short si[kSortN];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int per = cdiv(V, kSampThreads);
+  int64_t slot = idx[row];
+  if (slot < 0 || slot > st.max_slots) {
+    report(status, M3_DEV_BAD_SLOT);
+    slot = st.max_slots;
+  }
+  // logits / temp (+ AEOS bias) (- presence penalty)   maya3/engine.py:657-665
+  const float temp = st.temp[slot];
+  if (apply_rep && st.rep_win > 0) {
+    for (int i = tid; i < V; i += kSampThreads) pen[i] = 0;
+    __syncthreads();
+    if (tid < st.rep_win) {
+      const int64_t h = st.hist[slot * st.rep_win + tid];
+      if (h >= 0 && h < V) pen[h] = 1;
+    }
+    __syncthreads();
+    if (tid == 0 && kAeos < V) pen[kAeos] = 0;
+    __syncthreads();
+  }
+  const float rep = st.rep[slot];
+  float x[kMaxPer];
+  uint32_t key[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    x[i] = -INFINITY;
+    key[i] = 0;
+    if (i < per && c < V) {
+      float v = to_f(logits[row * ld + c]) / temp;
+      if (c == kAeos) v += st.aeos_bias[slot];
+      if (apply_rep && st.rep_win > 0) v = v - rep * (pen[c] ? 1.f : 0.f);
+      x[i] = v;
+      key[i] = order_key(v);
+    }
+  }
+  // top-k: keep x >= k-th largest, k clamped to [1, V]   maya3/engine.py:666-668
+  int64_t k = st.top_k[slot];
+  k = k < 1 ? 1 : (k > V ? V : k);
+  const float kth = key_value(kth_largest_key(key, per, (int)k, red));
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i)
+    if (x[i] < kth) x[i] = -INFINITY;
+  // softmax
+  auto softmax = [&](float* p) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) mx = fmaxf(mx, x[i]);
+    mx = block_max(mx, redf);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      p[i] = (i < per && tid + i * kSampThreads < V) ? expf(x[i] - mx) : 0.f;
+      sum += p[i];
+    }
+    sum = block_sum(sum, redf);
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) p[i] = p[i] / sum;
+  };
+  float p[kMaxPer];
+  if (apply_top_p) {  // maya3/engine.py:669-672: drop entries whose preceding sorted mass exceeds top_p
+    softmax(p);
+    for (int i = tid; i < kSortN; i += kSampThreads) {
+      sv[i] = -INFINITY;
+      si[i] = (short)i;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int c = tid + i * kSampThreads;
+      if (i < per && c < V) sv[c] = p[i];
+    }
+    bitonic_sort_desc(sv, si);
+    // inclusive prefix sum of the sorted probabilities: each thread owns 16 consecutive entries
+    constexpr int kRun = kSortN / kSampThreads;
+    float run[kRun], tot = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) {
+      const float v = fmaxf(sv[tid * kRun + j], 0.f);
+      tot += v;
+      run[j] = tot;
+    }
+    // exclusive scan of thread totals
+    float incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, incl, o);
+      if ((tid & 31) >= o) incl += t;
+    }
+    __syncthreads();
+    if ((tid & 31) == 31) redf[tid >> 5] = incl;
+    __syncthreads();
+    float wpre = 0.f;
+    for (int w = 0; w < (tid >> 5); ++w) wpre += redf[w];
+    const float pre = wpre + incl - tot;
+    const float topp = st.top_p[slot];
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) {
+      const int pos = tid * kRun + j;
+      const float spv = fmaxf(sv[pos], 0.f);
+      const bool drop = (pre + run[j]) - spv > topp;
+      pen[pos] = 0;
+      sv[pos] = drop ? 1.f : 0.f;  // reuse as the drop flag of sorted position pos
+    }
+    __syncthreads();
+    for (int pos = tid; pos < kSortN; pos += kSampThreads) {
+      const int c = si[pos];
+      if (c < V && sv[pos] != 0.f) pen[c] = 1;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int c = tid + i * kSampThreads;
+      if (i < per && c < V && pen[c]) x[i] = -INFINITY;
+    }
+  }
+  softmax(p);
+  // controlled stop   maya3/engine.py:673-683
+  float pa = 0.f, best = -INFINITY;
+  int bidx = 0x7fffffff;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    if (i < per && c < V) {
+      if (c == kAeos) pa = p[i];
+      if (p[i] > best || bidx == 0x7fffffff) best = p[i], bidx = c;
+    }
+  }
+  const int arg = block_argmax(best, bidx, redv, redi);
+  pa = block_sum(pa, redf);  // only one thread holds the AEOS entry
+  // renormalise without AEOS, sample by the exponential race   maya3/engine.py:684-688
+  float qs = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    if (c == kAeos) p[i] = 0.f;
+    if (i < per && c < V) qs += p[i];
+  }
+  qs = fmaxf(block_sum(qs, redf), 1e-12f);
+  const int32_t sd = st.seed[slot];
+  const int32_t cr = st.ctr[slot];
+  const uint32_t base = (uint32_t)cr * 32u * 4096u;
+  best = -INFINITY;
+  bidx = 0x7fffffff;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int c = tid + i * kSampThreads;
+    if (i < per && c < V) {
+      const float u = fmaxf(philox_uniform(sd, base + (uint32_t)c), 1e-12f);
+      const float e = -logf(u);
+      const float r = (p[i] / qs) / e;
+      if (r > best || bidx == 0x7fffffff) best = r, bidx = c;
+    }
+  }
+  int cb0 = block_argmax(best, bidx, redv, redi);
+  if (cb0 > kAeos - 1) cb0 = kAeos - 1;
+  if (tid == 0) {
+    const int64_t frames = st.frames[slot];
+    const bool can = frames >= st.min_frames[slot];
+    float hz = st.hazard[slot];
+    if (can) hz = 1.f - (1.f - hz) * (1.f - pa);
+    int64_t code = 0;
+    if (can && hz >= 0.6f) code = 4;
+    if (can && pa >= 0.35f) code = 3;
+    if (can && arg == kAeos) code = 2;
+    code_out[row] = code;
+    cb0_out[row] = cb0;
+    st.ctr[slot] = cr + 1;
+    if (st.rep_win > 0) {
+      int64_t* h = st.hist + slot * st.rep_win;
+      for (int w = 0; w + 1 < st.rep_win; ++w) h[w] = h[w + 1];
+      h[st.rep_win - 1] = cb0;
+    }
+    st.hazard[slot] = hz;
+    st.frames[slot] = frames + 1;
+  }
+}
+
+}  // namespace m3
+
+using namespace m3;
+
+struct m3_cb0 {
+  m3_cb0_config c{};
+  Cb0Dev st{};
+  const bf16* head = nullptr;
+  void* ws = nullptr;
+  bf16* logits = nullptr;
+  int* status = nullptr;
+};
+
+extern "C" int m3_cb0_create(const m3_cb0_config* cfg, const m3_cb0_state* s, m3_cb0** out) {
+  M3_REQUIRE(cfg && s && out, M3_ERR_ARG, "m3_cb0_create: null argument");
+  M3_REQUIRE(cfg->n_cls > 0 && cfg->n_cls <= kSampThreads * kMaxPer, M3_ERR_UNSUPPORTED, "n_cls %d", cfg->n_cls);
+  M3_REQUIRE(cfg->rep_win >= 0 && cfg->rep_win <= kSampThreads, M3_ERR_UNSUPPORTED, "rep_win %d", cfg->rep_win);
+  M3_REQUIRE(cfg->hidden % 8 == 0, M3_ERR_UNSUPPORTED, "hidden %% 8");
+  auto* h = new m3_cb0();
+  h->c = *cfg;
+  h->head = (const bf16*)s->head;
+  h->st = Cb0Dev{s->frames, s->min_frames, s->hazard, s->aeos_bias, s->temp, s->top_k, s->top_p, s->rep, s->seed,
+                 s->ctr, s->hist, cfg->rep_win, cfg->max_slots};
+  const size_t lb = ((size_t)cfg->max_rows * cfg->n_cls * 2 + 255) / 256 * 256;
+  cudaError_t e = cudaMalloc(&h->ws, lb + 256);
+  if (e != cudaSuccess) {
+    delete h;
+    set_error("m3_cb0_create: cudaMalloc failed: %s", cudaGetErrorString(e));
+    return M3_ERR_CUDA;
+  }
+  h->logits = (bf16*)h->ws;
+  h->status = (int*)((char*)h->ws + lb);
+  cudaMemset(h->status, 0, 256);
+  *out = h;
+  return M3_OK;
+}
+
+extern "C" int m3_cb0_destroy(m3_cb0* s) {
+  if (!s) return M3_OK;
+  cudaFree(s->ws);
+  delete s;
+  return M3_OK;
+}
+
+static int cb0_launch(m3_cb0* s, const void* logits, bool bf, const int64_t* idx, int64_t* code, int64_t* cb0,
+                      int rows, int apply_rep, int apply_top_p, cudaStream_t st) {
+  if (rows == 0) return M3_OK;
+  if (bf)
+    cb0_sample_kernel<bf16><<<rows, kSampThreads, 0, st>>>((const bf16*)logits, s->c.n_cls, s->c.n_cls, idx,
+                                                            s->st, apply_rep, apply_top_p, code, cb0, s->status);
+  else
+    cb0_sample_kernel<float><<<rows, kSampThreads, 0, st>>>((const float*)logits, s->c.n_cls, s->c.n_cls, idx,
+                                                             s->st, apply_rep, apply_top_p, code, cb0, s->status);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+extern "C" int m3_cb0_step(m3_cb0* s, const void* h, const int64_t* idx, int64_t* code, int64_t* cb0, int32_t rows,
+                           int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
+  M3_REQUIRE(s && h && idx && code && cb0, M3_ERR_ARG, "m3_cb0_step: null argument");
+  M3_REQUIRE(rows >= 0 && rows <= s->c.max_rows, M3_ERR_RANGE, "rows %d > max_rows %d", rows, s->c.max_rows);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // cb0_head in the model dtype (bf16 output), read back as fp32 (tts/model/backbone.py:97, engine.py:657)
+  M3_TRY(gemm({(const bf16*)h, s->c.hidden, s->head, s->c.hidden, s->logits, s->c.n_cls, rows, s->c.n_cls,
+               s->c.hidden, false},
+              st));
+  return cb0_launch(s, s->logits, true, idx, code, cb0, rows, apply_rep, apply_top_p, st);
+}
+
+extern "C" int m3_cb0_sample_logits(m3_cb0* s, const float* logits, const int64_t* idx, int64_t* code, int64_t* cb0,
+                                    int32_t rows, int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
+  M3_REQUIRE(s && logits && idx && code && cb0, M3_ERR_ARG, "m3_cb0_sample_logits: null argument");
+  return cb0_launch(s, logits, false, idx, code, cb0, rows, apply_rep, apply_top_p,
+                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int m3_topk_sample(const void* logits, int32_t logits_bf16, int32_t rows, int32_t n, const int32_t* seed,
+                              const int32_t* ctr, int32_t level, float inv_temp, int32_t top_k, int32_t greedy,
+                              int64_t* codes, m3_stream stream) {
+  M3_REQUIRE(logits && codes && (greedy || (seed && ctr)), M3_ERR_ARG, "m3_topk_sample: null argument");
+  return launch_topk_sample(logits, logits_bf16 != 0, n, rows, n, seed, ctr, nullptr, level, inv_temp, top_k, greedy,
+                            codes, 1, nullptr, 0, nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+}

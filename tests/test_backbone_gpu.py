@@ -1,0 +1,132 @@
+"""GPU parity of the backbone decode (m3_backbone_step through the StaticBackbone mirror) against the reference's
+own fixtures and the CPU oracle.
+
+Tolerances: bf16 hidden states are compared by max-abs error relative to the tensor's scale, 2e-2 (the bf16 logit
+tolerance of the parity contract); bit-exact agreement is not expected because GEMM accumulation order differs.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from maya2_native_b200 import weights as WG
+from maya2_native_b200.backbone import StaticBackbone
+from maya2_native_b200.config import BASELINE, TINY
+from oracle.backbone import BackboneOracle
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def rel_maxabs(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    return float(np.abs(a - b).max() / max(1.0, float(np.abs(b).max())))
+
+
+def t(x, dev, dtype=torch.bfloat16):
+    return torch.as_tensor(np.asarray(x, np.float32)).to(dev, dtype)
+
+
+@pytest.mark.parametrize("use_graphs", [False, True])
+def test_tiny_matches_reference_fixture(cuda, use_graphs):
+    """The reference's fused bf16 path (fixture) on the same weights: inline prefill, decode, mixed steps."""
+    g = TINY.backbone
+    z = golden("backbone_tiny_bf16.npz")
+    sb = StaticBackbone(WG.backbone_weights(g), 3, capacity=64, ctx_buckets=(64,), batch_buckets=(1, 4, 8),
+                        use_graphs=use_graphs, geom=g)
+    x = [z[f"x{i}"] for i in range(6)]
+    outs = []
+    _, last = sb.step_mixed([], None, [(0, t(x[0][:5], cuda)), (1, t(x[0][5:], cuda))])
+    for i in (1, 2, 3):
+        outs.append((i, sb.step(list(z[f"slots{i}"]), t(x[i], cuda))))
+    dec, last4 = sb.step_mixed([0, 1], t(x[4][:2], cuda), [(2, t(x[4][2:], cuda))])
+    outs.append((5, sb.step(list(z["slots5"]), t(x[5], cuda))))
+    assert rel_maxabs(torch.stack(last).float().cpu(), z["out0"][[4, 7]]) < TOL
+    for i, y in outs:
+        assert rel_maxabs(y.float().cpu(), z[f"out{i}"]) < TOL, i
+    assert rel_maxabs(dec.float().cpu(), z["out4"][:2]) < TOL
+    assert rel_maxabs(last4[0].float().cpu(), z["out4"][-1]) < TOL
+    assert sb.lengths.cpu().tolist() == z["lengths"].tolist()
+    assert sb.lengths_cpu == z["lengths"].tolist()
+    assert sb.device_status() == 0
+
+
+@pytest.fixture(scope="module")
+def big():
+    g = BASELINE.backbone
+    shapes = {k: v for k, v in WG.backbone_shapes(g).items() if "embed_tokens" not in k}
+    W = WG.generate(shapes)
+    W["model.embed_tokens.weight"] = torch.zeros(1, g.hidden)
+    return g, W
+
+
+def _fill_random_kv(sb, orc, slot, length, seed):
+    gen = torch.Generator().manual_seed(seed)
+    g = sb.geom
+    keys = (torch.randn(g.layers, g.kv_heads, length, g.head_dim, generator=gen)).to(torch.bfloat16)
+    vals = (torch.randn(g.layers, g.kv_heads, length, g.head_dim, generator=gen)).to(torch.bfloat16)
+    sb.load_prefix(slot, [(keys[i][None].to(sb.device), vals[i][None].to(sb.device)) for i in range(g.layers)],
+                   length)
+    orc.load_slot(slot, keys.float().numpy(), vals.float().numpy(), length)
+
+
+def rel_l2(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_baseline_geometry_long_staggered_contexts(cuda, big):
+    """28-layer Qwen3-0.6B geometry; seats at staggered lengths up to the capacity edge (many KV splits, ragged
+    last stage), decode steps and a mixed step with an inline prefill.
+
+    On this random-init stack the reference's own bf16 arithmetic is chaotic: it sits ~5% (relative L2) from the
+    same computation in fp32.  So, as the reference's test_backbone_fused.py does, the bar is set against that noise
+    floor: the CUDA path must be within 2e-2 relative L2 of the bf16 oracle and no further from fp32 than the bf16
+    oracle itself is (x1.25)."""
+    g, W = big
+    cap = 2048
+    sb = StaticBackbone(W, 6, capacity=cap, ctx_buckets=(512, 2048), batch_buckets=(1, 8, 64), geom=g)
+    Wn = {k: v.numpy() for k, v in W.items()}
+    orc = BackboneOracle(Wn, g, 6, cap, "bf16")
+    o32 = BackboneOracle(Wn, g, 6, cap, "fp32")
+    lengths = {0: 1, 1: 37, 2: 300, 3: 1023, 4: 2040}
+    for s, n in lengths.items():
+        _fill_random_kv(sb, orc, s, n, seed=s)
+        o32.load_slot(s, orc.k[:, s, :, :n], orc.v[:, s, :, :n], n)
+    rng = np.random.default_rng(0)
+    slots = [0, 1, 2, 3, 4]
+
+    def check(y, r16, r32):
+        assert rel_l2(y, r16) < TOL
+        assert rel_l2(y, r32) < 1.25 * rel_l2(r16, r32) + 1e-3
+    for step in range(3):
+        x = rng.standard_normal((len(slots), g.hidden)).astype(np.float32)
+        y = sb.step(slots, t(x, cuda)).float().cpu().numpy()
+        check(y, orc.step(slots, x), o32.step(slots, x))
+    pre = rng.standard_normal((23, g.hidden)).astype(np.float32)
+    x = rng.standard_normal((2, g.hidden)).astype(np.float32)
+    dec, last = sb.step_mixed([2, 4], t(x, cuda), [(5, t(pre, cuda))])
+    rdec, rlast = orc.step_mixed([2, 4], x, [(5, pre)])
+    fdec, flast = o32.step_mixed([2, 4], x, [(5, pre)])
+    check(dec.float().cpu(), rdec, fdec)
+    check(last[0].float().cpu(), rlast[0], flast[0])
+    assert sb.lengths.cpu().tolist()[:6] == orc.lengths.tolist()[:6]
+    # the K cache rows the inline prefill wrote agree with the oracle's (first layer: no accumulated chaos)
+    assert rel_l2(sb.k[0][5, :, :23].float().cpu().numpy(), orc.k[0][5, :, :23]) < 5e-3
+    assert rel_l2(sb.v[0][5, :, :23].float().cpu().numpy(), orc.v[0][5, :, :23]) < 5e-3
+    check(sb.k[27][5, :, :23].float().cpu().numpy(), orc.k[27][5, :, :23], o32.k[27][5, :, :23])
+    assert sb.device_status() == 0
+
+
+def test_row_validation_matches_reference(cuda):
+    g = TINY.backbone
+    sb = StaticBackbone(WG.backbone_weights(g), 3, capacity=16, ctx_buckets=(16,), batch_buckets=(4,),
+                        use_graphs=False, geom=g)
+    x = torch.zeros(2, g.hidden, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError):
+        sb.step([1, 1], x)
+    with pytest.raises(IndexError):
+        sb.step([0, 3], x)
+    sb.lengths_cpu[0] = 16
+    with pytest.raises(ValueError):
+        sb.step([0], x[:1])

@@ -1,0 +1,73 @@
+"""The C ABI library loads and exports every entry point include/maya3_b200.h declares (no GPU calls), and the
+host-side layout logic agrees with the reference's.  CPU only."""
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+from maya2_native_b200 import _lib as L
+from maya2_native_b200.config import BASELINE, TINY
+from maya2_native_b200.weights import mimi_decoder_layout
+
+HEADER = os.path.join(REPO, "include", "maya3_b200.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^M3_API [^(]*?\b(m3_\w+)\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(L.LIB_PATH):
+        from maya2_native_b200.build import build
+        build()
+    return L.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_the_header():
+    assert sorted(L.SIGNATURES) == declared()
+
+
+def test_version_and_error_string(lib):
+    assert lib.m3_version() >= 1
+    assert isinstance(lib.m3_last_error(), bytes)
+
+
+def _mimi_cfg(g, max_slots=4):
+    return L.MimiConfig(g.hidden, g.n_q, g.n_semantic, g.codebook_size, g.codebook_dim, g.layers, g.heads, g.ffn,
+                        g.window, g.ring, len(g.ratios), (L.i32 * 8)(*(list(g.ratios) + [0] * (8 - len(g.ratios)))),
+                        g.num_filters, g.kernel, g.last_kernel, g.res_kernel, g.compress, g.upsample_stride,
+                        max_slots, max_slots, g.norm_eps)
+
+
+def test_mimi_state_row_matches_reference_layout(lib):
+    """StaticMimi keeps 12,672 state elements per slot at this geometry (serve/fast_codec.py:52-63, _plan :81-96):
+    the same histories and tails, here channels-last."""
+    assert lib.m3_mimi_state_elems(_mimi_cfg(BASELINE.mimi)) == 12672
+    g = TINY.mimi
+    ref = g.upsample_stride * g.hidden + (g.kernel - 1) * g.hidden
+    for _, kind, cin, cout, k, stride in mimi_decoder_layout(g):
+        if kind == "convt":
+            ref += stride * cout
+        elif kind == "resnet":
+            ref += (k - 1) * cin
+        elif kind == "conv" and cin == g.num_filters:
+            ref += (k - 1) * cin
+    assert lib.m3_mimi_state_elems(_mimi_cfg(g)) == ref
+
+
+def test_geometry_constants():
+    g = BASELINE.backbone
+    assert g.kv_bytes_per_token() == 112 * 1024          # docs/ENGINE.md:167
+    assert BASELINE.mimi.samples_per_frame == 1920
+    assert BASELINE.depth.group_of_level == (None, 0, 1, 2, 3, 4, 5, 6)
+    assert BASELINE.depth.head_dim == 128
