@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""Headline benchmark: Maya3 decode ticks under continuous batching at 256 streams per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+One step = one engine tick over all seats of a replica: backbone decode (+ inline prefill rows of refilled seats),
+cb0 sampling, the depth RVQ loop, the Mimi frame and the packed readout.  Seats run prompts of U[64,512] random token
+ids for U[100,1500] frames (stops disabled: forced lengths) and are refilled the tick they finish; the replica starts
+in the steady state of that process (per-seat KV lengths drawn from its stationary, length-biased distribution), so
+KV positions are staggered up to 2011.  Weights are random-init at the benchmark geometry (no checkpoint exists).
+
+Numbers (one JSON line on rank 0):
+  value       audio-seconds per second over all GPUs, device-timed: the K ticks' plans are staged in HBM before the
+              timed region and replayed back to back (CUDA events on the tick stream, max over ranks);
+  e2e         the same metric through the engine's public tick (TickEngine.tick): per tick the plan is copied
+              host->device and the packed (stop, cb0, PCM) readout device->host, with one sync, wall-clocked;
+  roofline    the split-KV decode attention (the dominant kernel) re-timed on the live cache after the run;
+  cpu_baseline the CPU oracle (fp32 numpy port of the reference's eager path) on this host's cores, on a bounded
+              sample (one tick of 16 seats at the same KV-length distribution).
+The KV cache (~60 GB per replica) is far larger than L2, so consecutive ticks never hit in L2 on the cache.
+Multi-GPU: one process per GPU, each an independent replica with its own 256 seats (weak scaling, no collective on
+the path; torch.distributed only for the start/stop barriers and the max-over-ranks reduction).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+FRAME_S = 0.08
+PROMPT = (64, 512)
+TARGET = (100, 1500)
+METRIC = "audio-s/s at 256 streams per GPU (continuous batching)"
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="native", choices=("native", "reference"))
+    ap.add_argument("--seats", type=int, default=256)
+    ap.add_argument("--capacity", type=int, default=2048)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seats", type=int, default=16)
+    ap.add_argument("--profile-ticks", type=int, default=0,
+                    help="after warm-up, run this many ticks inside cudaProfilerStart/Stop (for ncu "
+                         "--profile-from-start off) and exit")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------ workload
+class Workload:
+    """The closed-loop request stream of configs[2]: a finished seat is refilled immediately."""
+
+    def __init__(self, vocab, seed):
+        self.rng = np.random.default_rng(seed)
+        self.vocab = vocab
+
+    def request(self):
+        P = int(self.rng.integers(PROMPT[0], PROMPT[1] + 1))
+        T = int(self.rng.integers(TARGET[0], TARGET[1] + 1))
+        return self.rng.integers(0, self.vocab, P), T
+
+    def steady_state(self):
+        """A seat observed at a random time: its request's length is length-biased (density ~ T), its age uniform."""
+        P = int(self.rng.integers(PROMPT[0], PROMPT[1] + 1))
+        lo, hi = TARGET
+        T = int(np.sqrt(self.rng.uniform(lo * lo, hi * hi)))
+        age = int(self.rng.integers(0, T))
+        return P, T, age
+
+
+def init_steady_state(eng, wl, n_seats):
+    """Fill every seat with a request part-way through its frames; caches hold synthetic values."""
+    import torch
+    g = eng.geom
+    with torch.inference_mode():
+        for k, v in zip(eng.backbone.k, eng.backbone.v):
+            k.normal_()
+            v.normal_()
+        eng.codec.kv.normal_()
+        ring = g.mimi.ring
+        for _ in range(n_seats):
+            P, T, age = wl.steady_state()
+            s = eng.submit(wl.rng.integers(0, wl.vocab, P), T)
+            eng.pending.remove(s)
+            eng._bind(s)
+            L = P + age
+            eng.backbone.lengths[s.slot] = L
+            eng.backbone.lengths_cpu[s.slot] = L
+            s.frames = age
+            s.new = False
+            eng.cb0.frames_t[s.slot] = age
+            eng.cb0.ctr_t[s.slot] = age
+            eng.cb0.hist_t[s.slot] = torch.from_numpy(wl.rng.integers(0, 2048, eng.cfg.cb0_rep_win))
+            eng.depth.row_ctr[s.slot] = age
+            tok = 2 * age
+            eng.codec.tokens[s.slot] = tok
+            pos = np.arange(max(0, tok - ring), tok)
+            kp = np.full(ring, -(1 << 40), np.int64)
+            kp[pos % ring] = pos
+            eng.codec.key_pos[s.slot] = torch.from_numpy(kp)
+            eng.active.append(s)
+    torch.cuda.synchronize()
+
+
+def top_up(eng, wl):
+    while len(eng.pending) < 8:
+        p, T = wl.request()
+        eng.submit(p, T)
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, max clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        busy = [r for r in rows if r[2] > 250] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in busy for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in busy), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(busy)}
+
+
+# ------------------------------------------------------------------------------------------------ native arm
+def run_native(a, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.config import BASELINE
+    from maya2_native_b200.engine import TickConfig, TickEngine
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = BASELINE
+    W = WG.generate(WG.all_shapes(g), seed=a.seed, device=dev)
+    cfg = TickConfig(max_seats=a.seats, capacity=a.capacity, stops=False, max_inline_rows=512)
+    eng = TickEngine(g, W, cfg, device=dev)
+    del W
+    wl = Workload(g.backbone.vocab, a.seed * 7919 + rank)
+    init_steady_state(eng, wl, a.seats)
+    top_up(eng, wl)
+    for _ in range(a.warmup):
+        eng.tick()
+        top_up(eng, wl)
+    if a.profile_ticks:
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(a.profile_ticks):
+            eng.tick()
+            top_up(eng, wl)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        return {"profiled_ticks": a.profile_ticks}
+
+    # ---- device-resident run: plan K ticks on the host, stage them in HBM, replay back to back
+    plans = []
+    for _ in range(a.steps):
+        new = eng._admit(device=False)
+        dec = list(eng.active)
+        tp = eng.make_plan(dec, new)
+        eng.commit(tp)
+        eng.deliver_forced(dec + new)
+        top_up(eng, wl)
+        plans.append(tp)
+    for tp in plans:
+        eng.graph_for(tp.rows, tp.seats, tp.ctx)
+    staged = torch.from_numpy(np.concatenate([tp.plan for tp in plans])).to(dev)
+    offs = np.cumsum([0] + [len(tp.plan) for tp in plans])
+    frames = sum(len(tp.dec) + len(tp.new) for tp in plans)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    from maya2_native_b200 import _lib as L
+    lib = L.load()
+    launches = 0
+    with Clocks(local) as clk:
+        c0 = lib.m3_launch_count()
+        e0.record(stream)
+        for k, tp in enumerate(plans):
+            for s in tp.new:
+                eng.reset_slot(s)
+            gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
+            gr.plan.copy_(staged[offs[k]:offs[k + 1]], non_blocking=True)
+            eng.replay(gr, tp.rows, tp.seats, tp.ctx)
+            launches += gr.launches
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launches += lib.m3_launch_count() - c0          # eager launches in the region (slot resets)
+    dev_ms = e0.elapsed_time(e1)
+    status = eng.device_status()
+
+    # ---- end to end through the public tick: H2D plan + D2H readout + sync every tick, wall clock
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_frames, d2h = 0, 0
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        out = eng.tick()
+        e2e_frames += len(out)
+        d2h += len(out) * (2 + eng.spf // 4) * 8      # the packed readout rows copied back
+        top_up(eng, wl)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    h2d = int(np.mean([len(tp.plan) * 8 for tp in plans]))   # the tick plan (slots, offsets, prompt token ids)
+
+    # ---- roofline of the decode attention on the live cache (the last tick's rows)
+    tp = eng.make_plan(list(eng.active), [])
+    gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
+    gr.plan.copy_(torch.from_numpy(tp.plan).to(dev))
+    eng.replay(gr, tp.rows, tp.seats, tp.ctx)     # leaves this step's q / slots / positions in the scratch
+    eng.commit(tp)
+    eng.deliver_forced(tp.dec)
+    bg = g.backbone
+    reps = 20
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for i in range(reps):
+        L.check(lib.m3_backbone_attention(eng.backbone._handle, i % bg.layers, tp.rows, tp.ctx, L.stream_ptr()))
+    a1.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = a0.elapsed_time(a1) / reps
+    kv_bytes = tp.keys * bg.kv_heads * bg.head_dim * 2 * 2
+    qo_bytes = tp.rows * bg.heads * bg.head_dim * 2 * 2
+    attn_bytes = kv_bytes + qo_bytes
+
+    # ---- reduce over ranks
+    clocks = clk.summary()
+    vals = torch.tensor([dev_ms, e2e_s * 1e3, float(frames), float(e2e_frames)], device=dev, dtype=torch.float64)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx[:2], op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm[2:], op=dist.ReduceOp.SUM)
+        dev_ms, e2e_ms, frames, e2e_frames = float(mx[0]), float(mx[1]), float(sm[2]), float(sm[3])
+    else:
+        e2e_ms = e2e_s * 1e3
+    value = frames * FRAME_S / (dev_ms / 1e3)
+    e2e = e2e_frames * FRAME_S / (e2e_ms / 1e3)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(dev_ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompt token ids)",
+        "config": {"workload": "configs[2]: continuous batching, 256 seats/GPU, prompts U[64,512], targets "
+                               "U[100,1500] frames, refill on finish, KV positions staggered up to 2011",
+                   "seats_per_gpu": a.seats, "capacity": a.capacity, "geometry": "Qwen3-0.6B backbone, 4x1024 depth "
+                   "(8 codebooks), Mimi 8 codebooks", "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (KV cache ~60 GB per replica)"},
+        "e2e": {"value": round(e2e, 2), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": int(d2h / max(a.steps, 1))},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": "decode attention (split + combine)",
+                     "peak_source": peak_src, "algorithmic_bytes": int(attn_bytes), "launch_ms": round(attn_ms, 5)},
+        "tick_ms": round(dev_ms / a.steps, 4), "frames_timed": int(frames), "device_status": status,
+        "clocks": clocks,
+        "gpu_launches": int(launches),
+    }
+    eng.close()
+    return line
+
+
+# ------------------------------------------------------------------------------------------------ CPU arm
+def cpu_tick_sample(seats, seed=0, reps=1):
+    """The fp32 CPU oracle (numpy port of the reference's eager path) on `seats` seats at the configs[2] KV-length
+    distribution; returns (seconds per tick, threads)."""
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.config import BASELINE
+    from oracle.tick import OracleTick
+    g = BASELINE
+    shapes = {k: v for k, v in WG.all_shapes(g).items() if "embed_tokens" not in k}
+    W = {k: v.numpy() for k, v in WG.generate(shapes, seed=seed).items()}
+    wl = Workload(g.backbone.vocab, seed)
+    cap = 2048
+    o = OracleTick(W, g, seats, cap, "fp32")
+    bg = g.backbone
+    block = np.random.default_rng(seed).standard_normal((bg.kv_heads, 256, bg.head_dim)).astype(np.float32)
+    for s in range(seats):
+        P, T, age = wl.steady_state()
+        n = P + age
+        reps_ = -(-n // 256)
+        kv = np.tile(block, (1, reps_, 1))[:, :n]
+        o.bb.k[:, s, :, :n] = kv[None]
+        o.bb.v[:, s, :, :n] = kv[None]
+        o.bb.lengths[s] = n
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        o.tick(list(range(seats)))
+        times.append(time.perf_counter() - t0)
+    return min(times), os.cpu_count()
+
+
+def run_reference(a, rank, world):
+    """--impl reference: the reference's algorithm on this host's CPU cores (the numpy oracle port; the reference
+    is Python and cannot travel to this machine), one step = one tick of 8 seats at the configs[2] distribution."""
+    seats = 8
+    t_per = []
+    from maya2_native_b200 import weights as WG   # noqa: F401  (weights are generated inside the sample)
+    ticks = max(1, a.steps)
+    sec, cores = cpu_tick_sample(seats, a.seed, reps=1)
+    t_per.append(sec)
+    for _ in range(min(ticks - 1, 2)):
+        s2, _ = cpu_tick_sample(seats, a.seed, reps=1)
+        t_per.append(s2)
+    sec = float(np.median(t_per))
+    v = seats * FRAME_S / sec
+    return {"metric": METRIC, "value": round(v, 4), "unit": "audio-s/s", "n_gpus": world, "steps": len(t_per),
+            "warmup": 0, "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "configs[2] seat mix, CPU sample: one tick of 8 seats", "seats": seats},
+            "cpu_baseline": {"value": round(v, 4), "unit": "audio-s/s", "cores": cores, "kind": "port",
+                             "sample": f"one decode tick of {seats} seats at the configs[2] KV-length distribution"},
+            "e2e": {"value": round(v, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    a = args_()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if a.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(a, rank, world)), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    with torch.inference_mode():
+        line = run_native(a, rank, world, local)
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        sec, cores = cpu_tick_sample(a.cpu_seats, a.seed)
+        line["cpu_baseline"] = {"value": round(a.cpu_seats * FRAME_S / sec, 4), "unit": "audio-s/s", "cores": cores,
+                                "kind": "port", "sample": f"one decode tick of {a.cpu_seats} seats at the configs[2] "
+                                                          "KV-length distribution, fp32 numpy oracle"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -53,6 +53,9 @@ typedef void* m3_stream; /* cudaStream_t */
 
 M3_API const char* m3_last_error(void);
 M3_API int m3_version(void);
+/* Number of this library's kernel launches issued by this process so far (a launch captured into a CUDA graph
+ * counts once at capture; the difference across a capture is the number of library kernels in the graph). */
+M3_API int64_t m3_launch_count(void);
 
 /* ---------------------------------------------------------------------------------------------- utilities */
 /* Y[M,N] = X[M,K] . W[N,K]^T, bf16 inputs, fp32 accumulation, Y bf16 (y_f32 = 0) or fp32 (y_f32 = 1).
@@ -104,6 +107,10 @@ M3_API int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t
                      const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream);
 /* Read (and optionally clear) the device status word; synchronises with the device. */
 M3_API int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clear);
+/* Measurement hook: re-run layer `layer`'s decode attention (split-KV pass + combine) on the queries, slots and
+ * positions the last m3_backbone_step left in the handle's scratch (rows and ctx as that step), to time the kernel
+ * on the live cache.  Overwrites only the handle's attention output scratch. */
+M3_API int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream);
 
 /* ---------------------------------------------------------------------------------------------- cb0 sampler */
 /* Replaces Engine._cb0 + Backbone.cb0_logits + row_exponential (maya3/engine.py:652-694,
@@ -252,6 +259,37 @@ M3_API int m3_mimi_reset(m3_mimi* m, int32_t slot, int32_t zero_kv, m3_stream st
 M3_API int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* codes, float* pcm, int32_t rows,
                    m3_stream stream);
 M3_API int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear);
+
+/* ---------------------------------------------------------------------------------------------- tick */
+/* The device half of one engine tick (maya3/engine.py:534-561, Engine._tick from the backbone step through the
+ * packed readout) as one call over the four stage handles. */
+typedef struct m3_tick m3_tick;
+
+typedef struct {
+  m3_backbone* bb;
+  m3_cb0* cb0;
+  m3_depth* depth;
+  m3_mimi* mimi;
+  const void* embed;   /* [vocab, hidden] bf16 token embeddings read by inline-prefill rows (may be NULL) */
+  int64_t vocab;
+  void* feedback;      /* [max_slots + 1, hidden] bf16 per-slot next backbone input (maya3/engine.py:211) */
+  int32_t hidden, max_rows, max_seats, n_q, spf, max_slots;
+} m3_tick_config;
+
+M3_API int m3_tick_create(const m3_tick_config* cfg, m3_tick** out);
+M3_API int m3_tick_destroy(m3_tick* t);
+/* plan: device int64 [4 rows + 2 seats]: per backbone row (slot, offset, real, source) then per seat (slot, row of
+ * the backbone output holding its hidden state).  A row's source is -2 for a decode row (input = feedback[slot]),
+ * a prompt token id for an inline-prefill row (input = embed[token]) or -1 for a padding row (zeros).  Runs the
+ * backbone over `rows` rows, then cb0, depth, the feedback write-back, Mimi and the readout over `seats` seats;
+ * packed receives [seats, 2 + spf / 4] int64 (stop code, cb0, int16 PCM). */
+M3_API int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx, int32_t apply_rep,
+                       int32_t apply_top_p, int64_t* packed, m3_stream stream);
+/* Device pointers of the last tick's per-seat hidden states [max_seats, hidden] bf16, codes [max_seats, n_q] and
+ * fp32 PCM [max_seats, spf] (any may be NULL). */
+M3_API int m3_tick_outputs(m3_tick* t, void** h, int64_t** codes, float** pcm);
+/* First non-zero device status word over the tick and its stage handles; synchronises. */
+M3_API int m3_tick_status(m3_tick* t, int32_t* status, int32_t clear);
 
 /* ---------------------------------------------------------------------------------------------- readout */
 /* The engine's per-tick readout (maya3/engine.py:557-561): packed [rows, 2 + spf / 4] int64 rows holding

@@ -72,15 +72,23 @@ class MimiWeights(C.Structure):
                 ("final_b", vp), ("conv_state", vp), ("kv", vp), ("key_pos", vp), ("tokens", vp)]
 
 
+class TickConfig(C.Structure):
+    _fields_ = [("bb", vp), ("cb0", vp), ("depth", vp), ("mimi", vp), ("embed", vp), ("vocab", i64),
+                ("feedback", vp), ("hidden", i32), ("max_rows", i32), ("max_seats", i32), ("n_q", i32), ("spf", i32),
+                ("max_slots", i32)]
+
+
 # name -> (restype, argtypes); every entry point declared in include/maya3_b200.h
 SIGNATURES = {
     "m3_last_error": (C.c_char_p, []),
     "m3_version": (C.c_int, []),
+    "m3_launch_count": (i64, []),
     "m3_gemm_bf16": (C.c_int, [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp]),
     "m3_backbone_create": (C.c_int, [P(BackboneConfig), P(BackboneWeights), P(vp)]),
     "m3_backbone_destroy": (C.c_int, [vp]),
     "m3_backbone_step": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, vp]),
     "m3_backbone_status": (C.c_int, [vp, P(i32), i32]),
+    "m3_backbone_attention": (C.c_int, [vp, i32, i32, i32, vp]),
     "m3_cb0_create": (C.c_int, [P(Cb0Config), P(Cb0State), P(vp)]),
     "m3_cb0_destroy": (C.c_int, [vp]),
     "m3_cb0_step": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
@@ -98,6 +106,11 @@ SIGNATURES = {
     "m3_mimi_decode": (C.c_int, [vp, vp, vp, vp, i32, vp]),
     "m3_mimi_status": (C.c_int, [vp, P(i32), i32]),
     "m3_pack_readout": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+    "m3_tick_create": (C.c_int, [P(TickConfig), P(vp)]),
+    "m3_tick_destroy": (C.c_int, [vp]),
+    "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
+    "m3_tick_outputs": (C.c_int, [vp, P(vp), P(vp), P(vp)]),
+    "m3_tick_status": (C.c_int, [vp, P(i32), i32]),
 }
 
 _lock = threading.Lock()

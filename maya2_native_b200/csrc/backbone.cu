@@ -532,6 +532,7 @@ static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t
   attn_split_kernel<GG><<<grid, kAttnThreads, sizeof(AttnSmem<GG>), s>>>(                                    \
       bb->q, bb->kc[layer], bb->vc[layer], slot_stride, head_stride, bb->slot32, bb->pos32, bb->part_o,     \
       bb->part_ml, nsplit, chunk, c.heads, qscale, bb->status);                                             \
+  M3_LAUNCHED();                                                                                             \
   attn_combine_kernel<GG><<<dim3(c.kv_heads, rows), kHeadDim, 0, s>>>(bb->part_o, bb->part_ml, bb->pos32,   \
                                                                       bb->o, nsplit, chunk, c.heads);
   if (G == 1) {
@@ -593,4 +594,12 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
   lengths_add_kernel<<<cdiv(rows, 128), 128, 0, s>>>(bb->slot32, real, rows, bb->lengths);
   M3_LAUNCHED();
   return M3_OK;
+}
+
+extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream) {
+  M3_REQUIRE(bb, M3_ERR_ARG, "m3_backbone_attention: null handle");
+  M3_REQUIRE(layer >= 0 && layer < bb->c.layers && rows > 0 && rows <= bb->c.max_rows && ctx > 0 &&
+                 ctx <= bb->c.capacity,
+             M3_ERR_RANGE, "m3_backbone_attention: layer %d rows %d ctx %d out of range", layer, rows, ctx);
+  return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
 }

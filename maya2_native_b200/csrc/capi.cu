@@ -1,4 +1,5 @@
 // Library-wide C ABI pieces: error reporting, version, and the engine's per-tick readout packing.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -16,6 +17,10 @@ void set_error(const char* fmt, ...) {
 }
 
 const char* last_error() { return g_err; }
+
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 // One row per seat: [stop code, cb0, pcm16 packed four samples per int64] (maya3/engine.py:557-561):
 // pcm16 = round(clamp(pcm, -1, 1) * 32767) with round-half-to-even, as torch.round.
@@ -48,6 +53,8 @@ __global__ void pack_readout_kernel(const int64_t* __restrict__ code, const int6
 extern "C" const char* m3_last_error(void) { return m3::last_error(); }
 
 extern "C" int m3_version(void) { return 1; }
+
+extern "C" int64_t m3_launch_count(void) { return m3::launch_count(); }
 
 extern "C" int m3_pack_readout(const int64_t* code, const int64_t* cb0, const float* pcm, int64_t* packed,
                                int32_t rows, int32_t spf, m3_stream stream) {

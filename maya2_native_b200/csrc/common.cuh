@@ -41,8 +41,14 @@ const char* last_error();
     }                                 \
   } while (0)
 
-// Launch-error check after a kernel launch (does not synchronize).
-#define M3_LAUNCHED() M3_CUDA(cudaGetLastError())
+// Every launch of one of this library's kernels is followed by M3_LAUNCHED(): it counts the launch (the count a
+// CUDA graph capture sees is the number of this library's kernels in the graph) and checks the launch error.
+void count_launch();
+#define M3_LAUNCHED()                  \
+  do {                                 \
+    ::m3::count_launch();              \
+    M3_CUDA(cudaGetLastError());       \
+  } while (0)
 
 // Device status word: kernels record the first problem they see (bad index, timed-out wait) and carry on safely;
 // the host reads it after the tick's synchronization point.

@@ -121,9 +121,10 @@ __global__ void add_ln_kernel(const bf16* __restrict__ src, int T, int64_t sb, i
 }
 
 // ------------------------------------------------------------------------------------------------ attention
-// Tiny attention over at most kMaxKeys positions: query i of row b sits at absolute position q0 + i and sees keys
-// 0..q0+i (causal; the last-position and incremental forms are q0 = n-1 with one query).  One warp per query, lanes
-// split the head dim; fp32 scores and softmax, output rounded once (F.scaled_dot_product_attention).
+// Tiny attention over at most kMaxKeys positions: query i of seat b sits at absolute position q0 + i and sees keys
+// 0..q0+i (causal; the last-position and incremental forms are q0 = n-1 with one query).  One warp per
+// (seat, head, query), each lane holding PER consecutive dims; fp32 scores with an online softmax, output rounded
+// once (F.scaled_dot_product_attention).
 constexpr int kMaxKeys = 64;
 
 struct KeySrc {
@@ -132,47 +133,53 @@ struct KeySrc {
   int64_t sb, sj;
 };
 
-__global__ void depth_attn_kernel(const bf16* __restrict__ qkv, int T, int q0, int Tq, KeySrc ks, int H, int HD,
-                                  float scale, bf16* __restrict__ out) {
-  const int b = blockIdx.x, h = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int D = H * HD;
-  for (int i = warp; i < Tq; i += nw) {
-    const int qp = q0 + i;  // absolute position of this query
-    // the queries are the last Tq of the T qkv rows of seat b
-    const bf16* q = qkv + ((int64_t)b * T + (T - Tq) + i) * 3 * D + (int64_t)h * HD;
-    float qv[4];
-    const int per = HD / 32;
-    for (int e = 0; e < per; ++e) qv[e] = to_f(q[lane * per + e]);
-    float s[kMaxKeys];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kMaxKeys; ++j) {
-      if (j > qp) break;
-      const bf16* kr = ks.k + (int64_t)b * ks.sb + (int64_t)j * ks.sj + (int64_t)h * HD;
-      float d = 0.f;
-      for (int e = 0; e < per; ++e) d = fmaf(qv[e], to_f(kr[lane * per + e]), d);
-      d = warp_sum(d) * scale;
-      s[j] = d;
-      mx = fmaxf(mx, d);
-    }
-    float den = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxKeys; ++j) {
-      if (j > qp) break;
-      s[j] = expf(s[j] - mx);
-      den += s[j];
-    }
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < kMaxKeys; ++j) {
-      if (j > qp) break;
-      const bf16* vr = ks.v + (int64_t)b * ks.sb + (int64_t)j * ks.sj + (int64_t)h * HD;
-      for (int e = 0; e < per; ++e) o[e] = fmaf(s[j], to_f(vr[lane * per + e]), o[e]);
-    }
-    bf16* dst = out + ((int64_t)b * Tq + i) * D + (int64_t)h * HD;
-    for (int e = 0; e < per; ++e) dst[lane * per + e] = to_bf(o[e] / den);
+template <int PER>
+__device__ __forceinline__ void load_per(const bf16* p, float* f) {
+  if constexpr (PER == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    f[0] = bf_lo(u.x); f[1] = bf_hi(u.x); f[2] = bf_lo(u.y); f[3] = bf_hi(u.y);
+  } else if constexpr (PER == 2) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    f[0] = bf_lo(u); f[1] = bf_hi(u);
+  } else {
+    f[0] = to_f(*p);
   }
+}
+
+template <int PER>
+__global__ void depth_attn_kernel(const bf16* __restrict__ qkv, int T, int q0, int Tq, KeySrc ks, int H,
+                                  float scale, bf16* __restrict__ out) {
+  constexpr int HD = 32 * PER;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int i = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (i >= Tq) return;
+  const int D = H * HD;
+  const int qp = q0 + i;
+  const bf16* q = qkv + ((int64_t)b * T + (T - Tq) + i) * 3 * D + (int64_t)h * HD + lane * PER;
+  float qv[PER], kv[PER], o[PER];
+  load_per<PER>(q, qv);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) o[e] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const bf16* kb = ks.k + (int64_t)b * ks.sb + (int64_t)h * HD + lane * PER;
+  const bf16* vb = ks.v + (int64_t)b * ks.sb + (int64_t)h * HD + lane * PER;
+  for (int j = 0; j <= qp && j < kMaxKeys; ++j) {
+    load_per<PER>(kb + (int64_t)j * ks.sj, kv);
+    float d = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) d = fmaf(qv[e], kv[e], d);
+    d = warp_sum(d) * scale;
+    const float mn = fmaxf(m, d);
+    const float c = expf(m - mn), p = expf(d - mn);
+    load_per<PER>(vb + (int64_t)j * ks.sj, kv);
+    l = l * c + p;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) o[e] = fmaf(p, kv[e], o[e] * c);
+    m = mn;
+  }
+  bf16* dst = out + ((int64_t)b * Tq + i) * D + (int64_t)h * HD + lane * PER;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) dst[e] = to_bf(o[e] / l);
 }
 
 // kvbuf[b, p0 + t] = (k, v) of qkv rows t of b  (serve/fast_depth.py:170,176)
@@ -294,8 +301,8 @@ extern "C" int m3_depth_create(const m3_depth_config* cfg, const m3_depth_weight
   M3_REQUIRE(cfg && w && out, M3_ERR_ARG, "m3_depth_create: null argument");
   const m3_depth_config& c = *cfg;
   M3_REQUIRE(c.n_q >= 2 && c.n_q <= 64 && c.n_q <= kMaxKeys, M3_ERR_UNSUPPORTED, "n_q %d", c.n_q);
-  M3_REQUIRE(c.d % c.heads == 0 && (c.d / c.heads) % 32 == 0 && c.d / c.heads <= 128, M3_ERR_UNSUPPORTED,
-             "depth head dim must be 32, 64, 96 or 128");
+  M3_REQUIRE(c.d % c.heads == 0 && (c.d / c.heads == 32 || c.d / c.heads == 64 || c.d / c.heads == 128),
+             M3_ERR_UNSUPPORTED, "depth head dim must be 32, 64 or 128");
   M3_REQUIRE(c.d % 8 == 0 && c.ffn % 8 == 0 && c.d_backbone % 8 == 0 && c.d <= 8192, M3_ERR_UNSUPPORTED, "sizes");
   auto* d = new m3_depth();
   d->c = c;
@@ -438,18 +445,27 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       KeySrc ks;
       if (incremental) {
         kv_store_kernel<<<dim3(R, 1), 128, 0, s>>>(d->qkvb, 1, kvl, NL, level, D);
+        M3_LAUNCHED();
         ks = {kvl, kvl + D, (int64_t)NL * 2 * D, 2 * D};
         q0 = level;
       } else {
-        if (reused_later) kv_store_kernel<<<dim3(R, n), 128, 0, s>>>(d->qkvb, n, kvl, NL, 0, D);
+        if (reused_later) {
+          kv_store_kernel<<<dim3(R, n), 128, 0, s>>>(d->qkvb, n, kvl, NL, 0, D);
+          M3_LAUNCHED();
+        }
         ks = {d->qkvb + D, d->qkvb + 2 * D, (int64_t)n * 3 * D, 3 * D};
         if (li == L - 1) {
           Tq = 1;
           q0 = n - 1;
         }
       }
-      M3_LAUNCHED();
-      depth_attn_kernel<<<dim3(R, H), 128, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, HD, scale, d->a);
+      const dim3 ag(R, H);
+      if (HD == 128)
+        depth_attn_kernel<4><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
+      else if (HD == 64)
+        depth_attn_kernel<2><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
+      else
+        depth_attn_kernel<1><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
       M3_LAUNCHED();
       if (Tq != Tr) {  // the last layer keeps only each seat's final position
         take_last_kernel<<<R, 128, 0, s>>>(d->x, Tr, d->x2, D);

@@ -113,26 +113,29 @@ __global__ void mimi_rope_kernel(const bf16* __restrict__ qkv, const int64_t* __
 }
 
 // Sliding-window attention of the frame's T queries over the slot's ring: key r is visible to the query at
-// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head); one
-// thread per ring entry for the scores, one thread per (query, dim) for the weighted sum.
+// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head): one
+// thread per ring entry for the scores (16-byte key loads), then the weighted sum split over 8-dim column groups x
+// ring chunks, reduced through shared memory.
 constexpr int kRingMax = 512;
+constexpr int kRingThreads = 256;
 
-__global__ void ring_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kring,
-                                 const bf16* __restrict__ vring, const int64_t* __restrict__ key_pos,
-                                 const int64_t* __restrict__ pos, const int* __restrict__ slot32, int T, int heads,
-                                 int hd, int ring, int window, int64_t slot_stride, float scale,
-                                 bf16* __restrict__ out) {
+__global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ kring, const bf16* __restrict__ vring,
+    const int64_t* __restrict__ key_pos, const int64_t* __restrict__ pos, const int* __restrict__ slot32, int T,
+    int heads, int hd, int ring, int window, int64_t slot_stride, float scale, bf16* __restrict__ out) {
   __shared__ float sc[4][kRingMax];
   __shared__ float qs[4][128];
   __shared__ float red[32];
+  __shared__ float part[kRingThreads * 8];
   const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int H = heads * hd;
   const int s = slot32[b];
   const bf16* K = kring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
   const bf16* V = vring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
-  for (int i = tid; i < T * hd; i += blockDim.x) qs[i / hd][i % hd] = to_f(q[((int64_t)b * T + i / hd) * H + h * hd + i % hd]);
+  for (int i = tid; i < T * hd; i += kRingThreads)
+    qs[i / hd][i % hd] = to_f(q[((int64_t)b * T + i / hd) * H + h * hd + i % hd]);
   __syncthreads();
-  for (int r = tid; r < ring; r += blockDim.x) {
+  for (int r = tid; r < ring; r += kRingThreads) {
     const int64_t kp = key_pos[(int64_t)s * ring + r];
     const uint4* kr = reinterpret_cast<const uint4*>(K + (int64_t)r * hd);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -152,25 +155,42 @@ __global__ void ring_attn_kernel(const bf16* __restrict__ q, const bf16* __restr
   __syncthreads();
   for (int t = 0; t < T; ++t) {
     float mx = -INFINITY;
-    for (int r = tid; r < ring; r += blockDim.x) mx = fmaxf(mx, sc[t][r]);
+    for (int r = tid; r < ring; r += kRingThreads) mx = fmaxf(mx, sc[t][r]);
     mx = block_max(mx, red);
     float sum = 0.f;
     __syncthreads();
-    for (int r = tid; r < ring; r += blockDim.x) {
+    for (int r = tid; r < ring; r += kRingThreads) {
       const float e = sc[t][r] == -INFINITY ? 0.f : expf(sc[t][r] - mx);
       sc[t][r] = e;
       sum += e;
     }
     sum = block_sum(sum, red);
     __syncthreads();
-    for (int r = tid; r < ring; r += blockDim.x) sc[t][r] /= sum;
+    for (int r = tid; r < ring; r += kRingThreads) sc[t][r] /= sum;
   }
   __syncthreads();
-  for (int i = tid; i < T * hd; i += blockDim.x) {
-    const int t = i / hd, d = i % hd;
-    float o = 0.f;
-    for (int r = 0; r < ring; ++r) o = fmaf(sc[t][r], to_f(V[(int64_t)r * hd + d]), o);
-    out[((int64_t)b * T + t) * H + h * hd + d] = to_bf(o);
+  // weighted sum: pair = (query, 8-dim group); chunks of the ring per thread group
+  const int G8 = hd / 8, pairs = T * G8, chunks = kRingThreads / pairs;
+  const int pi = tid % pairs, ch = tid / pairs;
+  const int t = pi / G8, g = pi % G8;
+  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (ch < chunks)
+    for (int r = ch; r < ring; r += chunks) {
+      const float pr = sc[t][r];
+      float vf[8];
+      unpack8(reinterpret_cast<const uint4*>(V + (int64_t)r * hd)[g], vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = fmaf(pr, vf[e], o[e]);
+    }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) part[tid * 8 + e] = o[e];
+  __syncthreads();
+  for (int i = tid; i < pairs * 8; i += kRingThreads) {
+    const int pp = i / 8, e = i % 8;
+    float v = 0.f;
+    for (int c = 0; c < chunks; ++c) v += part[(c * pairs + pp) * 8 + e];
+    const int tt = pp / G8, gg = pp % G8;
+    out[((int64_t)b * T + tt) * H + h * hd + gg * 8 + e] = to_bf(v);
   }
 }
 
@@ -235,107 +255,178 @@ __global__ void tokens_advance_kernel(const int* __restrict__ slot32, int rows, 
 // ------------------------------------------------------------------------------------------------ SEANet
 __device__ __forceinline__ float elu(float x) { return x > 0.f ? x : expm1f(x); }
 
-// im2col of a causal stride-1 conv with k taps over [history (k-1 rows, stored), new rows]:
-// A[b*L + t, j*C + c] = joined[t + j][c], joined = [hist; act(x)] with act = ELU (rounded) when elu_in.
-// The slot's history becomes the last k-1 rows of joined.  One CTA per (row, channel chunk): every read of the
-// history happens before the CTA's own write of it.
-__global__ void im2col_hist_kernel(const bf16* __restrict__ x, int L, int C, int k, int elu_in,
-                                   const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
-                                   int64_t hist_off, bf16* __restrict__ A) {
-  const int b = blockIdx.x;
-  const int c = blockIdx.y * blockDim.x + threadIdx.x;
-  const bool on = c < C;
-  bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;  // [k-1, C]
-  const int P = k - 1;
-  float hv[8];
-  for (int j = 0; j < P && on; ++j) hv[j] = to_f(hist[(int64_t)j * C + c]);
-  __syncthreads();
-  if (!on) return;
-  auto joined = [&](int i) -> float {
-    if (i < P) return hv[i];
-    const float v = to_f(x[((int64_t)b * L + (i - P)) * C + c]);
-    return elu_in ? rbf(elu(v)) : v;
-  };
-  for (int t = 0; t < L; ++t)
-    for (int j = 0; j < k; ++j) A[((int64_t)b * L + t) * k * C + (int64_t)j * C + c] = to_bf(joined(t + j));
-  for (int j = 0; j < P; ++j) hist[(int64_t)j * C + c] = to_bf(joined(L + j));
+__device__ __forceinline__ uint4 elu8(const uint4& u) {
+  float f[8];
+  unpack8(u, f);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) f[e] = elu(f[e]);
+  return pack8(f);
 }
 
-// y = bf16(z + bias); mode 1: y = bf16(elu(y)); mode 2: y = bf16(res + y)
+// im2col of a causal stride-1 conv with k taps over joined = [history (k-1 stored rows); act(x)], act = ELU
+// (rounded) when elu_in: A[b*L + t, j*C + c] = joined[t + j][c].  One thread per (row, step, 8 channels); the
+// history itself is refreshed afterwards by conv_hist_kernel (so no thread reads a row another thread rewrote).
+__global__ void im2col_kernel(const bf16* __restrict__ x, int L, int C, int k, int elu_in,
+                              const int* __restrict__ slot32, const bf16* __restrict__ state, int64_t state_row,
+                              int64_t hist_off, bf16* __restrict__ A) {
+  const int b = blockIdx.x;
+  const int C8 = C / 8, P = k - 1;
+  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  if (idx >= L * C8) return;
+  const int t = idx / C8, c8 = idx % C8;
+  const uint4* hist = reinterpret_cast<const uint4*>(state + (int64_t)slot32[b] * state_row + hist_off);
+  const uint4* xs = reinterpret_cast<const uint4*>(x + (int64_t)b * L * C);
+  uint4* dst = reinterpret_cast<uint4*>(A + ((int64_t)b * L + t) * k * C);
+  for (int j = 0; j < k; ++j) {
+    const int i = t + j;
+    uint4 v;
+    if (i < P) {
+      v = hist[i * C8 + c8];
+    } else {
+      v = xs[(int64_t)(i - P) * C8 + c8];
+      if (elu_in) v = elu8(v);
+    }
+    dst[j * C8 + c8] = v;
+  }
+}
+
+// The conv's history becomes the last k-1 rows of joined (serve/fast_codec.py:106-110).  One thread per
+// (row, 8 channels) reads the old rows it needs before writing.
+__global__ void conv_hist_kernel(const bf16* __restrict__ x, int L, int C, int k, int elu_in,
+                                 const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
+                                 int64_t hist_off) {
+  const int b = blockIdx.x;
+  const int C8 = C / 8, P = k - 1;
+  const int c8 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c8 >= C8 || P == 0) return;
+  uint4* hist = reinterpret_cast<uint4*>(state + (int64_t)slot32[b] * state_row + hist_off);
+  const uint4* xs = reinterpret_cast<const uint4*>(x + (int64_t)b * L * C);
+  uint4 old[8];
+  for (int j = 0; j < P; ++j) old[j] = hist[j * C8 + c8];
+  for (int j = 0; j < P; ++j) {
+    const int i = L + j;
+    uint4 v;
+    if (i < P) {
+      v = old[i];
+    } else {
+      v = xs[(int64_t)(i - P) * C8 + c8];
+      if (elu_in) v = elu8(v);
+    }
+    hist[j * C8 + c8] = v;
+  }
+}
+
+// y = bf16(z + bias); mode 1: y = bf16(elu(y)); mode 2: y = bf16(res + y).  Eight elements per thread.
 __global__ void bias_epilogue_kernel(const float* __restrict__ z, const bf16* __restrict__ bias, int64_t M, int N,
                                      int mode, const bf16* __restrict__ res, bf16* __restrict__ y) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * N) return;
-  float v = rbf(z[i] + to_f(bias[i % N]));
-  if (mode == 1) v = rbf(elu(v));
-  if (mode == 2) v = rbf(to_f(res[i]) + v);
-  y[i] = to_bf(v);
+  const int64_t i8 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i8 >= M * N / 8) return;
+  const int n0 = (int)((i8 * 8) % N);
+  const float4 z0 = reinterpret_cast<const float4*>(z)[2 * i8], z1 = reinterpret_cast<const float4*>(z)[2 * i8 + 1];
+  float v[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w}, bv[8], rv[8];
+  unpack8(*reinterpret_cast<const uint4*>(bias + n0), bv);
+  if (mode == 2) unpack8(reinterpret_cast<const uint4*>(res)[i8], rv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] = rbf(v[e] + bv[e]);
+    if (mode == 1) v[e] = elu(v[e]);
+    if (mode == 2) v[e] = rv[e] + v[e];
+  }
+  reinterpret_cast<uint4*>(y)[i8] = pack8(v);
 }
 
-// In place y = bf16(elu(y)).
-__global__ void elu_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int64_t n) {
+// y = bf16(elu(x)), eight elements per thread.
+__global__ void elu_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int64_t n8) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = to_bf(elu(to_f(x[i])));
+  if (i < n8) reinterpret_cast<uint4*>(y)[i] = elu8(reinterpret_cast<const uint4*>(x)[i]);
 }
 
 // Transposed conv fold: Z[b*L + t, j*Co + o] (fp32, j < 2r) are the per-step contributions.  Output step
-// s = t*r + jj gets Z[t, jj] + Z[t-1, jj + r]; conv output = bf16(sum + bias); the first r outputs add the slot's
-// stored tail; the new tail = bf16(bf16(Z[L-1, r + jj] + bias) - bias)   (serve/fast_codec.py:112-126).
+// s = t*r + jj gets Z[t, jj] + Z[t-1, jj + r]; the conv output is bf16(sum + bias) and the first r outputs add the
+// slot's stored tail (serve/fast_codec.py:112-126).  One thread per (row, output step, 8 channels).
 __global__ void convt_fold_kernel(const float* __restrict__ Z, const bf16* __restrict__ bias, int L, int r, int Co,
-                                  const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
+                                  const int* __restrict__ slot32, const bf16* __restrict__ state, int64_t state_row,
                                   int64_t tail_off, bf16* __restrict__ y) {
   const int b = blockIdx.x;
-  const int o = blockIdx.y * blockDim.x + threadIdx.x;
-  if (o >= Co) return;
-  bf16* tail = state + (int64_t)slot32[b] * state_row + tail_off;  // [r, Co]
-  const float bo = to_f(bias[o]);
+  const int C8 = Co / 8;
+  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  if (idx >= L * r * C8) return;
+  const int st = idx / C8, o8 = idx % C8;
+  const int t = st / r, jj = st % r;
   const int64_t zr = (int64_t)2 * r * Co;
   const float* zb = Z + (int64_t)b * L * zr;
-  for (int t = 0; t < L; ++t)
-    for (int jj = 0; jj < r; ++jj) {
-      float v = zb[(int64_t)t * zr + (int64_t)jj * Co + o];
-      if (t > 0) v += zb[(int64_t)(t - 1) * zr + (int64_t)(jj + r) * Co + o];
-      v = rbf(v + bo);
-      if (t == 0) v = rbf(v + to_f(tail[(int64_t)jj * Co + o]));
-      y[((int64_t)b * L * r + (int64_t)t * r + jj) * Co + o] = to_bf(v);
-    }
-  for (int jj = 0; jj < r; ++jj) {
-    const float v = rbf(zb[(int64_t)(L - 1) * zr + (int64_t)(jj + r) * Co + o] + bo);
-    tail[(int64_t)jj * Co + o] = to_bf(v - bo);
+  const float4* a = reinterpret_cast<const float4*>(zb + (int64_t)t * zr + (int64_t)jj * Co + o8 * 8);
+  float4 a0 = a[0], a1 = a[1];
+  float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  if (t > 0) {
+    const float4* p = reinterpret_cast<const float4*>(zb + (int64_t)(t - 1) * zr + (int64_t)(jj + r) * Co + o8 * 8);
+    const float4 p0 = p[0], p1 = p[1];
+    v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+    v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
   }
+  float bv[8];
+  unpack8(*reinterpret_cast<const uint4*>(bias + o8 * 8), bv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = rbf(v[e] + bv[e]);
+  if (t == 0) {
+    float tv[8];
+    unpack8(*reinterpret_cast<const uint4*>(state + (int64_t)slot32[b] * state_row + tail_off +
+                                            (int64_t)jj * Co + o8 * 8), tv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = v[e] + tv[e];
+  }
+  reinterpret_cast<uint4*>(y + ((int64_t)b * L * r + st) * Co)[o8] = pack8(v);
 }
 
-// Final ELU + conv (C -> 1 channel, k taps, history k-1 rows of ELU(x)) -> fp32 PCM.  One CTA per row.
+// New overlap tail = bf16(bf16(Z[L-1, r + jj] + bias) - bias), after the fold has read the old one.
+__global__ void convt_tail_kernel(const float* __restrict__ Z, const bf16* __restrict__ bias, int L, int r, int Co,
+                                  const int* __restrict__ slot32, bf16* __restrict__ state, int64_t state_row,
+                                  int64_t tail_off) {
+  const int b = blockIdx.x;
+  const int C8 = Co / 8;
+  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  if (idx >= r * C8) return;
+  const int jj = idx / C8, o8 = idx % C8;
+  const int64_t zr = (int64_t)2 * r * Co;
+  const float4* a =
+      reinterpret_cast<const float4*>(Z + ((int64_t)b * L + L - 1) * zr + (int64_t)(jj + r) * Co + o8 * 8);
+  const float4 a0 = a[0], a1 = a[1];
+  const float z[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  float bv[8], v[8];
+  unpack8(*reinterpret_cast<const uint4*>(bias + o8 * 8), bv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = rbf(z[e] + bv[e]) - bv[e];
+  reinterpret_cast<uint4*>(state + (int64_t)slot32[b] * state_row + tail_off + (int64_t)jj * Co)[o8] = pack8(v);
+}
+
+// Final ELU + conv (C -> 1 channel, k taps) -> fp32 PCM.  CTA per (row, 128 output steps): the ELU'd input rows the
+// tile needs (history rows for the first tile) are staged in shared memory with a padded row stride.
+constexpr int kFinalTile = 128;
+
 __global__ void final_conv_kernel(const bf16* __restrict__ x, int L, int C, int k, const bf16* __restrict__ w,
                                   const bf16* __restrict__ bias, const int* __restrict__ slot32,
-                                  bf16* __restrict__ state, int64_t state_row, int64_t hist_off,
+                                  const bf16* __restrict__ state, int64_t state_row, int64_t hist_off,
                                   float* __restrict__ pcm) {
-  extern __shared__ float fsm[];  // [(k-1) * C] history, then w [k * C]
-  const int b = blockIdx.x;
-  bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;
-  const int P = k - 1;
-  float* hs = fsm;
-  float* ws = fsm + P * C;
-  for (int i = threadIdx.x; i < P * C; i += blockDim.x) hs[i] = to_f(hist[i]);
+  extern __shared__ float fsm[];
+  const int b = blockIdx.x, t0 = blockIdx.y * kFinalTile;
+  const int P = k - 1, S = C + 1;  // padded stride: conflict-free column reads
+  float* xs = fsm;                 // [(kFinalTile + P) rows, S]
+  float* ws = fsm + (kFinalTile + P) * S;
+  const bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;
+  const int rows = min(kFinalTile, L - t0) + P;
+  for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
+    const int rr = i / C, c = i % C;
+    const int ji = t0 + rr;  // index into joined = [hist; elu(x)]
+    xs[rr * S + c] = ji < P ? to_f(hist[ji * C + c]) : rbf(elu(to_f(x[((int64_t)b * L + ji - P) * C + c])));
+  }
   for (int i = threadIdx.x; i < k * C; i += blockDim.x) ws[i] = to_f(w[i]);
   __syncthreads();
-  const float bo = to_f(bias[0]);
-  for (int t = threadIdx.x; t < L; t += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int i = t + j;  // index into joined
-      for (int c = 0; c < C; ++c) {
-        const float v = i < P ? hs[i * C + c] : rbf(elu(to_f(x[((int64_t)b * L + i - P) * C + c])));
-        acc = fmaf(ws[j * C + c], v, acc);
-      }
-    }
-    pcm[(int64_t)b * L + t] = rbf(acc + bo);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < P * C; i += blockDim.x) {
-    const int row = L - P + i / C;  // last P rows of joined are new rows L-P .. L-1 (L >= P)
-    hist[i] = to_bf(elu(to_f(x[((int64_t)b * L + row) * C + i % C])));
-  }
+  const int t = threadIdx.x;
+  if (t0 + t >= L) return;
+  float acc = 0.f;
+  for (int j = 0; j < k; ++j)
+    for (int c = 0; c < C; ++c) acc = fmaf(ws[j * C + c], xs[(t + j) * S + c], acc);
+  pcm[(int64_t)b * L + t0 + t] = rbf(acc + to_f(bias[0]));
 }
 
 }  // namespace m3
@@ -584,7 +675,7 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
                                                    m->q, kr, kr + kv_half, slot_stride);
     M3_LAUNCHED();
-    ring_attn_kernel<<<dim3(R, c.heads), 128, 0, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32, T,
+    ring_attn_kernel<<<dim3(R, c.heads), kRingThreads, 0, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32, T,
                                                        c.heads, hd, c.ring, c.window, slot_stride,
                                                        1.f / sqrtf((float)hd), m->att);
     M3_LAUNCHED();
@@ -606,13 +697,16 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   M3_LAUNCHED();
   // SEANet: conv0 (k taps, hidden -> C0)
   const int C0 = (1 << c.n_ratios) * c.num_filters;
-  im2col_hist_kernel<<<dim3(R, cdiv(H, 128)), 128, 0, s>>>(m->h, T, H, c.kernel, 0, m->slot32, m->state,
-                                                            m->state_row, m->conv0_off, m->col);
+  im2col_kernel<<<dim3(R, cdiv(T * H / 8, 256)), 256, 0, s>>>(m->h, T, H, c.kernel, 0, m->slot32, m->state,
+                                                                m->state_row, m->conv0_off, m->col);
+  M3_LAUNCHED();
+  conv_hist_kernel<<<dim3(R, cdiv(H / 8, 128)), 128, 0, s>>>(m->h, T, H, c.kernel, 0, m->slot32, m->state,
+                                                              m->state_row, m->conv0_off);
   M3_LAUNCHED();
   M3_TRY(gemm({m->col, (int64_t)c.kernel * H, m->conv0_w, (int64_t)c.kernel * H, m->z, C0, R * T, C0, c.kernel * H,
                true},
               s));
-  int64_t n = (int64_t)R * T * C0;
+  int64_t n = (int64_t)R * T * C0 / 8;
   bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->conv0_b, (int64_t)R * T, C0, 0, nullptr,
                                                                    m->act0);
   M3_LAUNCHED();
@@ -622,40 +716,52 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     const StageDims& sd = m->stages[i];
     const int64_t Min = (int64_t)R * sd.L, Mout = Min * sd.r;
     // ELU -> ConvTranspose1d as X . Wt^T (fp32 contributions) -> fold with the overlap tail
-    elu_kernel<<<(unsigned)((Min * sd.cin + 255) / 256), 256, 0, s>>>(x, m->tmp, Min * sd.cin);
+    elu_kernel<<<(unsigned)((Min * sd.cin / 8 + 255) / 256), 256, 0, s>>>(x, m->tmp, Min * sd.cin / 8);
     M3_LAUNCHED();
     M3_TRY(gemm({m->tmp, sd.cin, m->convt_w[i], sd.cin, m->z, 2 * sd.r * sd.cout, (int)Min, 2 * sd.r * sd.cout, sd.cin,
                  true},
                 s));
-    convt_fold_kernel<<<dim3(R, cdiv(sd.cout, 128)), 128, 0, s>>>(m->z, m->convt_b[i], sd.L, sd.r, sd.cout,
-                                                                   m->slot32, m->state, m->state_row, sd.tail_off,
-                                                                   other);
+    convt_fold_kernel<<<dim3(R, cdiv(sd.L * sd.r * sd.cout / 8, 256)), 256, 0, s>>>(
+        m->z, m->convt_b[i], sd.L, sd.r, sd.cout, m->slot32, m->state, m->state_row, sd.tail_off, other);
+    M3_LAUNCHED();
+    convt_tail_kernel<<<dim3(R, cdiv(sd.r * sd.cout / 8, 128)), 128, 0, s>>>(m->z, m->convt_b[i], sd.L, sd.r, sd.cout,
+                                                                             m->slot32, m->state, m->state_row,
+                                                                             sd.tail_off);
     M3_LAUNCHED();
     std::swap(x, other);  // x = stage output y (residual)
     // resnet: ELU -> conv k3 (history) -> ELU -> conv k1 -> + y
     const int hid = sd.cout / c.compress;
-    im2col_hist_kernel<<<dim3(R, cdiv(sd.cout, 128)), 128, 0, s>>>(x, sd.L * sd.r, sd.cout, c.res_kernel, 1,
-                                                                    m->slot32, m->state, m->state_row, sd.hist_off,
-                                                                    m->col);
+    const int Lo = sd.L * sd.r;
+    im2col_kernel<<<dim3(R, cdiv(Lo * sd.cout / 8, 256)), 256, 0, s>>>(x, Lo, sd.cout, c.res_kernel, 1, m->slot32,
+                                                                       m->state, m->state_row, sd.hist_off, m->col);
+    M3_LAUNCHED();
+    conv_hist_kernel<<<dim3(R, cdiv(sd.cout / 8, 128)), 128, 0, s>>>(x, Lo, sd.cout, c.res_kernel, 1, m->slot32,
+                                                                      m->state, m->state_row, sd.hist_off);
     M3_LAUNCHED();
     M3_TRY(gemm({m->col, (int64_t)c.res_kernel * sd.cout, m->res1_w[i], (int64_t)c.res_kernel * sd.cout, m->z, hid,
                  (int)Mout, hid, c.res_kernel * sd.cout, true},
                 s));
-    n = Mout * hid;
+    n = Mout * hid / 8;
     bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res1_b[i], Mout, hid, 1, nullptr,
                                                                      m->tmp);
     M3_LAUNCHED();
     M3_TRY(gemm({m->tmp, hid, m->res2_w[i], hid, m->z, sd.cout, (int)Mout, sd.cout, hid, true}, s));
-    n = Mout * sd.cout;
+    n = Mout * sd.cout / 8;
     bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res2_b[i], Mout, sd.cout, 2, x, other);
     M3_LAUNCHED();
     std::swap(x, other);
   }
   const StageDims& last = m->stages.back();
   const int Lf = last.L * last.r;
-  const size_t fsmem = (size_t)(2 * c.last_kernel) * c.num_filters * sizeof(float);
-  final_conv_kernel<<<R, 256, fsmem, s>>>(x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32,
-                                          m->state, m->state_row, m->final_off, pcm);
+  const size_t fsmem = ((size_t)(kFinalTile + c.last_kernel - 1) * (c.num_filters + 1) +
+                        (size_t)c.last_kernel * c.num_filters) * sizeof(float);
+  final_conv_kernel<<<dim3(R, cdiv(Lf, kFinalTile)), kFinalTile, fsmem, s>>>(
+      x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32, m->state, m->state_row, m->final_off,
+      pcm);
+  M3_LAUNCHED();
+  conv_hist_kernel<<<dim3(R, cdiv(c.num_filters / 8, 128)), 128, 0, s>>>(x, Lf, c.num_filters, c.last_kernel, 1,
+                                                                          m->slot32, m->state, m->state_row,
+                                                                          m->final_off);
   M3_LAUNCHED();
   return M3_OK;
 }

@@ -1,0 +1,372 @@
+"""TickEngine: the per-tick seat loop of maya3/engine.py (Engine._admit/_bind/_tick/_release) on the native tick.
+
+What the reference's engine thread does per 80 ms frame for all seats -- admit new requests into free slots with an
+inline prefill of their prompt, one backbone step over decode + prefill rows, the cb0 sampler, the depth loop, the
+Mimi frame, one device->host readout and one sync (maya3/engine.py:514-630) -- is here one ``m3_tick_run`` call
+replayed from a CUDA graph per (row bucket, seat bucket, context bucket), plus the host bookkeeping around it.  Text
+normalisation, prompt building, voices and the loop guards stay above this layer (host-side, outside the decode
+step); a request here is a prompt of backbone token ids and a frame budget.
+"""
+from __future__ import annotations
+
+import dataclasses
+import itertools
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .backbone import StaticBackbone
+from .codec import StaticMimi
+from .config import FRAME, Maya3Geom
+from .depth import FastDepth
+from .sampler import Cb0Sampler
+
+BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256)        # maya3/engine.py:44
+ROW_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512, 640,
+               768, 1024)
+CTX = (256, 512, 768, 1024, 1536, 2048, 3072)                                               # maya3/engine.py:191
+REASONS = {1: "aeos", 2: "aeos_argmax", 3: "aeos_tau", 4: "aeos_hazard"}                    # maya3/engine.py:46
+FROM_FEEDBACK = -2   # plan source of a decode row: its seat's feedback vector
+
+
+@dataclasses.dataclass
+class TickConfig:
+    """The EngineConfig fields this layer uses (maya3/engine.py:49-79)."""
+    max_seats: int = 16
+    capacity: int = 2048
+    temp: float = 0.7                 # depth sampler
+    top_k: int = 64
+    cb0_temp: float = 0.9
+    cb0_top_k: int = 64
+    cb0_top_p: float = 1.0
+    cb0_rep: float = 0.8
+    cb0_rep_win: int = 12
+    max_inline_rows: int = 512        # prefill rows folded into one tick
+    max_admit_per_tick: int = 8
+    busy_frac: float = 0.75
+    busy_admit: int = 4
+    seed: int = 20261024
+    stops: bool = True                # False: forced lengths, stop codes are ignored
+    min_frames: int = 4
+    use_graphs: bool = True
+
+
+@dataclasses.dataclass
+class Seat:
+    rid: object
+    prompt: np.ndarray
+    max_frames: int
+    seed: int
+    slot: int = -1
+    frames: int = 0
+    new: bool = True
+    stop: Optional[str] = None
+
+
+@dataclasses.dataclass
+class TickPlan:
+    plan: np.ndarray
+    rows: int
+    seats: int
+    ctx: int
+    dec: list
+    new: list
+    keys: int = 0
+
+
+def _bucket(values, need, what):
+    for b in values:
+        if b >= need:
+            return b
+    raise ValueError(f"{what} {need} exceeds largest bucket {values[-1]}")
+
+
+class _Graph:
+    __slots__ = ("graph", "plan", "packed", "staging", "evt", "launches")
+
+
+class TickEngine:
+    def __init__(self, geom: Maya3Geom, weights: dict, config: TickConfig = None, device=None):
+        self.cfg = cfg = config or TickConfig()
+        self.geom = g = geom
+        self.device = dev = (torch.device(device) if device is not None
+                             else torch.device("cuda", torch.cuda.current_device()))
+        n = cfg.max_seats
+        self.buckets = tuple(b for b in BUCKETS if b < n) + (next((b for b in BUCKETS if b >= n), n),)
+        rows = tuple(b for b in ROW_BUCKETS if b <= self.buckets[-1] + cfg.max_inline_rows)
+        self.row_buckets = rows + tuple(b for b in ROW_BUCKETS if b > rows[-1])[:1]
+        self.max_rows = self.row_buckets[-1]
+        self.ctx_buckets = tuple(c for c in CTX if c < cfg.capacity) + (cfg.capacity,)
+        self.backbone = StaticBackbone(weights, n, capacity=cfg.capacity, batch_buckets=self.row_buckets,
+                                       ctx_buckets=self.ctx_buckets, use_graphs=False, geom=g.backbone, device=dev)
+        self.cb0 = Cb0Sampler(weights["cb0_head.weight"], n, max_rows=self.buckets[-1], temp=cfg.cb0_temp,
+                              top_k=cfg.cb0_top_k, top_p=cfg.cb0_top_p, rep=cfg.cb0_rep, rep_win=cfg.cb0_rep_win,
+                              device=dev)
+        self.depth = FastDepth(weights, n, temp=cfg.temp, top_k=cfg.top_k, batch_buckets=self.buckets,
+                               seed=cfg.seed + 1, geom=g.depth, device=dev)
+        self.codec = StaticMimi(weights, n, batch_buckets=self.buckets, geom=g.mimi, device=dev)
+        D = g.backbone.hidden
+        with torch.inference_mode():
+            self.embed = weights["model.embed_tokens.weight"].detach().to(dev, torch.bfloat16).contiguous()
+            self.feedback = torch.zeros(n + 1, D, device=dev, dtype=torch.bfloat16)
+            # one voice: every seat's speaker constant is FastDepth.set_speaker of the learned null memory
+            self.depth.set_speaker(0, weights["depth.null_mem"].reshape(1, 1, -1), torch.ones(1, 1, dtype=torch.bool))
+            self.voice_const = self.depth.cross_const[0].clone()
+        self.spf = g.mimi.samples_per_frame
+        tc = L.TickConfig(self.backbone._handle, self.cb0._handle, self.depth._handle, self.codec._handle,
+                          self.embed.data_ptr(), self.embed.shape[0], self.feedback.data_ptr(), D, self.max_rows,
+                          self.buckets[-1], g.depth.n_q, self.spf, n)
+        h = L.vp()
+        L.check(L.load().m3_tick_create(tc, h), "m3_tick_create")
+        self._handle = h
+        self.free = list(range(n))[::-1]
+        self.active: list[Seat] = []
+        self.pending: list[Seat] = []
+        self._rng = np.random.default_rng(cfg.seed)
+        self._ids = itertools.count()
+        self.graphs = {}
+        self.pool = None
+        self._host = torch.empty(self.buckets[-1], 2 + self.spf // 4, dtype=torch.int64).pin_memory()
+        self._evt = torch.cuda.Event()
+        self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0}
+
+    def close(self):
+        if getattr(self, "_handle", None):
+            self.graphs.clear()
+            L.load().m3_tick_destroy(self._handle)
+            self._handle = None
+            for c in (self.backbone, self.cb0, self.depth, self.codec):
+                c.close()
+
+    def device_status(self, clear=True) -> int:
+        s = L.i32(0)
+        L.check(L.load().m3_tick_status(self._handle, s, int(clear)), "m3_tick_status")
+        return int(s.value)
+
+    # ---------------------------------------------------------------- requests
+    def submit(self, prompt_ids, max_frames, rid=None, seed=None) -> Seat:
+        """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False)."""
+        prompt = np.asarray(prompt_ids, np.int64)
+        if prompt.ndim != 1 or len(prompt) == 0:
+            raise ValueError("prompt must be a non-empty 1-D array of token ids")
+        if len(prompt) > self.cfg.max_inline_rows:
+            raise ValueError(f"prompt of {len(prompt)} tokens exceeds max_inline_rows {self.cfg.max_inline_rows}")
+        if len(prompt) + int(max_frames) + 2 > self.cfg.capacity:
+            raise ValueError(f"prompt of {len(prompt)} tokens + {max_frames} frames exceeds the KV capacity")
+        seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
+        s = Seat(rid if rid is not None else next(self._ids), prompt, int(max_frames), seed)
+        self.pending.append(s)
+        return s
+
+    def _bind(self, s: Seat):
+        """maya3/engine.py:420-447: claim a slot and reset its per-slot state on the device."""
+        self._claim(s)
+        self.reset_slot(s)
+
+    def _claim(self, s: Seat):
+        s.slot = self.free.pop()
+        self.backbone.lengths_cpu[s.slot] = 0
+
+    @torch.inference_mode()
+    def reset_slot(self, s: Seat):
+        """The device half of binding a seat: sampler, depth, codec and backbone state of its slot (stream-ordered,
+        no host sync)."""
+        slot = s.slot
+        c = self.cb0
+        c.frames_t[slot] = 0
+        c.min_t[slot] = self.cfg.min_frames
+        c.hazard_t[slot] = 0
+        c.aeos_bias[slot] = 0
+        c.seed_t[slot] = s.seed
+        c.ctr_t[slot] = 0
+        c.hist_t[slot] = -1
+        self.depth.row_seed[slot] = (s.seed * 69069 + 1) % (2 ** 31 - 1)
+        self.depth.row_ctr[slot] = 0
+        self.depth.cross_const[slot] = self.voice_const
+        self.codec._reset_row(slot)
+        self.backbone.lengths[slot] = 0
+
+    def _release(self, s: Seat):
+        """maya3/engine.py:632-635."""
+        self.backbone.free(s.slot)
+        self.free.append(s.slot)
+
+    def _admit(self, device=True):
+        """maya3/engine.py:449-510 without prompt building: pending requests enter free slots while the tick's row
+        budget allows their inline prefill.  device=False only claims the slots (the caller resets them later, in
+        stream order, with reset_slot)."""
+        new, rows = [], len(self.active)
+        cap = self.cfg.max_admit_per_tick
+        if len(self.active) > self.cfg.busy_frac * self.cfg.max_seats:
+            cap = min(cap, self.cfg.busy_admit)
+        while self.pending and self.free and len(new) < cap:
+            s = self.pending[0]
+            if rows + len(s.prompt) > self.max_rows:
+                break
+            self.pending.pop(0)
+            self._bind(s) if device else self._claim(s)
+            new.append(s)
+            rows += len(s.prompt)
+            self.stats["admitted"] += 1
+        return new
+
+    # ---------------------------------------------------------------- plan
+    def make_plan(self, dec: list, new: list) -> TickPlan:
+        """Host plan of one tick (layout of m3_tick_run): rows = decode rows then each new seat's prompt rows."""
+        dummy = self.cfg.max_seats
+        n_rows = len(dec) + sum(len(s.prompt) for s in new)
+        seats = dec + new
+        rb = _bucket(self.row_buckets, max(n_rows, 1), "rows")
+        sb = _bucket(self.buckets, max(len(seats), 1), "seats")
+        lc = self.backbone.lengths_cpu
+        need = max([lc[s.slot] + 1 for s in dec] + [lc[s.slot] + len(s.prompt) for s in new] + [1])
+        cb = _bucket(self.ctx_buckets, need, "context")
+        # keys attended per layer by this step's rows (decode rows: length + 1; prefill row at offset o: o + 1;
+        # padding rows: 1), the algorithmic KV traffic of one attention launch
+        keys = (sum(lc[s.slot] + 1 for s in dec) + sum(len(s.prompt) * (len(s.prompt) + 1) // 2 for s in new)
+                + (rb - n_rows))
+        p = np.zeros(4 * rb + 2 * sb, np.int64)
+        r_slot, r_off, r_real, r_src = p[:rb], p[rb:2 * rb], p[2 * rb:3 * rb], p[3 * rb:4 * rb]
+        s_slot, s_row = p[4 * rb:4 * rb + sb], p[4 * rb + sb:]
+        r_slot[:] = dummy
+        r_src[:] = -1
+        s_slot[:] = dummy
+        nd = len(dec)
+        if nd:
+            r_slot[:nd] = [s.slot for s in dec]
+            r_real[:nd] = 1
+            r_src[:nd] = FROM_FEEDBACK
+            s_slot[:nd] = r_slot[:nd]
+            s_row[:nd] = np.arange(nd)
+        at = nd
+        for j, s in enumerate(new):
+            P = len(s.prompt)
+            r_slot[at:at + P] = s.slot
+            r_off[at:at + P] = np.arange(P)
+            r_real[at:at + P] = 1
+            r_src[at:at + P] = s.prompt
+            at += P
+            s_slot[nd + j] = s.slot
+            s_row[nd + j] = at - 1
+        return TickPlan(p, rb, sb, cb, list(dec), list(new), keys)
+
+    def commit(self, tp: TickPlan):
+        """Host mirror of what the tick did to the slots' lengths."""
+        lc = self.backbone.lengths_cpu
+        for s in tp.dec:
+            lc[s.slot] += 1
+        for s in tp.new:
+            lc[s.slot] += len(s.prompt)
+            self.stats["prefill_rows"] += len(s.prompt)
+
+    # ---------------------------------------------------------------- graphs
+    def graph_for(self, rb, sb, cb) -> _Graph:
+        key = (rb, sb, cb)
+        g = self.graphs.get(key)
+        if g is not None:
+            return g
+        g = _Graph()
+        n = 4 * rb + 2 * sb
+        dummy = self.cfg.max_seats
+        with torch.inference_mode():
+            idle = np.zeros(n, np.int64)
+            idle[:rb] = dummy
+            idle[3 * rb:4 * rb] = -1
+            idle[4 * rb:4 * rb + sb] = dummy
+            g.plan = torch.from_numpy(idle).to(self.device)
+            g.packed = torch.zeros(sb, 2 + self.spf // 4, dtype=torch.long, device=self.device)
+        g.staging = torch.zeros(n, dtype=torch.long).pin_memory()
+        g.evt = None
+        g.graph = None
+        if self.cfg.use_graphs:
+            stream = torch.cuda.Stream()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):     # an all-padding plan touches only the dummy slot
+                for _ in range(2):
+                    self._launch(g, rb, sb, cb, stream)
+            torch.cuda.current_stream().wait_stream(stream)
+            if self.pool is None:
+                self.pool = torch.cuda.graph_pool_handle()
+            g.graph = torch.cuda.CUDAGraph()
+            before = L.load().m3_launch_count()
+            with torch.cuda.graph(g.graph, pool=self.pool):
+                self._launch(g, rb, sb, cb)
+            g.launches = L.load().m3_launch_count() - before   # this library's kernels in one replay
+        else:
+            g.launches = None
+        self.graphs[key] = g
+        return g
+
+    def _launch(self, g, rb, sb, cb, stream=None):
+        rep, top_p = self.cb0.flags()
+        L.check(L.load().m3_tick_run(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p, g.packed.data_ptr(),
+                                     L.stream_ptr(stream)), "m3_tick_run")
+
+    def replay(self, g, rb, sb, cb):
+        if g.graph is not None:
+            g.graph.replay()
+        else:
+            self._launch(g, rb, sb, cb)
+
+    # ---------------------------------------------------------------- tick
+    @torch.inference_mode()
+    def tick(self):
+        """One engine tick through the public path: admit, copy the plan host->device, replay, read the packed
+        (stop code, cb0, PCM) rows back with one device->host copy and one sync (maya3/engine.py:557-563).
+        Returns [(seat, stop code, cb0, int16 PCM or None)] for the seats that ran."""
+        new = self._admit()
+        dec = list(self.active)
+        if not dec and not new:
+            return []
+        tp = self.make_plan(dec, new)
+        g = self.graph_for(tp.rows, tp.seats, tp.ctx)
+        if g.evt is not None:
+            g.evt.synchronize()     # the pinned staging row may still feed the previous copy
+        g.staging.numpy()[:] = tp.plan
+        g.plan.copy_(g.staging, non_blocking=True)
+        g.evt = torch.cuda.Event()
+        g.evt.record()
+        self.replay(g, tp.rows, tp.seats, tp.ctx)
+        B = len(dec) + len(new)
+        host = self._host[:B]
+        host.copy_(g.packed[:B], non_blocking=True)
+        self._evt.record()
+        self._evt.synchronize()
+        self.commit(tp)
+        return self._deliver(dec + new, host.numpy())
+
+    def deliver_forced(self, seats):
+        """Host bookkeeping of a tick whose readout is not read (stops disabled): every seat got one frame."""
+        return self._deliver(seats, None)
+
+    def _deliver(self, seats, hv):
+        out, finished = [], []
+        for i, s in enumerate(seats):
+            code = int(hv[i, 0]) if hv is not None else 0
+            s.new = False
+            if self.cfg.stops and code:
+                s.stop = REASONS.get(code, str(code))
+                finished.append(s)
+                out.append((s, code, int(hv[i, 1]), None))
+                continue
+            s.frames += 1
+            self.stats["frames"] += 1
+            if hv is not None:
+                out.append((s, code, int(hv[i, 1]), hv[i, 2:].view(np.int16)))
+            if s.frames >= s.max_frames:
+                s.stop = "max_frames"
+                finished.append(s)
+        self.active = list(seats)
+        if finished:
+            gone = {id(s) for s in finished}
+            for s in finished:
+                self._release(s)
+                self.stats["completed"] += 1
+            self.active = [s for s in self.active if id(s) not in gone]
+        self.stats["ticks"] += 1
+        return out
+
+
+__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "FRAME", "FROM_FEEDBACK"]

@@ -56,14 +56,17 @@ def _fan_in(shape: tuple) -> int:
     return 1
 
 
-def make(name: str, shape, seed: int = 0) -> torch.Tensor:
-    """The fp32 CPU tensor for ``name`` at ``shape`` (deterministic across machines for a fixed torch build)."""
+def make(name: str, shape, seed: int = 0, device=None) -> torch.Tensor:
+    """The fp32 tensor for ``name`` at ``shape``: deterministic on CPU (the default, shared with the oracle) for a
+    fixed torch build; ``device='cuda'`` draws the same distribution from the device generator (fast, for timing
+    runs that need no oracle)."""
     shape = tuple(int(s) for s in shape)
     kind = _kind(name, shape)
+    dev = torch.device(device) if device is not None else torch.device("cpu")
     if kind == "ones":
-        return torch.ones(shape)
-    g = torch.Generator().manual_seed((int(seed) * 1000003 + zlib.crc32(name.encode())) % (1 << 62))
-    r = torch.randn(shape, generator=g)
+        return torch.ones(shape, device=dev)
+    g = torch.Generator(device=dev).manual_seed((int(seed) * 1000003 + zlib.crc32(name.encode())) % (1 << 62))
+    r = torch.randn(shape, generator=g, device=dev)
     if kind == "randn":
         return r
     if kind == "table":
@@ -173,8 +176,16 @@ def mimi_shapes(g: MimiGeom) -> dict:
     return s
 
 
-def generate(shapes: dict, seed: int = 0) -> dict:
-    return {name: make(name, shape, seed) for name, shape in shapes.items()}
+def generate(shapes: dict, seed: int = 0, device=None) -> dict:
+    return {name: make(name, shape, seed, device) for name, shape in shapes.items()}
+
+
+def all_shapes(geom) -> dict:
+    """Every tensor the decode tick reads, for a Maya3Geom."""
+    s = backbone_shapes(geom.backbone)
+    s.update(depth_shapes(geom.depth))
+    s.update(mimi_shapes(geom.mimi))
+    return s
 
 
 def backbone_weights(g: BackboneGeom, seed: int = 0) -> dict:

@@ -37,7 +37,7 @@ class BackboneOracle:
         self.rnd = Prec(dtype)
         self.max_slots, self.capacity, self.dummy = max_slots, capacity, max_slots
         W = {k: self.rnd(f32(v)) for k, v in weights.items() if not k.startswith("model.embed_tokens")}
-        self.embed = weights["model.embed_tokens.weight"]
+        self.embed = weights.get("model.embed_tokens.weight")
         self.layers = []
         for i in range(g.layers):
             p = f"model.layers.{i}."

@@ -4,6 +4,8 @@ own fixtures and the CPU oracle.
 Tolerances: bf16 hidden states are compared by max-abs error relative to the tensor's scale, 2e-2 (the bf16 logit
 tolerance of the parity contract); bit-exact agreement is not expected because GEMM accumulation order differs.
 """
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -80,9 +82,10 @@ def test_baseline_geometry_long_staggered_contexts(cuda, big):
     last stage), decode steps and a mixed step with an inline prefill.
 
     On this random-init stack the reference's own bf16 arithmetic is chaotic: it sits ~5% (relative L2) from the
-    same computation in fp32.  So, as the reference's test_backbone_fused.py does, the bar is set against that noise
-    floor: the CUDA path must be within 2e-2 relative L2 of the bf16 oracle and no further from fp32 than the bf16
-    oracle itself is (x1.25)."""
+    same computation in fp32, so two bf16 implementations that differ only in accumulation order drift apart by a
+    similar amount.  As the reference's test_backbone_fused.py does, the bar is set against that noise floor: the
+    CUDA path must be closer to the bf16 oracle than the bf16 oracle is to fp32, and no further from fp32 than the
+    bf16 oracle itself is (x1.25).  test_one_layer_long_context pins the same kernels tightly without the chaos."""
     g, W = big
     cap = 2048
     sb = StaticBackbone(W, 6, capacity=cap, ctx_buckets=(512, 2048), batch_buckets=(1, 8, 64), geom=g)
@@ -97,8 +100,9 @@ def test_baseline_geometry_long_staggered_contexts(cuda, big):
     slots = [0, 1, 2, 3, 4]
 
     def check(y, r16, r32):
-        assert rel_l2(y, r16) < TOL
-        assert rel_l2(y, r32) < 1.25 * rel_l2(r16, r32) + 1e-3
+        floor = rel_l2(r16, r32)
+        assert rel_l2(y, r16) < max(floor, TOL)
+        assert rel_l2(y, r32) < 1.25 * floor + 1e-3
     for step in range(3):
         x = rng.standard_normal((len(slots), g.hidden)).astype(np.float32)
         y = sb.step(slots, t(x, cuda)).float().cpu().numpy()
@@ -115,6 +119,31 @@ def test_baseline_geometry_long_staggered_contexts(cuda, big):
     assert rel_l2(sb.k[0][5, :, :23].float().cpu().numpy(), orc.k[0][5, :, :23]) < 5e-3
     assert rel_l2(sb.v[0][5, :, :23].float().cpu().numpy(), orc.v[0][5, :, :23]) < 5e-3
     check(sb.k[27][5, :, :23].float().cpu().numpy(), orc.k[27][5, :, :23], o32.k[27][5, :, :23])
+    assert sb.device_status() == 0
+
+
+def test_one_layer_long_context(cuda):
+    """Full-width single layer, so bf16 chaos cannot build up: seats from 1 to 2047 keys (up to 16 KV splits, ragged
+    last stage, the capacity edge) and a 64-row inline prefill must match the bf16 oracle to 2e-2 max-abs."""
+    g = dataclasses.replace(BASELINE.backbone, layers=1)
+    W = WG.generate({k: v for k, v in WG.backbone_shapes(g).items() if "embed_tokens" not in k})
+    cap = 2048
+    sb = StaticBackbone(W, 8, capacity=cap, ctx_buckets=(2048,), batch_buckets=(8, 128), geom=g)
+    orc = BackboneOracle({k: v.numpy() for k, v in W.items()}, g, 8, cap, "bf16")
+    lengths = {0: 1, 1: 31, 2: 32, 3: 33, 4: 255, 5: 1000, 6: 2046}
+    for s, n in lengths.items():
+        _fill_random_kv(sb, orc, s, n, seed=100 + s)
+    rng = np.random.default_rng(1)
+    slots = list(lengths)
+    for step in range(2):
+        x = rng.standard_normal((len(slots), g.hidden)).astype(np.float32)
+        y = sb.step(slots, t(x, cuda)).float().cpu().numpy()
+        assert rel_maxabs(y, orc.step(slots, x)) < TOL, step
+    pre = rng.standard_normal((64, g.hidden)).astype(np.float32)
+    dec, last = sb.step_mixed(slots[:3], t(pre[:3], cuda), [(7, t(pre, cuda))])
+    rdec, rlast = orc.step_mixed(slots[:3], pre[:3], [(7, pre)])
+    assert rel_maxabs(dec.float().cpu(), rdec) < TOL
+    assert rel_maxabs(last[0].float().cpu(), rlast[0]) < TOL
     assert sb.device_status() == 0
 
 
