@@ -148,6 +148,18 @@ M3_API int m3_cb0_destroy(m3_cb0* s);
  * (`cb0_rep_win > 0 and (cb0_rep > 0 or any_rep)`, `_any_top_p`). */
 M3_API int m3_cb0_step(m3_cb0* s, const void* h, const int64_t* idx, int64_t* code, int64_t* cb0, int32_t rows,
                 int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
+/* m3_cb0_step without a handle and without allocating, for callers that must not allocate device memory while
+ * they sample: a host that gave this library a fixed device budget up front and forbids any later cudaMalloc, or a
+ * latency-critical serving thread on which cudaMalloc / cudaFree would synchronise the device and stall every seat.
+ * This entry point has no counterpart in the reference (which samples with eager torch ops that allocate freely).
+ * Same arguments and results as m3_cb0_step, with the configuration and per-slot state passed directly; limits:
+ * rows <= 8 per call, n_cls <= 4096, hidden <= 3072 (a multiple of 8); larger calls are rejected with M3_ERR_ARG.
+ * Scratch: a 64 KiB static device array inside the library, held by every GPU that loads it until the process
+ * exits.  The first call on a device looks up that array's device address, so make it before any stream capture.
+ * Every call shares the one array: calls that overlap on the GPU (different streams without ordering) race. */
+M3_API int m3_cb0_step_noalloc(const m3_cb0_config* cfg, const m3_cb0_state* st, const void* h, const int64_t* idx,
+                               int64_t* code, int64_t* cb0, int32_t rows, int32_t apply_rep, int32_t apply_top_p,
+                               m3_stream stream);
 /* The sampler alone on given fp32 logits [rows, n_cls] (the cb0 head output as fp32). */
 M3_API int m3_cb0_sample_logits(m3_cb0* s, const float* logits, const int64_t* idx, int64_t* code, int64_t* cb0,
                          int32_t rows, int32_t apply_rep, int32_t apply_top_p, m3_stream stream);

@@ -171,3 +171,19 @@ extern "C" int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t l
                  m, n, k, y_f32 != 0};
   return m3::gemm(g, reinterpret_cast<cudaStream_t>(stream));
 }
+
+namespace m3 {
+// The GEMV kernel alone (M <= 8), never a library call: for paths that must not allocate (cuBLAS creates its handle
+// and workspace lazily).  Returns M3_ERR_UNSUPPORTED when the shape or alignment does not fit the GEMV kernel.
+int gemv_only(const GemmDesc& g, cudaStream_t s) {
+  const bool ok = g.M >= 0 && g.M <= 8 && g.N > 0 && g.K > 0 && g.K % 8 == 0 && g.ldx % 8 == 0 && g.ldw % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(g.X) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.W) & 15) == 0 &&
+                  (size_t)8 * g.K * 2 <= 48 * 1024;
+  M3_REQUIRE(ok, M3_ERR_UNSUPPORTED, "gemv_only: M=%d N=%d K=%d outside the GEMV kernel's range", g.M, g.N, g.K);
+  if (g.M == 0) return M3_OK;
+  if (g.M <= 1) return launch_gemv<1>(g, s);
+  if (g.M <= 2) return launch_gemv<2>(g, s);
+  if (g.M <= 4) return launch_gemv<4>(g, s);
+  return launch_gemv<8>(g, s);
+}
+}  // namespace m3

@@ -16,5 +16,7 @@ struct GemmDesc {
 };
 
 int gemm(const GemmDesc& g, cudaStream_t s);
+// GEMV kernel only (M <= 8, K <= 3072); never calls a library that may allocate.
+int gemv_only(const GemmDesc& g, cudaStream_t s);
 
 }  // namespace m3

@@ -3,6 +3,7 @@
 // serve/fast_depth_kernels.py:339-355).  One CTA per row; the top-k threshold is found by a bitwise search over
 // order-preserving integer keys (exact k-th largest, no sort); noise is counter-based Philox, bit-identical to the
 // reference's tl.rand stream for the same (seed, counter, level, code).
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -481,4 +482,72 @@ extern "C" int m3_topk_sample(const void* logits, int32_t logits_bf16, int32_t r
   M3_REQUIRE(logits && codes && (greedy || (seed && ctr)), M3_ERR_ARG, "m3_topk_sample: null argument");
   return launch_topk_sample(logits, logits_bf16 != 0, n, rows, n, seed, ctr, nullptr, level, inv_temp, top_k, greedy,
                             codes, 1, nullptr, 0, nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ================================================================================================ allocation-free cb0 step
+// Some callers cannot allocate device memory when they sample: a host that hands this library a fixed device
+// budget up front and forbids any later cudaMalloc (every byte of a B200 already mapped to KV caches and weights),
+// or a caller on a latency-critical serving thread where cudaMalloc/cudaFree would synchronise the device and stall
+// every seat's frame.  For them m3_cb0_step_noalloc runs the same cb0 head + sampler as m3_cb0_step without a handle:
+// its only scratch (the bf16 logits and a status word) lives in this file-scope device array, which every GPU that
+// loads the library holds until the process exits.
+constexpr int kNoAllocRows = 8;      // rows per call (the head GEMM runs on the GEMV kernel, which serves M <= 8)
+constexpr int kNoAllocCls = 4096;    // classes per row
+constexpr size_t kNoAllocLogitsBytes = (size_t)kNoAllocRows * kNoAllocCls * sizeof(bf16);   // 64 KiB
+constexpr size_t kNoAllocScratchBytes = kNoAllocLogitsBytes + 256;                             // + status word
+static __device__ __align__(256) unsigned char g_cb0_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+std::vector<void*> g_noalloc_ptr;  // device address of the scratch array, per device ordinal
+
+// Host code cannot use the array's name as a device address: look the address up once per device, with that
+// device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  M3_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if ((int)g_noalloc_ptr.size() <= dev) g_noalloc_ptr.resize(dev + 1, nullptr);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_cb0_noalloc_scratch);
+    if (e != cudaSuccess) {
+      set_error("m3_cb0_step_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+      return M3_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return M3_OK;
+}
+}  // namespace
+
+extern "C" int m3_cb0_step_noalloc(const m3_cb0_config* cfg, const m3_cb0_state* st, const void* h,
+                                   const int64_t* idx, int64_t* code, int64_t* cb0, int32_t rows, int32_t apply_rep,
+                                   int32_t apply_top_p, m3_stream stream) {
+  M3_REQUIRE(cfg && st && st->head && h && idx && code && cb0, M3_ERR_ARG, "m3_cb0_step_noalloc: null argument");
+  M3_REQUIRE(rows >= 0 && rows <= kNoAllocRows, M3_ERR_ARG,
+             "m3_cb0_step_noalloc: %d rows exceed the allocation-free limit of %d rows per call", rows, kNoAllocRows);
+  M3_REQUIRE(cfg->n_cls > 0 && cfg->n_cls <= kNoAllocCls, M3_ERR_ARG,
+             "m3_cb0_step_noalloc: %d classes exceed the allocation-free limit of %d", cfg->n_cls, kNoAllocCls);
+  M3_REQUIRE(cfg->hidden > 0 && cfg->hidden % 8 == 0 && cfg->hidden <= 3072, M3_ERR_ARG,
+             "m3_cb0_step_noalloc: hidden %d must be a multiple of 8 and at most 3072", cfg->hidden);
+  M3_REQUIRE(cfg->rep_win >= 0 && cfg->rep_win <= kSampThreads, M3_ERR_ARG,
+             "m3_cb0_step_noalloc: rep_win %d exceeds %d", cfg->rep_win, kSampThreads);
+  void* scratch = nullptr;
+  M3_TRY(noalloc_scratch(&scratch));
+  if (rows == 0) return M3_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  bf16* logits = reinterpret_cast<bf16*>(scratch);
+  int* status = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + kNoAllocLogitsBytes);
+  M3_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));  // the array keeps the previous call's status word
+  M3_TRY(gemv_only({(const bf16*)h, cfg->hidden, (const bf16*)st->head, cfg->hidden, logits, cfg->n_cls, rows,
+                    cfg->n_cls, cfg->hidden, false},
+                   s));
+  const Cb0Dev dev{st->frames, st->min_frames, st->hazard, st->aeos_bias, st->temp, st->top_k, st->top_p, st->rep,
+                   st->seed, st->ctr, st->hist, cfg->rep_win, cfg->max_slots};
+  cb0_sample_kernel<bf16><<<rows, kSampThreads, 0, s>>>(logits, cfg->n_cls, cfg->n_cls, idx, dev, apply_rep,
+                                                         apply_top_p, code, cb0, status);
+  M3_LAUNCHED();
+  return M3_OK;
 }
