@@ -64,6 +64,11 @@ M3_API int64_t m3_launch_count(void);
 M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
                  int32_t n, int32_t k, int32_t y_f32, m3_stream stream);
 
+/* m3_gemm_bf16 on a chosen implementation: 0 = automatic (what every stage uses), 1 = the GEMV kernel (m <= 8),
+ * 2 = cuBLAS, 3 = this library's tcgen05 tensor-core kernel.  For tests and measurement. */
+M3_API int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
+                             int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream);
+
 /* ---------------------------------------------------------------------------------------------- backbone */
 /* Replaces StaticBackbone (serve/fast_backbone.py:111-362): the static-KV Qwen3 decode with per-seat positions. */
 typedef struct m3_backbone m3_backbone;

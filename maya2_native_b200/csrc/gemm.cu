@@ -187,3 +187,21 @@ int gemv_only(const GemmDesc& g, cudaStream_t s) {
   return launch_gemv<8>(g, s);
 }
 }  // namespace m3
+
+namespace m3 {
+int gemm_impl(const GemmDesc& g, int impl, cudaStream_t s) {
+  switch (impl) {
+    case kGemmGemv: return gemv_only(g, s);
+    case kGemmCublas: return g.M == 0 ? M3_OK : launch_cublas(g, s);
+    case kGemmUmma: return g.M == 0 ? M3_OK : umma_gemm(g, g.N >= 4096 ? 128 : 64, 1, false, s);
+    default: return gemm(g, s);
+  }
+}
+}  // namespace m3
+
+extern "C" int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                                 int32_t m, int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream) {
+  m3::GemmDesc g{reinterpret_cast<const m3::bf16*>(x), ldx, reinterpret_cast<const m3::bf16*>(w), ldw, y, ldy,
+                 m, n, k, y_f32 != 0};
+  return m3::gemm_impl(g, impl, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -18,5 +18,11 @@ struct GemmDesc {
 int gemm(const GemmDesc& g, cudaStream_t s);
 // GEMV kernel only (M <= 8, K <= 3072); never calls a library that may allocate.
 int gemv_only(const GemmDesc& g, cudaStream_t s);
+// Tensor-core GEMM (tcgen05, umma.cu): 128 x bn tiles (bn in {64, 128, 256}); partial = fp32 split-K partials
+// [splitk][M][ldy] at Y.
+int umma_gemm(const GemmDesc& g, int bn, int splitk, bool partial, cudaStream_t s);
+// The implementations behind gemm(), selectable for tests and measurement.
+enum GemmImpl { kGemmAuto = 0, kGemmGemv = 1, kGemmCublas = 2, kGemmUmma = 3 };
+int gemm_impl(const GemmDesc& g, int impl, cudaStream_t s);
 
 }  // namespace m3

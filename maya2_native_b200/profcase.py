@@ -67,14 +67,63 @@ def tick(a):
     print(f"tick case: {a.seats} seats, {a.steps} ticks")
 
 
+# (label, M, N, K) of the linear layers of one configs[2] tick
+TICK_GEMMS = [("bb.qkv", 256, 4096, 1024), ("bb.o", 256, 1024, 2048), ("bb.gu", 256, 6144, 1024),
+              ("bb.down", 256, 1024, 3072), ("bb.qkv+pf", 768, 4096, 1024), ("depth.qkv n8", 2048, 3072, 1024),
+              ("depth.o n8", 2048, 1024, 1024), ("depth.f1 n8", 2048, 3072, 1024), ("depth.f2 n8", 2048, 1024, 3072),
+              ("depth.qkv n2", 512, 3072, 1024), ("depth.f2 last", 256, 1024, 3072), ("depth.head", 256, 2048, 1024),
+              ("mimi.qkv", 512, 1536, 512), ("mimi.fc1", 512, 2048, 512), ("mimi.fc2", 512, 512, 2048),
+              ("mimi.conv0", 512, 1024, 3584), ("mimi.convt8", 512, 8192, 1024), ("mimi.res8", 4096, 256, 1536),
+              ("mimi.convt6", 4096, 3072, 512), ("mimi.res6", 24576, 128, 768), ("mimi.convt5", 24576, 1280, 256),
+              ("mimi.res5", 122880, 64, 384), ("mimi.convt4", 122880, 512, 128), ("mimi.res4", 491520, 32, 192),
+              ("mimi.res4k1", 491520, 64, 32)]
+
+
+@torch.inference_mode()
+def gemm(a):
+    """Time each implementation of m3_gemm_bf16 on the tick's linear-layer shapes (CUDA events, 50 launches)."""
+    from . import _lib as L
+    dev = torch.device("cuda", 0)
+    lib = L.load()
+    print(f"{'layer':16s} {'M':>7s} {'N':>5s} {'K':>5s}   cublas us  tcgen05 us   TF/s(tc)")
+    for name, M, N, K in TICK_GEMMS:
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        w = torch.randn(N, K, device=dev).to(torch.bfloat16)
+        y = torch.empty(M, N, device=dev, dtype=torch.float32)
+        res = []
+        for impl in (2, 3):
+            def call():
+                L.check(lib.m3_gemm_bf16_impl(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K, 1, impl,
+                                              L.stream_ptr()))
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    call()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):      # launches replayed without host overhead, as in the tick graph
+                for _ in range(20):
+                    call()
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            res.append(e0.elapsed_time(e1) / 100 * 1e3)
+        print(f"{name:16s} {M:7d} {N:5d} {K:5d}   {res[0]:9.2f}  {res[1]:10.2f}   {2 * M * N * K / res[1] / 1e6:8.1f}")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("attention", "tick"))
+    ap.add_argument("case", choices=("attention", "tick", "gemm"))
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
     a = ap.parse_args()
-    {"attention": attention, "tick": tick}[a.case](a)
+    {"attention": attention, "tick": tick, "gemm": gemm}[a.case](a)
 
 
 if __name__ == "__main__":
