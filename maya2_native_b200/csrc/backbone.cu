@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tma.cuh"
 #include "gemm.cuh"
 
 namespace m3 {
@@ -159,223 +160,298 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
 // Split-KV decode attention over the static cache (replaces _decode_attn, serve/fast_backbone.py:32-58).
 //
 // Grid (split, kv head, row).  A CTA owns keys [split*chunk, min((split+1)*chunk, pos+1)) of one (row, kv head)
-// and serves all G query heads of that kv head, so every K/V byte is read from HBM once.  K and V rows of one
-// (slot, head) are contiguous (256 B per token), so each 32-token stage is two 8 KB bulk copies into shared memory,
-// kStages deep.  Compute: 4 lanes per token (lane owns 16-byte chunks p, p+4, p+8, p+12 of the head dim), fp32
-// dot products, online softmax in the exp2 domain with a warp-uniform running max that is only raised when a new
-// score exceeds it by more than 2^8 (the result is exact: the same reference max is used for every term).
-constexpr int kStageTok = 32;
-constexpr int kStages = 4;
+// and serves all G query heads of that kv head, so every K/V byte is read from HBM once.  Online softmax in the
+// exp2 domain with a running max that is only raised when a new score exceeds it by more than 2^8 (the result is
+// exact: the same reference max is used for every term of a split).  Splits are merged in the same launch: a row
+// whose keys fit one split writes its bf16 output directly; otherwise each CTA publishes (O, m, l) in fp32, and the
+// last CTA of the (row, kv head) to take an atomic ticket merges them and re-arms the ticket.
 constexpr int kAttnThreads = 128;
-constexpr int kTokBytes = kHeadDim * 2;
 constexpr float kLazyRescale = 8.f;
 
+// Final step of a split CTA, thread tid owning head dim tid of the G query heads: (Og, Mg, Lg) is the CTA's
+// unnormalised output, running max (exp2 domain) and softmax denominator.  A row whose keys fit one split (n == 1)
+// writes bf16(O / L) directly.  Otherwise the CTA publishes its fp32 partial, takes a ticket on its (row, kv head),
+// and the last of the n CTAs merges all of them, out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M) with
+// M = max_s m_s, and re-arms the ticket for the next launch on the stream.
 template <int G>
-struct AttnSmem {
-  bf16 k[kStages][kStageTok * kHeadDim];
-  bf16 v[kStages][kStageTok * kHeadDim];
-  uint64_t bar[kStages];
+__device__ __forceinline__ void split_epilogue(const float (&Og)[G], const float (&Mg)[G], const float (&Lg)[G],
+                                               int tid, int row, int kvh, int KV, int split, int nsplit, int n,
+                                               float* __restrict__ part_o, float2* __restrict__ part_ml,
+                                               int* __restrict__ tickets, bf16* __restrict__ out, int H, int* last) {
+  bf16* orow = out + ((int64_t)row * H + kvh * G) * kHeadDim;
+  if (n == 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) orow[g * kHeadDim + tid] = to_bf(Lg[g] > 0.f ? Og[g] / Lg[g] : 0.f);
+    return;
+  }
+  const int64_t rk = (int64_t)row * KV + kvh;
+  const int64_t pidx = rk * nsplit + split;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    part_o[(pidx * G + g) * kHeadDim + tid] = Og[g];
+    if (tid == 0) part_ml[pidx * G + g] = make_float2(Mg[g], Lg[g]);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();  // release: the whole CTA's partial (ordered before this thread by the barrier)
+    const int prev = atomicAdd(&tickets[rk], 1);
+    __threadfence();  // acquire: the other CTAs' partials, for the merge below
+    *last = prev == n - 1;
+  }
+  __syncthreads();
+  if (!*last) return;
+  const int64_t pbase = rk * nsplit;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+    for (int s = 0; s < n; ++s) M = fmaxf(M, __ldcg(&part_ml[(pbase + s) * G + g]).x);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < n; ++s) {
+        const float2 ml = __ldcg(&part_ml[(pbase + s) * G + g]);
+        const float sc = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+        O = fmaf(__ldcg(&part_o[((pbase + s) * G + g) * kHeadDim + tid]), sc, O);
+        L = fmaf(ml.y, sc, L);
+      }
+    orow[g * kHeadDim + tid] = to_bf(L > 0.f ? O / L : 0.f);
+  }
+  if (tid == 0) tickets[rk] = 0;
+}
+
+// The dot products run on the tensor cores (mma.sync m16n8k16, bf16 operands, fp32 accumulation; the operands are
+// exact bf16 values, so only the summation order differs from fp32 FMAs: the reference's kernel is scalar fp32).
+// K and V arrive by TMA through per-layer tensor maps over the cache [slot * kv_heads + head][position][128]: a
+// 16-token block is four 2 KB boxes (K and V, dims 0-63 and 64-127), 128-byte swizzled so that ldmatrix reads them
+// without bank conflicts.  Each of the 4 warps owns every 4th block of the CTA's chunk and its own kMmaStages-deep
+// ring (no CTA-wide barrier in the loop).  Per block:
+//   S   = Q K^T       A = Q (16 rows, the G query heads, rest zero), B = K rows via ldmatrix      (16 mma)
+//   P   = 2^(S*scale - m) with the warp's lazily raised running max m, masked past the row's length
+//   O^T += V^T P^T    A = V^T via ldmatrix.trans, B = P^T straight from the S accumulators, P split into bf16
+//                     hi + lo parts so that the weights keep ~16 mantissa bits (the reference keeps them in fp32)
+// V rows past the row's last key are zeroed in shared memory before use (0 * stale data must stay 0).
+constexpr int kBlkTok = 16;
+constexpr int kMmaStages = 2;
+constexpr int kBoxBytes = kBlkTok * 128;   // 16 positions x 64 dims x bf16
+constexpr int kBlkBytes = 4 * kBoxBytes;   // K lo, K hi, V lo, V hi
+
+struct MmaAttnSmem {
+  unsigned char stage[4][kMmaStages][kBlkBytes];  // [warp][stage], every box 1024-byte aligned
+  uint64_t bar[4][kMmaStages];
+  int last;
 };
+constexpr int kMmaAttnSmemBytes = (int)sizeof(MmaAttnSmem) + 1024;  // + alignment slack
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A B, m16n8k16, A row-major bf16 {a0..a3}, B column-major bf16 {b0, b1}, fp32 accumulators
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf_lo_f(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi_f(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled box (rows of 128 B, 1024-byte aligned)
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc, int64_t slot_stride,
-    int64_t head_stride, const int* __restrict__ slot32, const int* __restrict__ pos32, float* __restrict__ part_o,
-    float2* __restrict__ part_ml, int nsplit, int chunk, int H, float qscale, int* status) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  AttnSmem<G>& sm = *reinterpret_cast<AttnSmem<G>*>(smem_raw);
+__global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
+    const int* __restrict__ slot32, const int* __restrict__ pos32, float* __restrict__ part_o,
+    float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out, int nsplit, int chunk, int H,
+    float qscale, int* status) {
+  static_assert(G <= 8, "the query heads of one kv head fill at most 8 of the 16 mma rows");
+  extern __shared__ unsigned char smem_raw[];
+  MmaAttnSmem& sm =
+      *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int KV = gridDim.y;
   const int pos = pos32[row];
   const int t0 = split * chunk;
   if (t0 > pos) return;
   const int ntok = min(chunk, pos + 1 - t0);
-  const int nst = cdiv(ntok, kStageTok);
+  const int nblk = cdiv(ntok, kBlkTok);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tl = warp * 8 + (lane >> 2), p = lane & 3;
-  const int64_t base = (int64_t)slot32[row] * slot_stride + (int64_t)kvh * head_stride + (int64_t)t0 * kHeadDim;
-  const bf16* kg = kc + base;
-  const bf16* vg = vc + base;
+  const int g = lane >> 2, t = lane & 3;
+  const int zc = slot32[row] * KV + kvh;
+  const int nmine = warp < nblk ? (nblk - 1 - warp) / 4 + 1 : 0;  // blocks warp, warp + 4, ...
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&sm.bar[s], 1);
+    for (int w = 0; w < 4; ++w)
+      for (int st = 0; st < kMmaStages; ++st) mbar_init(&sm.bar[w][st], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  auto issue = [&](int st) {
-    const int n = min(kStageTok, ntok - st * kStageTok);
-    const uint32_t bytes = (uint32_t)n * kTokBytes;
-    uint64_t* bar = &sm.bar[st % kStages];
-    mbar_expect_tx(bar, 2 * bytes);
-    bulk_g2s(sm.k[st % kStages], kg + (int64_t)st * kStageTok * kHeadDim, bytes, bar);
-    bulk_g2s(sm.v[st % kStages], vg + (int64_t)st * kStageTok * kHeadDim, bytes, bar);
+  auto issue = [&](int i) {  // lane 0: this warp's i-th block into stage i % kMmaStages
+    unsigned char* st = sm.stage[warp][i % kMmaStages];
+    uint64_t* bar = &sm.bar[warp][i % kMmaStages];
+    const int y = t0 + (warp + 4 * i) * kBlkTok;
+    mbar_expect_tx(bar, kBlkBytes);
+    tma_load_3d(st, &kmap, 0, y, zc, bar);
+    tma_load_3d(st + kBoxBytes, &kmap, 64, y, zc, bar);
+    tma_load_3d(st + 2 * kBoxBytes, &vmap, 0, y, zc, bar);
+    tma_load_3d(st + 3 * kBoxBytes, &vmap, 64, y, zc, bar);
   };
-  int issued = min(kStages, nst);  // meaningful in thread 0 only
-  if (tid == 0)
-    for (int st = 0; st < issued; ++st) issue(st);
+  if (lane == 0)
+    for (int i = 0; i < min(kMmaStages, nmine); ++i) issue(i);
 
-  // this thread's slice of the G query heads, pre-scaled into the exp2 domain
-  float qr[G][4][8];
+  // A fragments of Q (rows = query heads): a0 = Q[g][16ks + 2t, +1], a2 = Q[g][16ks + 8 + 2t, +1]; rows >= G zero
+  uint32_t qa[8][2];
+  {
+    const uint32_t* qp = reinterpret_cast<const uint32_t*>(q + ((int64_t)row * H + kvh * G + min(g, G - 1)) * kHeadDim);
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const uint4* qp = reinterpret_cast<const uint4*>(q + ((int64_t)row * H + kvh * G + g) * kHeadDim);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      unpack8(qp[p + 4 * j], qr[g][j]);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qr[g][j][e] *= qscale;
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = g < G ? qp[8 * ks + t] : 0u;
+      qa[ks][1] = g < G ? qp[8 * ks + 4 + t] : 0u;
     }
   }
-  float m[G], l[G], acc[G][4][8];
+  float o[8][4];  // O^T tiles: o[mt] = rows (dims) 16mt + g, 16mt + 8 + g; columns (query heads) 2t, 2t + 1
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][j][e] = 0.f;
-  }
-
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // of query head g, identical in the 4 lanes of quad g
   bool timed_out = false;
-  for (int st = 0; st < nst; ++st) {
-    const int buf = st % kStages;
-    const bool got = mbar_wait(&sm.bar[buf], (st / kStages) & 1, status);
-    if (got) {
-      const bool valid = st * kStageTok + tl < ntok;
-      const uint4* krow = reinterpret_cast<const uint4*>(sm.k[buf] + tl * kHeadDim);
-      float s[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) s[g] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float kf[8];
-        unpack8(krow[p + 4 * j], kf);
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) s[g] = fmaf(qr[g][j][e], kf[e], s[g]);
-      }
-      float pg[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        s[g] += __shfl_xor_sync(0xffffffffu, s[g], 1);
-        s[g] += __shfl_xor_sync(0xffffffffu, s[g], 2);
-        s[g] = valid ? s[g] : -INFINITY;
-        float mx = fmaxf(s[g], __shfl_xor_sync(0xffffffffu, s[g], 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        if (mx > m[g] + kLazyRescale) {  // warp-uniform
-          const float r = exp2f(m[g] - mx);
-          m[g] = mx;
-          l[g] *= r;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[g][j][e] *= r;
-        }
-        pg[g] = valid ? exp2f(s[g] - m[g]) : 0.f;
-        l[g] += pg[g];
-      }
-      if (valid) {
-        const uint4* vrow = reinterpret_cast<const uint4*>(sm.v[buf] + tl * kHeadDim);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float vf[8];
-          unpack8(vrow[p + 4 * j], vf);
-#pragma unroll
-          for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[g][j][e] = fmaf(pg[g], vf[e], acc[g][j][e]);
-        }
-      }
-    }
-    if (__syncthreads_or(!got)) {
+  int i = 0;
+  for (; i < nmine; ++i) {
+    const int stg = i % kMmaStages;
+    const bool got = mbar_wait(&sm.bar[warp][stg], (i / kMmaStages) & 1, status);
+    if (!__all_sync(0xffffffffu, got)) {
       timed_out = true;
       break;
     }
-    if (tid == 0 && st + kStages < nst) issue(issued++);
-  }
-  if (timed_out) {
-    // drain the copies still in flight (bounded) before the CTA's shared memory is released
-    if (tid == 0)
-      for (int st = max(0, issued - kStages); st < issued; ++st)
-        mbar_wait(&sm.bar[st % kStages], (st / kStages) & 1, nullptr);
-    __syncthreads();
-    return;
-  }
-
-  // reduce over the 8 token groups of the warp (lanes with equal p share dims; m is warp-uniform)
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][j][e] += __shfl_xor_sync(0xffffffffu, acc[g][j][e], o);
+    unsigned char* st = sm.stage[warp][stg];
+    const int b = warp + 4 * i;
+    const int nv = min(kBlkTok, ntok - b * kBlkTok);
+    if (nv < kBlkTok) {  // zero V rows nv..15 of both boxes
+      uint4* v4 = reinterpret_cast<uint4*>(st + 2 * kBoxBytes);
+      for (int e = lane; e < 2 * kBlkTok * 8; e += 32)
+        if (((e >> 3) & (kBlkTok - 1)) >= nv) v4[e] = make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
     }
-  }
-  // cross-warp merge through shared memory (the stage buffers are free now)
-  float* wacc = reinterpret_cast<float*>(sm.k[0]);            // [4 warps][G][128]
-  float* wml = wacc + 4 * G * kHeadDim;                        // [4 warps][G][2]
-  if (lane < 4) {
+    const uint32_t kb = smem_u32(st), vb = kb + 2 * kBoxBytes;
+    const int j = lane >> 3;                           // ldmatrix: this lane addresses row (lane & 7) of matrix j
+    const int lr = ((j >> 1) << 3) + (lane & 7), lc = j & 1;
+    // S = Q K^T over 16 positions: s[nt] = rows g (c0, c1) at positions nt*8 + 2t, +1
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t k0, k1, k2, k3;
+      ldsm_x4(kb + (ks >> 2) * kBoxBytes + sw128(lr, ((ks & 3) << 1) + lc), k0, k1, k2, k3);
+      mma_bf16(s[0], qa[ks][0], 0u, qa[ks][1], 0u, k0, k1);
+      mma_bf16(s[1], qa[ks][0], 0u, qa[ks][1], 0u, k2, k3);
+    }
+    float p[2][2];
+    float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) wacc[(warp * G + g) * kHeadDim + (p + 4 * j) * 8 + e] = acc[g][j][e];
-    if (lane == 0)
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        wml[(warp * G + g) * 2] = m[g];
-        wml[(warp * G + g) * 2 + 1] = l[g];
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = g < G && b * kBlkTok + nt * 8 + 2 * t + e < ntok;
+        p[nt][e] = valid ? s[nt][e] * qscale : -INFINITY;
+        mx = fmaxf(mx, p[nt][e]);
       }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float r = 1.f;
+    if (mx > m_run + kLazyRescale) {
+      r = exp2f(m_run - mx);
+      m_run = mx;
+      l_run *= r;
+    }
+    if (__any_sync(0xffffffffu, r != 1.f)) {  // O^T column q lives in the lanes with t = q / 2
+      const float r0 = __shfl_sync(0xffffffffu, r, 8 * t), r1 = __shfl_sync(0xffffffffu, r, 8 * t + 4);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= r0;
+        o[mt][1] *= r1;
+        o[mt][2] *= r0;
+        o[mt][3] *= r1;
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[nt][e] = p[nt][e] == -INFINITY ? 0.f : exp2f(p[nt][e] - m_run);
+        l_run += p[nt][e];
+      }
+    const uint32_t h0 = pack_bf2(p[0][0], p[0][1]), h1 = pack_bf2(p[1][0], p[1][1]);
+    const uint32_t l0 = pack_bf2(p[0][0] - bf_lo_f(h0), p[0][1] - bf_hi_f(h0));
+    const uint32_t l1 = pack_bf2(p[1][0] - bf_lo_f(h1), p[1][1] - bf_hi_f(h1));
+    // O^T += V^T P^T: per 16 dims, A = V^T (ldmatrix.trans of the V rows), B = P^T = {p[0], p[1]} of quad g
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb + (mt >> 2) * kBoxBytes + sw128(lr, ((mt & 3) << 1) + lc), a0, a1, a2, a3);
+      mma_bf16(o[mt], a0, a1, a2, a3, h0, h1);
+      mma_bf16(o[mt], a0, a1, a2, a3, l0, l1);
+    }
+    __syncwarp();
+    if (lane == 0 && i + kMmaStages < nmine) issue(i + kMmaStages);
+  }
+  if (timed_out) {  // drain this warp's copies still in flight (bounded) before its buffers are reused
+    if (lane == 0)
+      for (int k = i; k < min(nmine, i + kMmaStages); ++k)
+        mbar_wait(&sm.bar[warp][k % kMmaStages], (k / kMmaStages) & 1, nullptr);
+    __syncwarp();
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    m_run = -INFINITY;
+    l_run = 0.f;
+  }
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  // the warp's partial, in its own (now idle) stage buffers: wo[G][128], wml[G][2]
+  float* wo = reinterpret_cast<float*>(sm.stage[warp][0]);
+  float* wml = wo + G * kHeadDim;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int qh = 2 * t + (e & 1);
+      if (qh < G) wo[qh * kHeadDim + 16 * mt + g + ((e >> 1) << 3)] = o[mt][e];
+    }
+  if (t == 0 && g < G) {
+    wml[g * 2] = m_run;
+    wml[g * 2 + 1] = l_run;
   }
   __syncthreads();
-  const int64_t pidx = ((int64_t)row * KV + kvh) * nsplit + split;
+  float Og[G], Mg[G], Lg[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int gg = 0; gg < G; ++gg) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, reinterpret_cast<const float*>(sm.stage[w][0])[G * kHeadDim + gg * 2]);
     float O = 0.f, L = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float mw = wml[(w * G + g) * 2];
+      const float* ww = reinterpret_cast<const float*>(sm.stage[w][0]);
+      const float mw = ww[G * kHeadDim + gg * 2];
       const float sc = mw == -INFINITY ? 0.f : exp2f(mw - M);
-      O = fmaf(wacc[(w * G + g) * kHeadDim + tid], sc, O);
-      L = fmaf(wml[(w * G + g) * 2 + 1], sc, L);
+      O = fmaf(ww[gg * kHeadDim + tid], sc, O);
+      L = fmaf(ww[G * kHeadDim + gg * 2 + 1], sc, L);
     }
-    part_o[(pidx * G + g) * kHeadDim + tid] = O;
-    if (tid == 0) part_ml[pidx * G + g] = make_float2(M, L);
+    Og[gg] = O;
+    Mg[gg] = M;
+    Lg[gg] = L;
   }
-}
-
-// Merge the splits of one (row, kv head): out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M), rounded to bf16.
-template <int G>
-__global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __restrict__ part_o,
-                                                                const float2* __restrict__ part_ml,
-                                                                const int* __restrict__ pos32, bf16* __restrict__ out,
-                                                                int nsplit, int chunk, int H) {
-  const int kvh = blockIdx.x, row = blockIdx.y, KV = gridDim.x, d = threadIdx.x;
-  const int n = min(nsplit, pos32[row] / chunk + 1);
-  const int64_t pbase = ((int64_t)row * KV + kvh) * nsplit;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float M = -INFINITY;
-    for (int s = 0; s < n; ++s) M = fmaxf(M, part_ml[(pbase + s) * G + g].x);
-    float O = 0.f, L = 0.f;
-    for (int s = 0; s < n; ++s) {
-      const float2 ml = part_ml[(pbase + s) * G + g];
-      const float sc = exp2f(ml.x - M);
-      O = fmaf(part_o[((pbase + s) * G + g) * kHeadDim + d], sc, O);
-      L = fmaf(ml.y, sc, L);
-    }
-    out[((int64_t)row * H + kvh * G + g) * kHeadDim + d] = to_bf(O / L);
-  }
+  split_epilogue<G>(Og, Mg, Lg, tid, row, kvh, KV, split, nsplit, min(nsplit, pos / chunk + 1), part_o, part_ml,
+                    tickets, out, H, &sm.last);
 }
 
 }  // namespace m3
@@ -401,6 +477,8 @@ struct m3_backbone {
        *act = nullptr;
   float* part_o = nullptr;
   float2* part_ml = nullptr;
+  int* tickets = nullptr;  // [max_rows][kv_heads] split arrival counters, zero between launches
+  std::vector<CUtensorMap> kmap, vmap;  // per layer, over [(max_slots + 1) * kv_heads][capacity][head_dim]
 };
 
 namespace {
@@ -421,13 +499,6 @@ int choose_chunk(int rows, int ctx, int kv, int max_split) {
   return chunk;
 }
 
-int attn_smem_bytes(int G) {
-  switch (G) {
-    case 1: return sizeof(AttnSmem<1>);
-    case 2: return sizeof(AttnSmem<2>);
-    default: return sizeof(AttnSmem<4>);
-  }
-}
 
 }  // namespace
 
@@ -456,6 +527,35 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
     bb->kc.push_back((bf16*)w->k_cache[i]);
     bb->vc.push_back((bf16*)w->v_cache[i]);
   }
+  {
+    EncodeTiled enc;
+    if (tensor_map_encoder(&enc) != M3_OK) {
+      delete bb;
+      return M3_ERR_CUDA;
+    }
+    bb->kmap.resize(c.layers);
+    bb->vmap.resize(c.layers);
+    const cuuint64_t dims[3] = {(cuuint64_t)c.head_dim, (cuuint64_t)c.capacity,
+                                (cuuint64_t)(c.max_slots + 1) * c.kv_heads};
+    const cuuint64_t strides[2] = {(cuuint64_t)c.head_dim * 2, (cuuint64_t)c.capacity * c.head_dim * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kBlkTok, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    for (int i = 0; i < c.layers; ++i)
+      for (int kvv = 0; kvv < 2; ++kvv) {
+        void* base = kvv ? w->v_cache[i] : w->k_cache[i];
+        CUtensorMap* m = kvv ? &bb->vmap[i] : &bb->kmap[i];
+        const CUresult r = (reinterpret_cast<uintptr_t>(base) & 15) ? CUDA_ERROR_INVALID_VALUE
+                           : enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+          delete bb;
+          set_error("m3_backbone_create: tensor map of layer %d %s cache failed (%d); caches must be 16-byte aligned",
+                    i, kvv ? "V" : "K", (int)r);
+          return M3_ERR_ARG;
+        }
+      }
+  }
   bb->final_norm = (const bf16*)w->final_norm;
   bb->cos = (const bf16*)w->cos;
   bb->sin = (const bf16*)w->sin;
@@ -469,7 +569,7 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   add((size_t)R * Hd * 2); add((size_t)R * Hd * 2); add((size_t)R * qkvw * 2);
   add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * Hd * 2);
   add((size_t)R * 2 * c.ffn * 2); add((size_t)R * c.ffn * 2);
-  add(parts * kHeadDim * 4); add(parts * 8);
+  add(parts * kHeadDim * 4); add(parts * 8); add((size_t)R * c.kv_heads * 4);
   cudaError_t e = cudaMalloc(&bb->ws, bytes);
   if (e != cudaSuccess) {
     delete bb;
@@ -490,17 +590,17 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   bb->act = carve<bf16>(p, (size_t)R * c.ffn);
   bb->part_o = carve<float>(p, parts * kHeadDim);
   bb->part_ml = carve<float2>(p, parts);
-  if (cudaMemset(bb->status, 0, 256) != cudaSuccess) {
+  bb->tickets = carve<int>(p, (size_t)R * c.kv_heads);
+  if (cudaMemset(bb->status, 0, 256) != cudaSuccess ||
+      cudaMemset(bb->tickets, 0, (size_t)R * c.kv_heads * 4) != cudaSuccess) {
     cudaFree(bb->ws);
     delete bb;
     set_error("m3_backbone_create: memset failed");
     return M3_ERR_CUDA;
   }
-  const int smem = attn_smem_bytes(G);
-  cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(AttnSmem<1>));
-  cudaFuncSetAttribute(attn_split_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(AttnSmem<2>));
-  cudaFuncSetAttribute(attn_split_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(AttnSmem<4>));
-  (void)smem;
+  cudaFuncSetAttribute(attn_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
+  cudaFuncSetAttribute(attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
+  cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
   *out = bb;
   return M3_OK;
 }
@@ -524,17 +624,12 @@ static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t
   const int G = c.heads / c.kv_heads;
   const int chunk = choose_chunk(rows, ctx, c.kv_heads, bb->max_split);
   const int nsplit = cdiv(ctx, chunk);
-  const int64_t head_stride = (int64_t)c.capacity * c.head_dim;
-  const int64_t slot_stride = (int64_t)c.kv_heads * head_stride;
   const float qscale = (1.f / sqrtf((float)c.head_dim)) * 1.4426950408889634f;
   dim3 grid(nsplit, c.kv_heads, rows);
 #define M3_ATTN(GG)                                                                                          \
-  attn_split_kernel<GG><<<grid, kAttnThreads, sizeof(AttnSmem<GG>), s>>>(                                    \
-      bb->q, bb->kc[layer], bb->vc[layer], slot_stride, head_stride, bb->slot32, bb->pos32, bb->part_o,     \
-      bb->part_ml, nsplit, chunk, c.heads, qscale, bb->status);                                             \
-  M3_LAUNCHED();                                                                                             \
-  attn_combine_kernel<GG><<<dim3(c.kv_heads, rows), kHeadDim, 0, s>>>(bb->part_o, bb->part_ml, bb->pos32,   \
-                                                                      bb->o, nsplit, chunk, c.heads);
+  attn_mma_kernel<GG><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                         \
+      bb->kmap[layer], bb->vmap[layer], bb->q, bb->slot32, bb->pos32, bb->part_o, bb->part_ml, bb->tickets,    \
+      bb->o, nsplit, chunk, c.heads, qscale, bb->status);
   if (G == 1) {
     M3_ATTN(1)
   } else if (G == 2) {

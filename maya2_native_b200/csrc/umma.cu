@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "tma.cuh"
 
 namespace m3 {
 
@@ -22,14 +23,6 @@ constexpr int kUmmaK = 16;
 constexpr int kUmmaThreads = 128;
 
 // ------------------------------------------------------------------------------------------------ PTX wrappers
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
   const uint64_t addr = smem_u32(p);
@@ -193,13 +186,11 @@ __global__ void __launch_bounds__(kUmmaThreads) umma_gemm_kernel(const __grid_co
 
 // ------------------------------------------------------------------------------------------------ host
 namespace {
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiled g_encode = nullptr;
 std::once_flag g_encode_once;
+}  // namespace
 
-int get_encode(EncodeTiled* out) {
+int tensor_map_encoder(EncodeTiled* out) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -212,10 +203,11 @@ int get_encode(EncodeTiled* out) {
   return M3_OK;
 }
 
+namespace {
 // 2-D map over a row-major bf16 matrix [rows, cols] with leading dimension ld (elements); box = 64 cols x box_rows.
 int make_map(CUtensorMap* map, const void* ptr, int rows, int cols, int64_t ld, int box_rows) {
   EncodeTiled enc;
-  M3_TRY(get_encode(&enc));
+  M3_TRY(tensor_map_encoder(&enc));
   M3_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 8 == 0, M3_ERR_ARG,
              "tensor-core GEMM operand must be 16-byte aligned with a leading dimension multiple of 8");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
