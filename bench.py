@@ -42,6 +42,9 @@ FRAME_S = 0.08
 PROMPT = (64, 512)
 TARGET = (100, 1500)
 METRIC = "audio-s/s at 256 streams per GPU (continuous batching)"
+# DRAM bytes / algorithmic bytes of attn_mma_kernel from an Nsight Compute capture at 256 seats x 1 layer (894.0 MB
+# read + written for 877.7 MB of K/V, q and o): the whole-block granularity of the last 16 positions of each split.
+ATTN_TRAFFIC_RATIO = 1.0186
 
 
 def args_():
@@ -55,6 +58,7 @@ def args_():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seats", type=int, default=16)
+    ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] TTFA and configs[3] Mimi runs")
     ap.add_argument("--profile-ticks", type=int, default=0,
                     help="after warm-up, run this many ticks inside cudaProfilerStart/Stop (for ncu "
                          "--profile-from-start off) and exit")
@@ -221,7 +225,7 @@ def run_native(a, rank, world, local):
     offs = np.cumsum([0] + [len(tp.plan) for tp in plans])
     frames = sum(len(tp.dec) + len(tp.new) for tp in plans)
     stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(plans) + 1)]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -230,7 +234,7 @@ def run_native(a, rank, world, local):
     launches = 0
     with Clocks(local) as clk:
         c0 = lib.m3_launch_count()
-        e0.record(stream)
+        ev[0].record(stream)
         for k, tp in enumerate(plans):
             for s in tp.new:
                 eng.reset_slot(s)
@@ -238,10 +242,11 @@ def run_native(a, rank, world, local):
             gr.plan.copy_(staged[offs[k]:offs[k + 1]], non_blocking=True)
             eng.replay(gr, tp.rows, tp.seats, tp.ctx)
             launches += gr.launches
-        e1.record(stream)
+            ev[k + 1].record(stream)
         torch.cuda.synchronize()
         launches += lib.m3_launch_count() - c0          # eager launches in the region (slot resets)
-    dev_ms = e0.elapsed_time(e1)
+    dev_ms = ev[0].elapsed_time(ev[-1])
+    tick_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(len(plans))]
     status = eng.device_status()
 
     # ---- end to end through the public tick: H2D plan + D2H readout + sync every tick, wall clock
@@ -282,15 +287,7 @@ def run_native(a, rank, world, local):
 
     # ---- reduce over ranks
     clocks = clk.summary()
-    vals = torch.tensor([dev_ms, e2e_s * 1e3, float(frames), float(e2e_frames)], device=dev, dtype=torch.float64)
-    if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx[:2], op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm[2:], op=dist.ReduceOp.SUM)
-        dev_ms, e2e_ms, frames, e2e_frames = float(mx[0]), float(mx[1]), float(sm[2]), float(sm[3])
-    else:
-        e2e_ms = e2e_s * 1e3
+    dev_ms, e2e_ms, frames, e2e_frames = reduce_over_ranks(dev_ms, e2e_s * 1e3, frames, e2e_frames, world, dev)
     value = frames * FRAME_S / (dev_ms / 1e3)
     e2e = e2e_frames * FRAME_S / (e2e_ms / 1e3)
     peaks = {}
@@ -314,14 +311,110 @@ def run_native(a, rank, world, local):
         "e2e": {"value": round(e2e, 2), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": int(d2h / max(a.steps, 1))},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": "decode attention (split + combine)",
+                     "frac": round(achieved / hbm, 4), "traffic": int(attn_bytes * ATTN_TRAFFIC_RATIO),
+                     "traffic_source": "ncu DRAM bytes of the same kernel at 256 seats x 1 layer, scaled by keys",
+                     "kernel": "attn_mma_kernel (split-KV decode attention, splits merged in the launch)",
                      "peak_source": peak_src, "algorithmic_bytes": int(attn_bytes), "launch_ms": round(attn_ms, 5)},
-        "tick_ms": round(dev_ms / a.steps, 4), "frames_timed": int(frames), "device_status": status,
+        "tick_ms": round(dev_ms / a.steps, 4),
+        "tick_ms_p50": round(float(np.percentile(tick_ms, 50)), 4),
+        "tick_ms_p99": round(float(np.percentile(tick_ms, 99)), 4),
+        "frames_timed": int(frames), "device_status": status,
         "clocks": clocks,
         "gpu_launches": int(launches),
     }
     eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    if world == 1 and not a.no_extra:
+        line["ttfa"] = run_ttfa(dev, a.seed)
+        line["mimi"] = run_mimi(dev, a.seed)
     return line
+
+
+def reduce_over_ranks(dev_ms, e2e_ms, frames, e2e_frames, world, device):
+    """Max of the timed durations and sum of the frames over ranks (every rank is one replica)."""
+    if world == 1:
+        return dev_ms, e2e_ms, frames, e2e_frames
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([dev_ms, e2e_ms], device=device, dtype=torch.float64)
+    n = torch.tensor([float(frames), float(e2e_frames)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    return float(t[0]), float(t[1]), float(n[0]), float(n[1])
+
+
+def run_ttfa(dev, seed, n_req=100, warm=8):
+    """B = 1, capacity 1024, one prompt of 300 uniform-random token ids per request (generator seed i),
+    temperature 0.8 / top-k 50 for cb0 and depth.  TTFA = submit -> the tick that returns the request's first PCM
+    frame (inline prefill of the prompt + the first frame), host clock; the engine is warm (graphs captured)."""
+    import torch
+
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.config import BASELINE
+    from maya2_native_b200.engine import TickConfig, TickEngine
+    W = WG.generate(WG.all_shapes(BASELINE), seed=seed, device=dev)
+    cfg = TickConfig(max_seats=1, capacity=1024, temp=0.8, top_k=50, cb0_temp=0.8, cb0_top_k=50, stops=False)
+    eng = TickEngine(BASELINE, W, cfg, device=dev)
+    del W
+    out = []
+    for i in range(warm + n_req):
+        prompt = np.random.default_rng(i).integers(0, BASELINE.backbone.vocab, 300)
+        t0 = time.perf_counter()
+        s = eng.submit(prompt, 2)
+        first = None
+        for _ in range(8):
+            res = eng.tick()
+            if first is None and any(x[0] is s and x[3] is not None for x in res):
+                first = time.perf_counter()
+            if s.stop is not None:
+                break
+        if first is None:
+            raise RuntimeError("TTFA request produced no audio")
+        if i >= warm:
+            out.append((first - t0) * 1e3)
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    return {"p50_ms": round(float(np.percentile(out, 50)), 3), "p99_ms": round(float(np.percentile(out, 99)), 3),
+            "n": n_req, "workload": "configs[1]: B=1, capacity 1024, 300-token prompts, temp 0.8 / top-k 50",
+            "measured": "submit -> first PCM frame out of TickEngine.tick (host clock, warm engine)"}
+
+
+def run_mimi(dev, seed, streams=256, warm=130, frames=50):
+    """StaticMimi.decode over 256 streams, codes U[0, 2048) x 8 codebooks (seed 0), after 130 warm
+    frames (the 250-position window and the 256-entry ring are full); device-timed with CUDA events.  hbm_gbs =
+    (ring K/V read + decoder weights) per frame batch / time."""
+    import torch
+
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.codec import StaticMimi
+    from maya2_native_b200.config import BASELINE
+    g = BASELINE.mimi
+    shapes = {k: v for k, v in WG.all_shapes(BASELINE).items() if k.startswith("mimi.")}
+    W = WG.generate(shapes, seed=seed, device=dev)
+    codec = StaticMimi(W, streams, batch_buckets=(streams,), geom=g, device=dev)
+    wbytes = sum(int(np.prod(v)) for v in shapes.values()) * 2
+    del W
+    gen = torch.Generator(device=dev).manual_seed(0)
+    codes = torch.randint(0, g.codebook_size, (warm + frames, streams, g.n_q), device=dev, generator=gen)
+    slots = torch.arange(streams, device=dev)
+    with torch.inference_mode():
+        for f in range(warm):
+            codec.decode(slots, codes[f])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for f in range(warm, warm + frames):
+            codec.decode(slots, codes[f])
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / frames
+    kv = streams * g.layers * 2 * g.heads * g.ring * (g.hidden // g.heads) * 2
+    codec.close()
+    return {"samples_per_s": round(streams * g.samples_per_frame / (ms / 1e3)),
+            "ms_per_frame": round(ms, 4), "hbm_gbs": round((kv + wbytes) / (ms / 1e3) / 1e9, 1),
+            "workload": "configs[3]: 256 streams, codes U[0,2048) x 8, 130 warm frames, StaticMimi.decode"}
 
 
 # ------------------------------------------------------------------------------------------------ CPU arm

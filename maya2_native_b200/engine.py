@@ -337,6 +337,24 @@ class TickEngine:
         self.commit(tp)
         return self._deliver(dec + new, host.numpy())
 
+    @torch.inference_mode()
+    def last_outputs(self, n):
+        """Copies of the last tick's per-seat device outputs for its first n seats (tick order: decode seats, then
+        admitted ones): final-normed backbone hidden [n, hidden] bf16, codes [n, n_q] int64, pre-clamp PCM
+        [n, samples_per_frame] fp32."""
+        hp, cp, pp = L.vp(), L.vp(), L.vp()
+        L.check(L.load().m3_tick_outputs(self._handle, hp, cp, pp), "m3_tick_outputs")
+        D, nq = self.geom.backbone.hidden, self.geom.depth.n_q
+
+        def view(ptr, shape, typestr):
+            class _Dev:
+                __cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (int(ptr.value), False),
+                                            "version": 3, "strides": None}
+            return torch.as_tensor(_Dev(), device=self.device).clone()
+
+        h = view(hp, (n, D), "<i2").view(torch.bfloat16)
+        return h, view(cp, (n, nq), "<i8"), view(pp, (n, self.spf), "<f4")
+
     def deliver_forced(self, seats):
         """Host bookkeeping of a tick whose readout is not read (stops disabled): every seat got one frame."""
         return self._deliver(seats, None)

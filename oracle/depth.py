@@ -53,8 +53,11 @@ class DepthOracle:
             s = np.where(mask, np.float32(-np.inf), s)
         return self.rnd(np.einsum("bhqk,bhkd->bhqd", softmax(s), v))
 
-    def step(self, slots, h, cb0):
-        """FastDepth.__call__ -> (codes [B, n_q] int64, feedback [B, d_backbone]); advances row_ctr."""
+    def step(self, slots, h, cb0, force=None):
+        """FastDepth.__call__ -> (codes [B, n_q] int64, feedback [B, d_backbone]); advances row_ctr.
+
+        force [B, n_q] (teacher forcing, for stage-by-stage comparisons): the next prefix rows and the feedback are
+        built from these codes instead of the sampled ones; the sampled codes are still returned."""
         g, rnd, W = self.g, self.rnd, self.W
         slots = np.asarray(slots, np.int64)
         B, D, NL, H, HD, L = len(slots), g.d, g.n_q, g.heads, g.head_dim, g.layers
@@ -104,12 +107,13 @@ class DepthOracle:
             self.last_logits.append(logits)
             code = topk_sample(logits, seeds, ctrs, level, self.temp, self.top_k, self.greedy)
             codes.append(code)
+            used = code if force is None else np.asarray(force, np.int64)[:, level]
             if n < NL:
-                prefix[:, n] = self.embed[level][code]
+                prefix[:, n] = self.embed[level][used]
             previous = group
         np.add.at(self.row_ctr, slots, 1)
         codes = np.stack(codes, -1)
-        return codes, self.feedback(codes)
+        return codes, self.feedback(codes if force is None else np.asarray(force, np.int64))
 
     def feedback(self, codes):
         """AudioInputEmbed.frames without its range check: RMSNorm(sum_k table[code_k + k*n_codes] / sqrt(n_q)),
