@@ -59,6 +59,9 @@ def args_():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seats", type=int, default=16)
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] TTFA and configs[3] Mimi runs")
+    ap.add_argument("--stages", action="store_true",
+                    help="print the device time of each stage of a decode tick (backbone, cb0, depth, Mimi) at the "
+                         "configs[2] steady state, each stage called through its own mirror object, and exit")
     ap.add_argument("--profile-ticks", type=int, default=0,
                     help="after warm-up, run this many ticks inside cudaProfilerStart/Stop (for ncu "
                          "--profile-from-start off) and exit")
@@ -417,6 +420,49 @@ def run_mimi(dev, seed, streams=256, warm=130, frames=50):
             "workload": "configs[3]: 256 streams, codes U[0,2048) x 8, 130 warm frames, StaticMimi.decode"}
 
 
+def run_stages(a):
+    """Per-stage device time of a decode tick: every seat decodes one frame, stage by stage through the mirror
+    objects (StaticBackbone.step, the cb0 sampler, FastDepth, StaticMimi.decode), CUDA events between the stages."""
+    import torch
+
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.config import BASELINE
+    from maya2_native_b200.engine import TickConfig, TickEngine
+    dev = torch.device("cuda", 0)
+    g = BASELINE
+    W = WG.generate(WG.all_shapes(g), seed=a.seed, device=dev)
+    eng = TickEngine(g, W, TickConfig(max_seats=a.seats, capacity=a.capacity, stops=False), device=dev)
+    del W
+    wl = Workload(g.backbone.vocab, a.seed * 7919)
+    init_steady_state(eng, wl, a.seats)
+    slots = [s.slot for s in eng.active]
+    idx = torch.tensor(slots, device=dev)
+    names = ("backbone", "cb0", "depth", "mimi")
+    times = {k: [] for k in names}
+    with torch.inference_mode():
+        for it in range(a.warmup + a.steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            x = eng.feedback[idx]
+            ev[0].record()
+            h = eng.backbone.step(slots, x)
+            ev[1].record()
+            _, cb0 = eng.cb0(h, idx)
+            ev[2].record()
+            codes, fb = eng.depth(slots, h, cb0)
+            ev[3].record()
+            eng.codec.decode(idx, codes)
+            ev[4].record()
+            eng.feedback[idx] = fb
+            torch.cuda.synchronize()
+            if it >= a.warmup:
+                for k, n in enumerate(names):
+                    times[n].append(ev[k].elapsed_time(ev[k + 1]))
+    med = {n: round(float(np.median(v)), 4) for n, v in times.items()}
+    eng.close()
+    return {"stages_ms": med, "sum_ms": round(sum(med.values()), 4), "seats": a.seats, "steps": a.steps,
+            "note": "eager stage calls (backbone not graph-captured), events between stages"}
+
+
 # ------------------------------------------------------------------------------------------------ CPU arm
 def cpu_tick_sample(seats, seed=0, reps=1):
     """The fp32 CPU oracle (numpy port of the reference's eager path) on `seats` seats at the configs[2] KV-length
@@ -476,6 +522,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    if a.stages:
+        print(json.dumps(run_stages(a)), flush=True)
+        return
     if a.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(a, rank, world)), flush=True)

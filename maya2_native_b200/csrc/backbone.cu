@@ -90,6 +90,13 @@ __global__ void add_rms_kernel(const bf16* __restrict__ hin, const bf16* __restr
   }
 }
 
+int launch_add_rms(int rows, const bf16* hin, const bf16* a, bf16* hout, bf16* y, const bf16* w, float eps, int n,
+                   cudaStream_t s) {
+  add_rms_kernel<<<rows, std::min(1024, std::max(32, (n / 8 + 31) / 32 * 32)), 0, s>>>(hin, a, hout, y, w, eps, n);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
 // ------------------------------------------------------------------------------------------------ q/k norm + RoPE
 // One warp per (row, head): heads [0, H) are query heads written to q; heads [H, H + KV) are key heads written to
 // the K cache at (slot, kv head, pos) together with the matching value head (serve/fast_backbone.py:62-92).
@@ -651,7 +658,6 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
   if (rows == 0) return M3_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int Hd = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
-  const int norm_threads = std::min(1024, std::max(32, (Hd / 8 + 31) / 32 * 32));
   prep_rows_kernel<<<cdiv(rows, 128), 128, 0, s>>>(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity,
                                                    bb->slot32, bb->pos32, bb->status);
   M3_LAUNCHED();
@@ -660,11 +666,10 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
     if (i == 0) {
       // h = x; y = RMSNorm(x) (HF Qwen3RMSNorm module on the first layer)
       M3_CUDA(cudaMemcpyAsync(bb->h, xin, (size_t)rows * Hd * 2, cudaMemcpyDeviceToDevice, s));
-      add_rms_kernel<<<rows, norm_threads, 0, s>>>(bb->h, nullptr, nullptr, bb->y, bb->in_norm[0], c.eps, Hd);
+      M3_TRY(launch_add_rms(rows, bb->h, nullptr, nullptr, bb->y, bb->in_norm[0], c.eps, Hd, s));
     } else {
-      add_rms_kernel<<<rows, norm_threads, 0, s>>>(bb->h, bb->a, bb->h, bb->y, bb->in_norm[i], c.eps, Hd);
+      M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, bb->y, bb->in_norm[i], c.eps, Hd, s));
     }
-    M3_LAUNCHED();
     M3_TRY(gemm({bb->y, Hd, bb->wqkv[i], Hd, bb->qkv, qkvw, rows, qkvw, Hd, false}, s));
     qk_rope_cache_kernel<<<rows, 32 * (c.heads + c.kv_heads), 0, s>>>(
         bb->qkv, bb->q, bb->kc[i], bb->vc[i], (int64_t)c.kv_heads * c.capacity * c.head_dim,
@@ -675,17 +680,14 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
     M3_TRY(gemm({bb->o, c.heads * c.head_dim, bb->wo[i], c.heads * c.head_dim, bb->a, Hd, rows, Hd,
                  c.heads * c.head_dim, false},
                 s));
-    add_rms_kernel<<<rows, norm_threads, 0, s>>>(bb->h, bb->a, bb->h, bb->y, bb->post_norm[i], c.eps, Hd);
-    M3_LAUNCHED();
+    M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, bb->y, bb->post_norm[i], c.eps, Hd, s));
     M3_TRY(gemm({bb->y, Hd, bb->wgu[i], Hd, bb->gu, 2 * c.ffn, rows, 2 * c.ffn, Hd, false}, s));
     const int64_t nv = (int64_t)rows * (c.ffn / 8);
     silu_mul_kernel<<<(unsigned)((nv + 255) / 256), 256, 0, s>>>(bb->gu, bb->act, rows, c.ffn);
     M3_LAUNCHED();
     M3_TRY(gemm({bb->act, c.ffn, bb->wdown[i], c.ffn, bb->a, Hd, rows, Hd, c.ffn, false}, s));
   }
-  add_rms_kernel<<<rows, norm_threads, 0, s>>>(bb->h, bb->a, bb->h, reinterpret_cast<bf16*>(out), bb->final_norm,
-                                               c.eps, Hd);
-  M3_LAUNCHED();
+  M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, reinterpret_cast<bf16*>(out), bb->final_norm, c.eps, Hd, s));
   lengths_add_kernel<<<cdiv(rows, 128), 128, 0, s>>>(bb->slot32, real, rows, bb->lengths);
   M3_LAUNCHED();
   return M3_OK;

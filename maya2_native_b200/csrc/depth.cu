@@ -120,11 +120,21 @@ __global__ void add_ln_kernel(const bf16* __restrict__ src, int T, int64_t sb, i
   }
 }
 
+int launch_add_ln(int rows, const bf16* src, int T, int64_t sb, int64_t st, const bf16* a, const bf16* c,
+                  int64_t c_slot_stride, const int* slot32, bf16* xout, bf16* y, const bf16* w, const bf16* bias,
+                  float eps, int D, cudaStream_t s) {
+  if (rows <= 0) return M3_OK;
+  add_ln_kernel<<<rows, norm_block(D), 0, s>>>(src, T, sb, st, a, c, c_slot_stride, slot32, xout, y, w, bias, eps, D);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
 // ------------------------------------------------------------------------------------------------ attention
 // Tiny attention over at most kMaxKeys positions: query i of seat b sits at absolute position q0 + i and sees keys
 // 0..q0+i (causal; the last-position and incremental forms are q0 = n-1 with one query).  One warp per
-// (seat, head, query), each lane holding PER consecutive dims; fp32 scores with an online softmax, output rounded
-// once (F.scaled_dot_product_attention).
+// (seat, head, query), each lane holding PER consecutive dims; keys go in batches of 8 whose K and V loads are all
+// in flight together (the kernel is load-latency bound); fp32 scores with an online softmax over the batches, output
+// rounded once (F.scaled_dot_product_attention).
 constexpr int kMaxKeys = 64;
 
 struct KeySrc {
@@ -150,32 +160,57 @@ template <int PER>
 __global__ void depth_attn_kernel(const bf16* __restrict__ qkv, int T, int q0, int Tq, KeySrc ks, int H,
                                   float scale, bf16* __restrict__ out) {
   constexpr int HD = 32 * PER;
+  constexpr int KB = 8;  // keys per batch: their loads are all issued before the first dot product
   const int b = blockIdx.x, h = blockIdx.y;
   const int i = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (i >= Tq) return;
   const int D = H * HD;
   const int qp = q0 + i;
+  const int nk = min(qp + 1, kMaxKeys);
   const bf16* q = qkv + ((int64_t)b * T + (T - Tq) + i) * 3 * D + (int64_t)h * HD + lane * PER;
-  float qv[PER], kv[PER], o[PER];
+  float qv[PER], o[PER];
   load_per<PER>(q, qv);
 #pragma unroll
   for (int e = 0; e < PER; ++e) o[e] = 0.f;
   float m = -INFINITY, l = 0.f;
   const bf16* kb = ks.k + (int64_t)b * ks.sb + (int64_t)h * HD + lane * PER;
   const bf16* vb = ks.v + (int64_t)b * ks.sb + (int64_t)h * HD + lane * PER;
-  for (int j = 0; j <= qp && j < kMaxKeys; ++j) {
-    load_per<PER>(kb + (int64_t)j * ks.sj, kv);
-    float d = 0.f;
+  for (int j0 = 0; j0 < nk; j0 += KB) {
+    float kf[KB][PER], vf[KB][PER], d[KB];
 #pragma unroll
-    for (int e = 0; e < PER; ++e) d = fmaf(qv[e], kv[e], d);
-    d = warp_sum(d) * scale;
-    const float mn = fmaxf(m, d);
-    const float c = expf(m - mn), p = expf(d - mn);
-    load_per<PER>(vb + (int64_t)j * ks.sj, kv);
-    l = l * c + p;
+    for (int jj = 0; jj < KB; ++jj) {
+      const int j = min(j0 + jj, nk - 1);  // past the last key: reload it, masked below
+      load_per<PER>(kb + (int64_t)j * ks.sj, kf[jj]);
+      load_per<PER>(vb + (int64_t)j * ks.sj, vf[jj]);
+    }
 #pragma unroll
-    for (int e = 0; e < PER; ++e) o[e] = fmaf(p, kv[e], o[e] * c);
-    m = mn;
+    for (int jj = 0; jj < KB; ++jj) {
+      d[jj] = 0.f;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) d[jj] = fmaf(qv[e], kf[jj][e], d[jj]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int jj = 0; jj < KB; ++jj) d[jj] += __shfl_xor_sync(0xffffffffu, d[jj], off);
+    float mb = m;
+#pragma unroll
+    for (int jj = 0; jj < KB; ++jj) {
+      d[jj] = j0 + jj < nk ? d[jj] * scale : -INFINITY;
+      mb = fmaxf(mb, d[jj]);
+    }
+    const float c = expf(m - mb);  // m = -inf on the first batch: c = 0
+    l *= c;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) o[e] *= c;
+#pragma unroll
+    for (int jj = 0; jj < KB; ++jj) {
+      const float p = j0 + jj < nk ? expf(d[jj] - mb) : 0.f;
+      l += p;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) o[e] = fmaf(p, vf[jj][e], o[e]);
+    }
+    m = mb;
   }
   bf16* dst = out + ((int64_t)b * Tq + i) * D + (int64_t)h * HD + lane * PER;
 #pragma unroll
@@ -434,9 +469,8 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
     const int start = incremental ? level : 0;
     const int gl = group * L;
     // y = n1(x); x (the residual stream) becomes a contiguous copy of the prefix slice
-    add_ln_kernel<<<R * T, nt, 0, s>>>(d->prefix + (int64_t)start * D, T, (int64_t)NL * D, D, nullptr, nullptr, 0,
-                                       nullptr, d->x, d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D);
-    M3_LAUNCHED();
+    M3_TRY(launch_add_ln(R * T, d->prefix + (int64_t)start * D, T, (int64_t)NL * D, D, nullptr, nullptr, 0, nullptr, d->x,
+                  d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D, s));
     int Tr = T;  // rows per seat in the residual stream
     for (int li = 0; li < L; ++li) {
       M3_TRY(gemm({d->y, D, d->qkv[gl + li], D, d->qkvb, 3 * D, R * Tr, 3 * D, D, false}, s));
@@ -475,9 +509,8 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       }
       M3_TRY(gemm({d->a, D, d->o[gl + li], D, d->ob, D, R * Tr, D, D, false}, s));
       // x, y2 = add_ln(x, o(a), n2)
-      add_ln_kernel<<<R * Tr, nt, 0, s>>>(d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
-                                          d->n2_b[gl + li], c.ln_eps, D);
-      M3_LAUNCHED();
+      M3_TRY(launch_add_ln(R * Tr, d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
+                    d->n2_b[gl + li], c.ln_eps, D, s));
       M3_TRY(gemm({d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
       const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
       gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);
@@ -486,9 +519,8 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       // x, y = add_ln(x, f, next n1 (or the final norm), cross[slot][li])
       const bf16* nw = li + 1 < L ? d->n1_w[gl + li + 1] : d->norm_w;
       const bf16* nb = li + 1 < L ? d->n1_b[gl + li + 1] : d->norm_b;
-      add_ln_kernel<<<R * Tr, nt, 0, s>>>(d->x, Tr, (int64_t)Tr * D, D, d->ob, d->cross_const + (int64_t)li * D,
-                                          (int64_t)L * D, d->slot32, d->x, d->y, nw, nb, c.ln_eps, D);
-      M3_LAUNCHED();
+      M3_TRY(launch_add_ln(R * Tr, d->x, Tr, (int64_t)Tr * D, D, d->ob, d->cross_const + (int64_t)li * D, (int64_t)L * D,
+                    d->slot32, d->x, d->y, nw, nb, c.ln_eps, D, s));
     }
     // level head on the final position, then sample and write the next prefix row
     M3_TRY(gemm({d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, d->logits, c.n_codes, R,

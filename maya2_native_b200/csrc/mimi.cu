@@ -113,84 +113,139 @@ __global__ void mimi_rope_kernel(const bf16* __restrict__ qkv, const int64_t* __
 }
 
 // Sliding-window attention of the frame's T queries over the slot's ring: key r is visible to the query at
-// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head): one
-// thread per ring entry for the scores (16-byte key loads), then the weighted sum split over 8-dim column groups x
-// ring chunks, reduced through shared memory.
-constexpr int kRingMax = 512;
+// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head): the
+// head's K and V rings (ring x hd bf16 each, contiguous) arrive by two bulk copies on separate mbarriers, so the
+// scores start as soon as K has landed while V is still in flight.  hd/8 lanes share a ring entry (16 bytes each;
+// a quarter-warp reads whole 128-byte rows, conflict-free); fp32 scores, softmax statistics by one warp per query,
+// weighted sum of V reduced over lanes and warps.  Every wait is bounded.
 constexpr int kRingThreads = 256;
+constexpr int kRingWarps = kRingThreads / 32;
+constexpr int kRingMaxT = 4;
 
+inline size_t ring_attn_smem(int T, int ring, int hd) {
+  return 128 + 2 * (size_t)ring * hd * 2 + (size_t)ring * 8 +
+         ((size_t)T * ring + (size_t)kRingWarps * T * hd + 2 * T) * 4;
+}
+
+template <int T>
 __global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ kring, const bf16* __restrict__ vring,
-    const int64_t* __restrict__ key_pos, const int64_t* __restrict__ pos, const int* __restrict__ slot32, int T,
-    int heads, int hd, int ring, int window, int64_t slot_stride, float scale, bf16* __restrict__ out) {
-  __shared__ float sc[4][kRingMax];
-  __shared__ float qs[4][128];
-  __shared__ float red[32];
-  __shared__ float part[kRingThreads * 8];
-  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int64_t* __restrict__ key_pos, const int64_t* __restrict__ pos, const int* __restrict__ slot32, int heads,
+    int hd, int ring, int window, int64_t slot_stride, float scale, bf16* __restrict__ out, int* status) {
+  extern __shared__ __align__(128) unsigned char rsm[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(rsm);
+  const uint32_t ring_bytes = (uint32_t)ring * hd * 2;
+  bf16* Ks = reinterpret_cast<bf16*>(rsm + 128);
+  bf16* Vs = reinterpret_cast<bf16*>(rsm + 128 + ring_bytes);
+  int64_t* kps = reinterpret_cast<int64_t*>(rsm + 128 + 2 * ring_bytes);  // [ring] key positions
+  float* sc = reinterpret_cast<float*>(kps + ring);                        // [T][ring]
+  float* wred = sc + T * ring;                                              // [warps][T][hd]
+  float* stat = wred + kRingWarps * T * hd;                                 // [T] (max, 1 / sum)
+  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = heads * hd;
   const int s = slot32[b];
-  const bf16* K = kring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
-  const bf16* V = vring + (int64_t)s * slot_stride + (int64_t)h * ring * hd;
-  for (int i = tid; i < T * hd; i += kRingThreads)
-    qs[i / hd][i % hd] = to_f(q[((int64_t)b * T + i / hd) * H + h * hd + i % hd]);
-  __syncthreads();
-  for (int r = tid; r < ring; r += kRingThreads) {
-    const int64_t kp = key_pos[(int64_t)s * ring + r];
-    const uint4* kr = reinterpret_cast<const uint4*>(K + (int64_t)r * hd);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < hd / 8; ++c) {
-      float kf[8];
-      unpack8(kr[c], kf);
-      for (int t = 0; t < T; ++t)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[t] = fmaf(qs[t][c * 8 + e], kf[e], acc[t]);
-    }
-    for (int t = 0; t < T; ++t) {
-      const int64_t p = pos[(int64_t)b * T + t];
-      const bool vis = kp <= p && kp > p - window;
-      sc[t][r] = vis ? acc[t] * scale : -INFINITY;
-    }
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
   }
   __syncthreads();
+  if (tid == 0) {
+    const int64_t off = (int64_t)s * slot_stride + (int64_t)h * ring * hd;
+    mbar_expect_tx(&bar[0], ring_bytes);
+    bulk_g2s(Ks, kring + off, ring_bytes, &bar[0]);
+    mbar_expect_tx(&bar[1], ring_bytes);
+    bulk_g2s(Vs, vring + off, ring_bytes, &bar[1]);
+  }
+  for (int r = tid; r < ring; r += kRingThreads) kps[r] = key_pos[(int64_t)s * ring + r];
+  const int LPR = hd / 8, RPW = 32 / LPR;  // lanes per ring entry, entries per warp step
+  const int c8 = lane % LPR, rsub = lane / LPR;
+  float qr[T][8];
+  int64_t pq[T];
+#pragma unroll
   for (int t = 0; t < T; ++t) {
-    float mx = -INFINITY;
-    for (int r = tid; r < ring; r += kRingThreads) mx = fmaxf(mx, sc[t][r]);
-    mx = block_max(mx, red);
-    float sum = 0.f;
+    unpack8(reinterpret_cast<const uint4*>(q + ((int64_t)b * T + t) * H + h * hd)[c8], qr[t]);
+    pq[t] = pos[(int64_t)b * T + t];
+  }
+  const bool kok = mbar_wait(&bar[0], 0, status);
+  if (__syncthreads_or(!kok)) {  // give up: let the V copy land (bounded) before the CTA exits
+    if (tid == 0) mbar_wait(&bar[1], 0, nullptr);
     __syncthreads();
-    for (int r = tid; r < ring; r += kRingThreads) {
-      const float e = sc[t][r] == -INFINITY ? 0.f : expf(sc[t][r] - mx);
-      sc[t][r] = e;
-      sum += e;
+    return;
+  }
+  for (int r0 = warp * RPW; r0 < ring; r0 += kRingWarps * RPW) {
+    const int r = r0 + rsub;
+    float kf[8];
+    unpack8(reinterpret_cast<const uint4*>(Ks + r * hd)[c8], kf);
+    float acc[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      acc[t] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[t] = fmaf(qr[t][e], kf[e], acc[t]);
     }
-    sum = block_sum(sum, red);
-    __syncthreads();
-    for (int r = tid; r < ring; r += kRingThreads) sc[t][r] /= sum;
+    for (int o = LPR / 2; o > 0; o >>= 1)
+#pragma unroll
+      for (int t = 0; t < T; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+    if (c8 == 0) {
+      const int64_t kp = kps[r];
+#pragma unroll
+      for (int t = 0; t < T; ++t) sc[t * ring + r] = (kp <= pq[t] && kp > pq[t] - window) ? acc[t] * scale : -INFINITY;
+    }
   }
   __syncthreads();
-  // weighted sum: pair = (query, 8-dim group); chunks of the ring per thread group
-  const int G8 = hd / 8, pairs = T * G8, chunks = kRingThreads / pairs;
-  const int pi = tid % pairs, ch = tid / pairs;
-  const int t = pi / G8, g = pi % G8;
-  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (ch < chunks)
-    for (int r = ch; r < ring; r += chunks) {
-      const float pr = sc[t][r];
-      float vf[8];
-      unpack8(reinterpret_cast<const uint4*>(V + (int64_t)r * hd)[g], vf);
+  if (warp < T) {
+    float mx = -INFINITY;
+    for (int r = lane; r < ring; r += 32) mx = fmaxf(mx, sc[warp * ring + r]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = fmaf(pr, vf[e], o[e]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int r = lane; r < ring; r += 32) {
+      const float v = sc[warp * ring + r];
+      sum += v == -INFINITY ? 0.f : expf(v - mx);
     }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      stat[2 * warp] = mx;
+      stat[2 * warp + 1] = sum > 0.f ? 1.f / sum : 0.f;
+    }
+  }
+  const bool vok = mbar_wait(&bar[1], 0, status);
+  if (__syncthreads_or(!vok)) return;
+  float o[T][8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) part[tid * 8 + e] = o[e];
+  for (int t = 0; t < T; ++t)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[t][e] = 0.f;
+  for (int r0 = warp * RPW; r0 < ring; r0 += kRingWarps * RPW) {
+    const int r = r0 + rsub;
+    float vf[8];
+    unpack8(reinterpret_cast<const uint4*>(Vs + r * hd)[c8], vf);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const float v = sc[t * ring + r];
+      const float pr = v == -INFINITY ? 0.f : expf(v - stat[2 * t]) * stat[2 * t + 1];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[t][e] = fmaf(pr, vf[e], o[t][e]);
+    }
+  }
+  for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[t][e] += __shfl_xor_sync(0xffffffffu, o[t][e], off);
+  if (rsub == 0)
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wred[(warp * T + t) * hd + c8 * 8 + e] = o[t][e];
   __syncthreads();
-  for (int i = tid; i < pairs * 8; i += kRingThreads) {
-    const int pp = i / 8, e = i % 8;
+  for (int i = tid; i < T * hd; i += kRingThreads) {
+    const int t = i / hd, d = i % hd;
     float v = 0.f;
-    for (int c = 0; c < chunks; ++c) v += part[(c * pairs + pp) * 8 + e];
-    const int tt = pp / G8, gg = pp % G8;
-    out[((int64_t)b * T + tt) * H + h * hd + gg * 8 + e] = to_bf(v);
+#pragma unroll
+    for (int w = 0; w < kRingWarps; ++w) v += wred[(w * T + t) * hd + d];
+    out[((int64_t)b * T + t) * H + h * hd + d] = to_bf(v);
   }
 }
 
@@ -414,10 +469,18 @@ __global__ void final_conv_kernel(const bf16* __restrict__ x, int L, int C, int 
   float* ws = fsm + (kFinalTile + P) * S;
   const bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;
   const int rows = min(kFinalTile, L - t0) + P;
-  for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
-    const int rr = i / C, c = i % C;
+  const int C8 = C / 8;
+  const uint4* hist8 = reinterpret_cast<const uint4*>(hist);
+  const uint4* x8 = reinterpret_cast<const uint4*>(x + (int64_t)b * L * C);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < rows * C8; i += blockDim.x) {  // 16-byte loads, several in flight per thread
+    const int rr = i / C8, c8 = i % C8;
     const int ji = t0 + rr;  // index into joined = [hist; elu(x)]
-    xs[rr * S + c] = ji < P ? to_f(hist[ji * C + c]) : rbf(elu(to_f(x[((int64_t)b * L + ji - P) * C + c])));
+    float f[8];
+    unpack8(ji < P ? hist8[ji * C8 + c8] : x8[(int64_t)(ji - P) * C8 + c8], f);
+    float* d = xs + rr * S + c8 * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) d[e] = ji < P ? f[e] : rbf(elu(f[e]));
   }
   for (int i = threadIdx.x; i < k * C; i += blockDim.x) ws[i] = to_f(w[i]);
   __syncthreads();
@@ -501,7 +564,10 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   M3_REQUIRE(c.n_ratios >= 1 && c.n_ratios <= 8, M3_ERR_ARG, "n_ratios %d", c.n_ratios);
   const int hd = c.hidden / c.heads;
   M3_REQUIRE(c.hidden % c.heads == 0 && hd % 8 == 0 && hd <= 128 && c.heads <= 32, M3_ERR_UNSUPPORTED, "head dim");
-  M3_REQUIRE(c.ring <= kRingMax && c.ring >= c.window + c.upsample_stride, M3_ERR_ARG, "ring %d", c.ring);
+  M3_REQUIRE(c.ring >= c.window + c.upsample_stride, M3_ERR_ARG, "ring %d", c.ring);
+  M3_REQUIRE((hd & (hd - 1)) == 0 && c.ring % (256 / hd) == 0 &&
+                 ring_attn_smem(c.upsample_stride, c.ring, hd) <= 227 * 1024,
+             M3_ERR_UNSUPPORTED, "ring %d x head dim %d unsupported by the ring attention", c.ring, hd);
   M3_REQUIRE(c.upsample_stride <= 4 && c.upsample_stride <= 8 && c.kernel - 1 <= 8 && c.res_kernel - 1 <= 8 &&
                  c.last_kernel - 1 <= 8,
              M3_ERR_UNSUPPORTED, "kernel sizes");
@@ -587,6 +653,13 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   m->tmp = carve<bf16>(p, act);
   m->z = carve<float>(p, zf);
   cudaMemset(m->status, 0, 256);
+  {
+    const int sm = (int)ring_attn_smem(c.upsample_stride, c.ring, hd);
+    cudaFuncSetAttribute(ring_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    cudaFuncSetAttribute(ring_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    cudaFuncSetAttribute(ring_attn_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  }
   *out = m;
   return M3_OK;
 }
@@ -666,18 +739,30 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   const int64_t rows_all = c.max_slots + 1;
   const int64_t slot_stride = (int64_t)c.heads * c.ring * hd;  // one slot's block inside kv[layer][k|v]
   const int64_t kv_half = rows_all * slot_stride;
-  add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, 1, H, 0, nullptr, nullptr, 0, nullptr, nullptr, m->y, m->ln1_w[0],
-                                     m->ln1_b[0], c.norm_eps, H);
-  M3_LAUNCHED();
+  M3_TRY(launch_add_ln(R * T, m->h, 1, H, 0, nullptr, nullptr, 0, nullptr, nullptr, m->y, m->ln1_w[0], m->ln1_b[0],
+                c.norm_eps, H, s));
   for (int li = 0; li < c.layers; ++li) {
     M3_TRY(gemm({m->y, H, m->wqkv[li], H, m->qkv, 3 * H, R * T, 3 * H, H, false}, s));
     bf16* kr = m->kv + (int64_t)li * 2 * kv_half;
     mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
                                                    m->q, kr, kr + kv_half, slot_stride);
     M3_LAUNCHED();
-    ring_attn_kernel<<<dim3(R, c.heads), kRingThreads, 0, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32, T,
-                                                       c.heads, hd, c.ring, c.window, slot_stride,
-                                                       1.f / sqrtf((float)hd), m->att);
+    {
+      const dim3 grid(R, c.heads);
+      const size_t sm = ring_attn_smem(T, c.ring, hd);
+      const float sc = 1.f / sqrtf((float)hd);
+#define M3_RING(TT)                                                                                              \
+  ring_attn_kernel<TT><<<grid, kRingThreads, sm, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32,    \
+                                                      c.heads, hd, c.ring, c.window, slot_stride, sc, m->att,    \
+                                                      m->status)
+      switch (T) {
+        case 1: M3_RING(1); break;
+        case 2: M3_RING(2); break;
+        case 3: M3_RING(3); break;
+        default: M3_RING(4); break;
+      }
+#undef M3_RING
+    }
     M3_LAUNCHED();
     M3_TRY(gemm({m->att, H, m->wo[li], H, m->ob, H, R * T, H, H, false}, s));
     scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls1[li], m->y, m->ln2_w[li], m->ln2_b[li], c.norm_eps,

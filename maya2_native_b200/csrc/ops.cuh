@@ -11,6 +11,11 @@ __global__ void add_ln_kernel(const bf16* __restrict__ src, int T, int64_t sb, i
                               const int* __restrict__ slot32, bf16* __restrict__ xout, bf16* __restrict__ y,
                               const bf16* __restrict__ w, const bf16* __restrict__ bias, float eps, int D);
 
+// add_ln_kernel over `rows` rows, one CTA per row (counts its launch).
+int launch_add_ln(int rows, const bf16* src, int T, int64_t sb, int64_t st, const bf16* a, const bf16* c,
+                   int64_t c_slot_stride, const int* slot32, bf16* xout, bf16* y, const bf16* w, const bf16* bias,
+                   float eps, int D, cudaStream_t s);
+
 // In place: f = bf16(gelu_erf(f)) over n8 groups of 8 elements.
 __global__ void gelu_kernel(bf16* __restrict__ f, int64_t n8);
 
