@@ -11,7 +11,9 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "mma.cuh"
 #include "ops.cuh"
+#include "tma.cuh"
 
 namespace m3 {
 
@@ -119,8 +121,8 @@ __global__ void mimi_rope_kernel(const bf16* __restrict__ qkv, const int64_t* __
 // a quarter-warp reads whole 128-byte rows, conflict-free); fp32 scores, softmax statistics by one warp per query,
 // weighted sum of V reduced over lanes and warps.  Every wait is bounded.
 constexpr int kRingThreads = 256;
+constexpr float kLazyRescale2 = 8.f;  // raise the running max only when a score exceeds it by 2^8
 constexpr int kRingWarps = kRingThreads / 32;
-constexpr int kRingMaxT = 4;
 
 inline size_t ring_attn_smem(int T, int ring, int hd) {
   return 128 + 2 * (size_t)ring * hd * 2 + (size_t)ring * 8 +
@@ -246,6 +248,184 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(
 #pragma unroll
     for (int w = 0; w < kRingWarps; ++w) v += wred[(w * T + t) * hd + d];
     out[((int64_t)b * T + t) * H + h * hd + d] = to_bf(v);
+  }
+}
+
+// Tensor-core form of the ring attention for head dims 32 and 64 (the decode attention's design, without splits):
+// one CTA of 4 warps per (row, head); the ring is cut into 16-entry blocks, warp w takes blocks w, w+4, ... through
+// its own 2-deep TMA ring (tensor maps over kv[layer][k|v] as [slot * heads + head][entry][head_dim]); S = Q K^T with
+// the T queries as mma rows, the key_pos window as the mask, online softmax in exp2, O^T += V^T P^T with P split into
+// bf16 hi + lo.  Every wait is bounded.
+constexpr int kRingBlk = 16;
+
+template <int HD>
+__device__ __forceinline__ uint32_t ring_off(int r, int c) {
+  if constexpr (HD == 64) return sw128(r, c);  // 128-byte rows, 128-byte swizzle
+  else return (uint32_t)(r * HD * 2 + c * 16);  // 64-byte rows, no swizzle
+}
+
+template <int HD>
+struct RingMmaSmem {
+  unsigned char stage[4][2][2 * kRingBlk * HD * 2];  // [warp][stage][K box | V box]
+  uint64_t bar[4][2];
+};
+
+template <int HD, int T>
+__global__ void __launch_bounds__(128) ring_mma_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
+    const int64_t* __restrict__ key_pos, const int64_t* __restrict__ pos, const int* __restrict__ slot32, int heads,
+    int ring, int window, float qscale, bf16* __restrict__ out, int* status) {
+  constexpr int BOX = kRingBlk * HD * 2, KS = HD / 16;
+  static_assert(T <= 8, "the queries fill at most 8 of the 16 mma rows");
+  extern __shared__ unsigned char smem_raw[];
+  RingMmaSmem<HD>& sm =
+      *reinterpret_cast<RingMmaSmem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int b = blockIdx.x, h = blockIdx.y, H = heads * HD;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int s = slot32[b];
+  const int zc = s * heads + h;
+  const int nblk = ring / kRingBlk;
+  const int nmine = warp < nblk ? (nblk - 1 - warp) / 4 + 1 : 0;
+  if (tid == 0) {
+    for (int w = 0; w < 4; ++w)
+      for (int st = 0; st < 2; ++st) mbar_init(&sm.bar[w][st], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {
+    unsigned char* st = sm.stage[warp][i & 1];
+    uint64_t* bar = &sm.bar[warp][i & 1];
+    const int y = (warp + 4 * i) * kRingBlk;
+    mbar_expect_tx(bar, 2 * BOX);
+    tma_load_3d(st, &kmap, 0, y, zc, bar);
+    tma_load_3d(st + BOX, &vmap, 0, y, zc, bar);
+  };
+  if (lane == 0)
+    for (int i = 0; i < min(2, nmine); ++i) issue(i);
+  uint32_t qa[KS][2];
+  {
+    const uint32_t* qp = reinterpret_cast<const uint32_t*>(q + ((int64_t)b * T + min(g, T - 1)) * H + h * HD);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      qa[ks][0] = g < T ? qp[8 * ks + t] : 0u;
+      qa[ks][1] = g < T ? qp[8 * ks + 4 + t] : 0u;
+    }
+  }
+  const int64_t pg = pos[(int64_t)b * T + min(g, T - 1)];
+  const int64_t* kps = key_pos + (int64_t)s * ring;
+  float o[KS][4];
+#pragma unroll
+  for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool timed_out = false;
+  int i = 0;
+  for (; i < nmine; ++i) {
+    const bool got = mbar_wait(&sm.bar[warp][i & 1], (i >> 1) & 1, status);
+    if (!__all_sync(0xffffffffu, got)) {
+      timed_out = true;
+      break;
+    }
+    const uint32_t kb = smem_u32(sm.stage[warp][i & 1]), vb = kb + BOX;
+    const int e0 = (warp + 4 * i) * kRingBlk;
+    const int j = lane >> 3, lr = ((j >> 1) << 3) + (lane & 7), lc = j & 1;
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t k0, k1, k2, k3;
+      ldsm_x4(kb + ring_off<HD>(lr, 2 * ks + lc), k0, k1, k2, k3);
+      mma_bf16(sc[0], qa[ks][0], 0u, qa[ks][1], 0u, k0, k1);
+      mma_bf16(sc[1], qa[ks][0], 0u, qa[ks][1], 0u, k2, k3);
+    }
+    float p[2][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t kp = kps[e0 + nt * 8 + 2 * t + e];
+        const bool vis = g < T && kp <= pg && kp > pg - window;
+        p[nt][e] = vis ? sc[nt][e] * qscale : -INFINITY;
+        mx = fmaxf(mx, p[nt][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float r = 1.f;
+    if (mx > m_run + kLazyRescale2) {
+      r = exp2f(m_run - mx);
+      m_run = mx;
+      l_run *= r;
+    }
+    if (__any_sync(0xffffffffu, r != 1.f)) {
+      const float r0 = __shfl_sync(0xffffffffu, r, 8 * t), r1 = __shfl_sync(0xffffffffu, r, 8 * t + 4);
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        o[mt][0] *= r0;
+        o[mt][1] *= r1;
+        o[mt][2] *= r0;
+        o[mt][3] *= r1;
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[nt][e] = p[nt][e] == -INFINITY ? 0.f : exp2f(p[nt][e] - m_run);
+        l_run += p[nt][e];
+      }
+    const uint32_t h0 = pack_bf2(p[0][0], p[0][1]), h1 = pack_bf2(p[1][0], p[1][1]);
+    const uint32_t l0 = pack_bf2(p[0][0] - bf_lo_f(h0), p[0][1] - bf_hi_f(h0));
+    const uint32_t l1 = pack_bf2(p[1][0] - bf_lo_f(h1), p[1][1] - bf_hi_f(h1));
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb + ring_off<HD>(lr, 2 * mt + lc), a0, a1, a2, a3);
+      mma_bf16(o[mt], a0, a1, a2, a3, h0, h1);
+      mma_bf16(o[mt], a0, a1, a2, a3, l0, l1);
+    }
+    __syncwarp();
+    if (lane == 0 && i + 2 < nmine) issue(i + 2);
+  }
+  if (timed_out) {  // drain this warp's copies in flight (bounded), publish an empty partial
+    if (lane == 0)
+      for (int k = i; k < min(nmine, i + 2); ++k) mbar_wait(&sm.bar[warp][k & 1], (k >> 1) & 1, nullptr);
+    __syncwarp();
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    m_run = -INFINITY;
+    l_run = 0.f;
+  }
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  float* wo = reinterpret_cast<float*>(sm.stage[warp][0]);  // [T][HD], then (m, l) per query
+  float* wml = wo + T * HD;
+#pragma unroll
+  for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int qh = 2 * t + (e & 1);
+      if (qh < T) wo[qh * HD + 16 * mt + g + ((e >> 1) << 3)] = o[mt][e];
+    }
+  if (t == 0 && g < T) {
+    wml[2 * g] = m_run;
+    wml[2 * g + 1] = l_run;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < T * HD; idx += 128) {
+    const int qh = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, reinterpret_cast<const float*>(sm.stage[w][0])[T * HD + 2 * qh]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* ww = reinterpret_cast<const float*>(sm.stage[w][0]);
+      const float mw = ww[T * HD + 2 * qh];
+      const float c = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      O = fmaf(ww[qh * HD + d], c, O);
+      L = fmaf(ww[T * HD + 2 * qh + 1], c, L);
+    }
+    out[((int64_t)b * T + qh) * H + h * HD + d] = to_bf(L > 0.f ? O / L : 0.f);
   }
 }
 
@@ -511,6 +691,8 @@ struct m3_mimi {
   std::vector<StageDims> stages;
   void* ws = nullptr;
   int *slot32 = nullptr, *status = nullptr;
+  std::vector<CUtensorMap> kmap, vmap;  // per layer, over kv[layer][k|v] as [slot * heads + head][entry][head_dim]
+  bool ring_mma = false;                // tensor-core ring attention (head dim 32 or 64, ring a multiple of 16)
   int64_t* pos = nullptr;
   bf16 *a_sem = nullptr, *a_ac = nullptr, *p_sem = nullptr, *p_ac = nullptr, *h = nullptr, *y = nullptr,
        *qkv = nullptr, *q = nullptr, *att = nullptr, *ob = nullptr, *ff = nullptr, *act0 = nullptr, *act1 = nullptr,
@@ -653,6 +835,43 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   m->tmp = carve<bf16>(p, act);
   m->z = carve<float>(p, zf);
   cudaMemset(m->status, 0, 256);
+  m->ring_mma = (hd == 32 || hd == 64) && c.ring % kRingBlk == 0 && c.upsample_stride <= 8;
+  if (m->ring_mma) {
+    EncodeTiled enc;
+    if (tensor_map_encoder(&enc) != M3_OK) {
+      cudaFree(m->ws);
+      delete m;
+      return M3_ERR_CUDA;
+    }
+    const int64_t rows_all = c.max_slots + 1;
+    const int64_t kv_half = rows_all * c.heads * c.ring * hd;
+    const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)c.ring, (cuuint64_t)(rows_all * c.heads)};
+    const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)c.ring * hd * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)hd, (cuuint32_t)kRingBlk, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    m->kmap.resize(c.layers);
+    m->vmap.resize(c.layers);
+    for (int li = 0; li < c.layers; ++li)
+      for (int kvv = 0; kvv < 2; ++kvv) {
+        bf16* base = m->kv + (int64_t)(2 * li + kvv) * kv_half;
+        const CUresult r = (reinterpret_cast<uintptr_t>(base) & 15)
+                               ? CUDA_ERROR_INVALID_VALUE
+                               : enc(kvv ? &m->vmap[li] : &m->kmap[li], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims,
+                                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                     hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+          cudaFree(m->ws);
+          delete m;
+          set_error("m3_mimi_create: ring tensor map of layer %d failed (%d); kv must be 16-byte aligned", li, (int)r);
+          return M3_ERR_ARG;
+        }
+      }
+    const int rs = (int)(sizeof(RingMmaSmem<64>) + 1024);
+    cudaFuncSetAttribute(ring_mma_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
+    cudaFuncSetAttribute(ring_mma_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
+    cudaFuncSetAttribute(ring_mma_kernel<64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
+  }
   {
     const int sm = (int)ring_attn_smem(c.upsample_stride, c.ring, hd);
     cudaFuncSetAttribute(ring_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
@@ -747,7 +966,20 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
                                                    m->q, kr, kr + kv_half, slot_stride);
     M3_LAUNCHED();
-    {
+    if (m->ring_mma && (T == 1 || T == 2 || T == 4)) {
+      const dim3 grid(R, c.heads);
+      const float qs = 1.4426950408889634f / sqrtf((float)hd);
+#define M3_RING_MMA(HDD, TT)                                                                                      \
+  ring_mma_kernel<HDD, TT><<<grid, 128, sizeof(RingMmaSmem<HDD>) + 1024, s>>>(                                    \
+      m->kmap[li], m->vmap[li], m->q, m->key_pos, m->pos, m->slot32, c.heads, c.ring, c.window, qs, m->att,        \
+      m->status)
+      if (hd == 64) {
+        if (T == 1) M3_RING_MMA(64, 1); else if (T == 2) M3_RING_MMA(64, 2); else M3_RING_MMA(64, 4);
+      } else {
+        if (T == 1) M3_RING_MMA(32, 1); else if (T == 2) M3_RING_MMA(32, 2); else M3_RING_MMA(32, 4);
+      }
+#undef M3_RING_MMA
+    } else {
       const dim3 grid(R, c.heads);
       const size_t sm = ring_attn_smem(T, c.ring, hd);
       const float sc = 1.f / sqrtf((float)hd);
