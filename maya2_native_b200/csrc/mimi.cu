@@ -13,6 +13,7 @@
 #include "gemm.cuh"
 #include "mma.cuh"
 #include "ops.cuh"
+#include "seanet.cuh"
 #include "tma.cuh"
 
 namespace m3 {
@@ -488,15 +489,6 @@ __global__ void tokens_advance_kernel(const int* __restrict__ slot32, int rows, 
 }
 
 // ------------------------------------------------------------------------------------------------ SEANet
-__device__ __forceinline__ float elu(float x) { return x > 0.f ? x : expm1f(x); }
-
-__device__ __forceinline__ uint4 elu8(const uint4& u) {
-  float f[8];
-  unpack8(u, f);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) f[e] = elu(f[e]);
-  return pack8(f);
-}
 
 // im2col of a causal stride-1 conv with k taps over joined = [history (k-1 stored rows); act(x)], act = ELU
 // (rounded) when elu_in: A[b*L + t, j*C + c] = joined[t + j][c].  One thread per (row, step, 8 channels); the
@@ -551,7 +543,8 @@ __global__ void conv_hist_kernel(const bf16* __restrict__ x, int L, int C, int k
   }
 }
 
-// y = bf16(z + bias); mode 1: y = bf16(elu(y)); mode 2: y = bf16(res + y).  Eight elements per thread.
+// y = bf16(z + bias); mode 1: y = bf16(elu(y)); mode 2: y = bf16(res + y); mode 3: y = bf16(elu(bf16(res + y))).
+// Eight elements per thread (y may alias res).
 __global__ void bias_epilogue_kernel(const float* __restrict__ z, const bf16* __restrict__ bias, int64_t M, int N,
                                      int mode, const bf16* __restrict__ res, bf16* __restrict__ y) {
   const int64_t i8 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -560,12 +553,13 @@ __global__ void bias_epilogue_kernel(const float* __restrict__ z, const bf16* __
   const float4 z0 = reinterpret_cast<const float4*>(z)[2 * i8], z1 = reinterpret_cast<const float4*>(z)[2 * i8 + 1];
   float v[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w}, bv[8], rv[8];
   unpack8(*reinterpret_cast<const uint4*>(bias + n0), bv);
-  if (mode == 2) unpack8(reinterpret_cast<const uint4*>(res)[i8], rv);
+  if (mode >= 2) unpack8(reinterpret_cast<const uint4*>(res)[i8], rv);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     v[e] = rbf(v[e] + bv[e]);
     if (mode == 1) v[e] = elu(v[e]);
-    if (mode == 2) v[e] = rv[e] + v[e];
+    if (mode >= 2) v[e] = rv[e] + v[e];
+    if (mode == 3) v[e] = elu(rbf(v[e]));
   }
   reinterpret_cast<uint4*>(y)[i8] = pack8(v);
 }
@@ -641,7 +635,7 @@ constexpr int kFinalTile = 128;
 __global__ void final_conv_kernel(const bf16* __restrict__ x, int L, int C, int k, const bf16* __restrict__ w,
                                   const bf16* __restrict__ bias, const int* __restrict__ slot32,
                                   const bf16* __restrict__ state, int64_t state_row, int64_t hist_off,
-                                  float* __restrict__ pcm) {
+                                  float* __restrict__ pcm, int elu_x) {
   extern __shared__ float fsm[];
   const int b = blockIdx.x, t0 = blockIdx.y * kFinalTile;
   const int P = k - 1, S = C + 1;  // padded stride: conflict-free column reads
@@ -660,7 +654,7 @@ __global__ void final_conv_kernel(const bf16* __restrict__ x, int L, int C, int 
     unpack8(ji < P ? hist8[ji * C8 + c8] : x8[(int64_t)(ji - P) * C8 + c8], f);
     float* d = xs + rr * S + c8 * 8;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) d[e] = ji < P ? f[e] : rbf(elu(f[e]));
+    for (int e = 0; e < 8; ++e) d[e] = (ji < P || !elu_x) ? f[e] : rbf(elu(f[e]));
   }
   for (int i = threadIdx.x; i < k * C; i += blockDim.x) ws[i] = to_f(w[i]);
   __syncthreads();
@@ -692,6 +686,14 @@ struct m3_mimi {
   void* ws = nullptr;
   int *slot32 = nullptr, *status = nullptr;
   std::vector<CUtensorMap> kmap, vmap;  // per layer, over kv[layer][k|v] as [slot * heads + head][entry][head_dim]
+  // fused SEANet stages (a suffix of the stages: first_fused .. n_ratios-1)
+  int first_fused = 1 << 30;
+  std::vector<ConvTFused> ct;
+  std::vector<ResFused> rs;
+  StateCopy snap_regions{};
+  int64_t snap_row = 0;
+  void* fws = nullptr;  // repacked transposed-conv weights + the state snapshot
+  bf16* snap = nullptr;
   bool ring_mma = false;                // tensor-core ring attention (head dim 32 or 64, ring a multiple of 16)
   int64_t* pos = nullptr;
   bf16 *a_sem = nullptr, *a_ac = nullptr, *p_sem = nullptr, *p_ac = nullptr, *h = nullptr, *y = nullptr,
@@ -738,6 +740,112 @@ extern "C" int64_t m3_mimi_state_elems(const m3_mimi_config* cfg) {
   if (!cfg || cfg->n_ratios < 1 || cfg->n_ratios > 8) return -1;
   int64_t a, b, c;
   return plan(*cfg, nullptr, &a, &b, &c);
+}
+
+// Pick the SEANet stages that run fused (the longest suffix of stages whose shapes the fused kernels support) and
+// build what they need: repacked transposed-conv weights, the state snapshot layout, and tensor maps over the two
+// activation buffers (stage input e in act0 -> transposed-conv output u in act1 -> residual-block output in act0).
+static int setup_fused_seanet(m3_mimi* m) {
+  const m3_mimi_config& c = m->c;
+  const int n = (int)m->stages.size();
+  auto fusable = [&](const StageDims& sd) {
+    const int hid = sd.cout / c.compress;
+    return c.res_kernel == 3 && sd.L >= 16 && convt_fused_ok(sd.cin, sd.cout, sd.r) && res_fused_ok(sd.cout, hid) &&
+           sd.tail_off % 8 == 0 && sd.hist_off % 8 == 0 && (sd.r * sd.cout) % 8 == 0;
+  };
+  int first = n;
+  while (first > 0 && fusable(m->stages[first - 1])) --first;
+  if (first == n || m->state_row % 8 != 0 || n - first > 8) return M3_OK;
+  EncodeTiled enc;
+  M3_TRY(tensor_map_encoder(&enc));
+  size_t wbytes = 0;
+  StateCopy sc{};
+  int64_t srow = 0;
+  for (int i = first; i < n; ++i) {
+    const StageDims& sd = m->stages[i];
+    wbytes += (size_t)sd.r * sd.cout * 2 * sd.cin * 2;
+    sc.off[sc.n] = sd.tail_off;
+    sc.len[sc.n] = sd.r * sd.cout;
+    sc.dst_off[sc.n++] = srow;
+    srow += sd.r * sd.cout;
+    sc.off[sc.n] = sd.hist_off;
+    sc.len[sc.n] = 2 * sd.cout;
+    sc.dst_off[sc.n++] = srow;
+    srow += 2 * sd.cout;
+  }
+  wbytes = (wbytes + 255) / 256 * 256;
+  const size_t snap_bytes = (size_t)c.max_rows * srow * 2;
+  M3_CUDA(cudaMalloc(&m->fws, wbytes + snap_bytes));
+  bf16* wc = (bf16*)m->fws;
+  bf16* snap = (bf16*)((char*)m->fws + wbytes);
+  M3_TRY(seanet_fused_init());
+  auto map3 = [&](CUtensorMap* map, bf16* base, int ch, int steps, int box_rows) -> int {
+    const cuuint64_t dims[3] = {(cuuint64_t)ch, (cuuint64_t)steps, (cuuint64_t)c.max_rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)ch * 2, (cuuint64_t)steps * ch * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    M3_REQUIRE(r == CUDA_SUCCESS, M3_ERR_CUDA, "SEANet tensor map failed (%d)", (int)r);
+    return M3_OK;
+  };
+  int si = 0;
+  for (int i = first; i < n; ++i, si += 2) {
+    const StageDims& sd = m->stages[i];
+    ConvTFused ct{};
+    M3_TRY(map3(&ct.amap, m->act0, sd.cin, sd.L, 128));
+    ct.wc = wc;
+    M3_TRY(launch_convt_repack(m->convt_w[i], sd.r, sd.cout, sd.cin, wc, 0));
+    {
+      const int N = sd.r * sd.cout, K = 2 * sd.cin;
+      const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+      const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+      const cuuint32_t box[2] = {64, (cuuint32_t)convt_fused_bn(N)};
+      const cuuint32_t estr[2] = {1, 1};
+      const CUresult r = enc(&ct.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wc, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      M3_REQUIRE(r == CUDA_SUCCESS, M3_ERR_CUDA, "SEANet weight tensor map failed (%d)", (int)r);
+    }
+    wc += (size_t)sd.r * sd.cout * 2 * sd.cin;
+    ct.bias = m->convt_b[i];
+    ct.tail_in = snap + sc.dst_off[si];
+    ct.in_row = srow;
+    ct.state = m->state;
+    ct.state_row = m->state_row;
+    ct.tail_off = sd.tail_off;
+    ct.slot32 = m->slot32;
+    ct.u = m->act1;
+    ct.L = sd.L;
+    ct.r = sd.r;
+    ct.cin = sd.cin;
+    ct.cout = sd.cout;
+    ResFused rs{};
+    M3_TRY(map3(&rs.umap, m->act1, sd.cout, sd.L * sd.r, 130));
+    rs.w1 = m->res1_w[i];
+    rs.b1 = m->res1_b[i];
+    rs.w2 = m->res2_w[i];
+    rs.b2 = m->res2_b[i];
+    rs.hist_in = snap + sc.dst_off[si + 1];
+    rs.in_row = srow;
+    rs.state = m->state;
+    rs.state_row = m->state_row;
+    rs.hist_off = sd.hist_off;
+    rs.slot32 = m->slot32;
+    rs.e = m->act0;
+    rs.Lo = sd.L * sd.r;
+    rs.cout = sd.cout;
+    rs.hid = sd.cout / c.compress;
+    m->ct.push_back(ct);
+    m->rs.push_back(rs);
+  }
+  M3_CUDA(cudaDeviceSynchronize());  // the weight repack finished before the first decode
+  m->first_fused = first;
+  m->snap_regions = sc;
+  m->snap_row = srow;
+  m->snap = snap;
+  return M3_OK;
 }
 
 extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* w, m3_mimi** out) {
@@ -879,6 +987,10 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
     cudaFuncSetAttribute(ring_attn_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
     cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   }
+  if (const int rc = setup_fused_seanet(m); rc != M3_OK) {
+    m3_mimi_destroy(m);
+    return rc;
+  }
   *out = m;
   return M3_OK;
 }
@@ -886,6 +998,7 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
 extern "C" int m3_mimi_destroy(m3_mimi* m) {
   if (!m) return M3_OK;
   cudaFree(m->ws);
+  if (m->fws) cudaFree(m->fws);
   delete m;
   return M3_OK;
 }
@@ -1024,13 +1137,22 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
                true},
               s));
   int64_t n = (int64_t)R * T * C0 / 8;
-  bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->conv0_b, (int64_t)R * T, C0, 0, nullptr,
-                                                                   m->act0);
+  const int nst = c.n_ratios, first_fused = std::min(m->first_fused, nst);
+  bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->conv0_b, (int64_t)R * T, C0,
+                                                                   first_fused == 0 ? 1 : 0, nullptr, m->act0);
   M3_LAUNCHED();
+  if (first_fused < nst)  // the fused stages read their previous state from a snapshot and rewrite it in place
+    M3_TRY(launch_state_snapshot(m->state, m->state_row, m->slot32, R, m->snap_regions, m->snap, m->snap_row, s));
   bf16* x = m->act0;
   bf16* other = m->act1;
-  for (int i = 0; i < c.n_ratios; ++i) {
+  for (int i = 0; i < nst; ++i) {
     const StageDims& sd = m->stages[i];
+    if (i >= first_fused) {  // e (act0) -> transposed conv -> u (act1) -> residual block -> next e (act0)
+      M3_TRY(launch_convt_fused(m->ct[i - first_fused], R, s, m->status));
+      M3_TRY(launch_res_fused(m->rs[i - first_fused], R, s, m->status));
+      x = m->act0;
+      continue;
+    }
     const int64_t Min = (int64_t)R * sd.L, Mout = Min * sd.r;
     // ELU -> ConvTranspose1d as X . Wt^T (fp32 contributions) -> fold with the overlap tail
     elu_kernel<<<(unsigned)((Min * sd.cin / 8 + 255) / 256), 256, 0, s>>>(x, m->tmp, Min * sd.cin / 8);
@@ -1064,6 +1186,14 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     M3_LAUNCHED();
     M3_TRY(gemm({m->tmp, hid, m->res2_w[i], hid, m->z, sd.cout, (int)Mout, sd.cout, hid, true}, s));
     n = Mout * sd.cout / 8;
+    if (i + 1 == first_fused && first_fused < nst) {  // the next stage is fused: hand it e = ELU(y) in act0 (in place when x is act0)
+      bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res2_b[i], Mout, sd.cout, 3, x,
+                                                                       m->act0);
+      M3_LAUNCHED();
+      x = m->act0;
+      other = m->act1;
+      continue;
+    }
     bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res2_b[i], Mout, sd.cout, 2, x, other);
     M3_LAUNCHED();
     std::swap(x, other);
@@ -1072,11 +1202,12 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   const int Lf = last.L * last.r;
   const size_t fsmem = ((size_t)(kFinalTile + c.last_kernel - 1) * (c.num_filters + 1) +
                         (size_t)c.last_kernel * c.num_filters) * sizeof(float);
+  const int elu_x = first_fused < nst ? 0 : 1;  // the fused stages hand over ELU(y)
   final_conv_kernel<<<dim3(R, cdiv(Lf, kFinalTile)), kFinalTile, fsmem, s>>>(
       x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32, m->state, m->state_row, m->final_off,
-      pcm);
+      pcm, elu_x);
   M3_LAUNCHED();
-  conv_hist_kernel<<<dim3(R, cdiv(c.num_filters / 8, 128)), 128, 0, s>>>(x, Lf, c.num_filters, c.last_kernel, 1,
+  conv_hist_kernel<<<dim3(R, cdiv(c.num_filters / 8, 128)), 128, 0, s>>>(x, Lf, c.num_filters, c.last_kernel, elu_x,
                                                                           m->slot32, m->state, m->state_row,
                                                                           m->final_off);
   M3_LAUNCHED();

@@ -19,6 +19,17 @@ int launch_add_ln(int rows, const bf16* src, int T, int64_t sb, int64_t st, cons
 // In place: f = bf16(gelu_erf(f)) over n8 groups of 8 elements.
 __global__ void gelu_kernel(bf16* __restrict__ f, int64_t n8);
 
+// ELU (alpha 1) of nn.ELU; elu8 applies it to 8 packed bf16 values and rounds each result to bf16.
+__device__ __forceinline__ float elu(float x) { return x > 0.f ? x : expm1f(x); }
+
+__device__ __forceinline__ uint4 elu8(const uint4& u) {
+  float f[8];
+  unpack8(u, f);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) f[e] = elu(f[e]);
+  return pack8(f);
+}
+
 inline int norm_block(int D) { return D / 8 < 32 ? 32 : (D / 8 > 1024 ? 1024 : (D / 8 + 31) / 32 * 32); }
 
 }  // namespace m3

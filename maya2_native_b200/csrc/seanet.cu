@@ -1,0 +1,446 @@
+// Fused SEANet decoder stages on the tensor cores (replace, for the long low-channel stages, the chain
+// ELU -> GEMM -> fp32 partials -> overlap fold -> im2col -> GEMM -> bias/ELU -> GEMM -> bias/residual of
+// serve/fast_codec.py:104-132 with two kernels per stage whose intermediates never leave the SM).
+//
+// Both kernels are persistent (a CTA per SM walks a strided list of 64-row tiles), keep their weight slice resident
+// in shared memory (rows padded by 16 bytes so ldmatrix reads are conflict-free), and double-buffer the activation
+// tiles, which arrive by TMA (3-D tensor maps [stream][step][channel], 64-channel boxes, 128-byte swizzle; causal
+// taps are row-shifted boxes, and rows before the first or after the last step of a stream read as zeros).  The
+// arithmetic is mma.sync m16n8k16 (bf16 operands, fp32 accumulation) with the reference's bf16 rounding points in the
+// epilogues.  All waits are bounded; a CTA that gives up drains its copies and reports M3_DEV_TIMEOUT.
+#include <algorithm>
+
+#include "mma.cuh"
+#include "ops.cuh"
+#include "seanet.cuh"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace m3 {
+
+namespace {
+constexpr int kUM = 128;                                // transposed conv: output rows per tile (tcgen05 M)
+constexpr int kBM = 128;                                // residual block: output rows per tile (8 warps x 16)
+constexpr int kResThreads = 256;
+constexpr int kResRows = kBM + 2;                       // residual-block tile rows incl. 2 causal history rows
+constexpr uint32_t kResBox = (kResRows * 128 + 1023) / 1024 * 1024;  // 130-row box, padded to the swizzle atom
+int g_sms = 0;
+uint16_t* g_elu_lut = nullptr;  // bf16 ELU of the negative bf16 patterns (one per process; device of the first init)
+
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
+}
+
+// output columns per transposed-conv CTA: the whole row when it fits one MMA (N <= 256), else 128
+int convt_bn(int N) { return N <= 256 ? N : 128; }
+int convt_stages(int bn) { return bn > 128 ? 2 : 3; }
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ transposed conv
+// Output rows t = t0 .. t0+127 of one stream (t = 0..L) against BN output columns: A = the 2-tap rows
+// [e[t-1], e[t]] (two row-shifted TMA boxes per 64-channel chunk; rows -1 and L read as zeros), B = Wc rows, on
+// tcgen05 (one thread issues the MMAs, fp32 accumulators in TMEM, a STAGES-deep TMA ring).  Epilogue (warp w owns
+// TMEM lanes 32w..32w+31 = rows): bf16(z + bias); row 0 adds the previous frame's tail after rounding, as the
+// streaming reference does; row L becomes the next tail bf16(bf16(z + b) - b).
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(128) convt_umma_kernel(
+    const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, const bf16* __restrict__ bias,
+    const bf16* __restrict__ tail_in, int64_t in_row, bf16* __restrict__ state, int64_t state_row, int64_t tail_off,
+    const int* __restrict__ slot32, bf16* __restrict__ u, int L, int r, int cin, int cout, int* status) {
+  constexpr int kA = kUM * 64 * 2, kB = BN * 64 * 2, kStage = kA + kB;
+  constexpr int kCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  const int n0 = blockIdx.x * BN, t0 = blockIdx.y * kUM, b = blockIdx.z;
+  const int N = r * cout, KT = 2 * cin / 64, CB = cin / 64;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * kStage);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES) ok = mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1, status);
+      if (!ok) break;
+      unsigned char* st = base + s * kStage;
+      mbar_expect_tx(&full[s], kStage);
+      tma_load_3d(st, &amap, (kt % CB) * 64, t0 - 1 + kt / CB, b, &full[s]);
+      tma_load_2d(st + kA, &bmap, kt * 64, n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    constexpr uint32_t idesc = umma_idesc(BN);
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int s = kt % STAGES;
+      ok = mbar_wait(&full[s], (kt / STAGES) & 1, status);
+      if (!ok) break;
+      tmem_fence_after();
+      const unsigned char* st = base + s * kStage;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_f16(tmem, sw128_desc(st + kk * 32), sw128_desc(st + kA + kk * 32), idesc, (kt | kk) != 0);
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);
+  }
+  __syncwarp();
+  ok = mbar_wait(done, 0, status) && ok;
+  tmem_fence_after();
+  const int t = t0 + warp * 32 + lane;
+  bf16* st = state + (int64_t)slot32[b] * state_row + tail_off;
+  if (ok) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t acc[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, acc);
+      if (t > L) continue;
+      const int n = n0 + c0, co0 = n % cout;  // a 32-column chunk never crosses a cout block (cout % 32 == 0)
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float bv[8], v[8];
+        unpack8(*reinterpret_cast<const uint4*>(bias + co0 + j), bv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = rbf(__uint_as_float(acc[j + e]) + bv[e]);
+        if (t == L) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = v[e] - bv[e];
+          *reinterpret_cast<uint4*>(st + n + j) = pack8(v);
+          continue;
+        }
+        if (t == 0) {
+          float tv[8];
+          unpack8(*reinterpret_cast<const uint4*>(tail_in + (int64_t)b * in_row + n + j), tv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = v[e] + tv[e];
+        }
+        *reinterpret_cast<uint4*>(u + ((int64_t)b * L + t) * N + n + j) = pack8(v);
+      }
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------------ residual block
+// ELU of a bf16 value by table: every ELU input in the block is an exact bf16 number, so the rounded result
+// bf16(ELU(x)) is a function of the 16 input bits.  x >= 0 maps to itself; negative x with |x| < 8 (15-bit magnitude
+// pattern below kEluLut) reads the table, filled once from expm1f exactly as the elementwise kernels compute it;
+// |x| >= 8 rounds to -1 (e^x < 2^-9); NaN stays NaN.
+constexpr int kEluLut = 0x4100;
+
+__device__ __forceinline__ uint32_t elu_bits(uint32_t h, const uint16_t* lut) {
+  if (!(h & 0x8000u)) return h;
+  const uint32_t i = h & 0x7FFFu;
+  if (i < (uint32_t)kEluLut) return lut[i];
+  return i > 0x7F80u ? h : 0xBF80u;
+}
+__device__ __forceinline__ uint32_t elu2(uint32_t v, const uint16_t* lut) {
+  return elu_bits(v & 0xFFFFu, lut) | (elu_bits(v >> 16, lut) << 16);
+}
+
+__global__ void elu_lut_kernel(uint16_t* __restrict__ lut) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kEluLut) return;
+  const float x = __uint_as_float(((uint32_t)i | 0x8000u) << 16);
+  const __nv_bfloat16 y = __float2bfloat16_rn(elu(x));
+  lut[i] = *reinterpret_cast<const uint16_t*>(&y);
+}
+
+// e = ELU(u + b2 + W2 . ELU(b1 + W1 . [ELU(u)[t-2], ELU(u)[t-1], ELU(u)[t]])) for 128 rows per tile, one warp per
+// 16 rows (8 warps): the first GEMM's accumulators become the second GEMM's A fragments in registers.  Values
+// between the steps stay as packed bf16 pairs, each rounding point is one paired conversion.
+template <int COUT, int HID>
+__global__ void __launch_bounds__(kResThreads) res_fused_kernel(
+    const __grid_constant__ CUtensorMap umap, const bf16* __restrict__ w1, const bf16* __restrict__ b1,
+    const bf16* __restrict__ w2, const bf16* __restrict__ b2, const bf16* __restrict__ hist_in, int64_t in_row,
+    bf16* __restrict__ state, int64_t state_row, int64_t hist_off, const int* __restrict__ slot32,
+    bf16* __restrict__ e, int Lo, int R, const uint16_t* __restrict__ elu_lut, int* status) {
+  constexpr int CB = COUT / 64, K1 = 3 * COUT, NT1 = HID / 8, NT2 = COUT / 8;
+  static_assert(COUT % 64 == 0 && HID % 16 == 0, "channel counts");
+  const int tps = (Lo + kBM - 1) / kBM;
+  const int total = R * tps;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* raw = align1024(smem_raw);                  // [2][CB][kResBox] u as loaded
+  unsigned char* ea = raw + 2 * CB * kResBox;                // [CB][kResBox] ELU(u), history rows patched in
+  bf16* W1 = reinterpret_cast<bf16*>(ea + CB * kResBox);    // [HID][K1 + 8]
+  bf16* W2 = W1 + HID * (K1 + 8);                            // [COUT][HID + 8]
+  uint16_t* lut = reinterpret_cast<uint16_t*>(W2 + COUT * (HID + 8));  // [kEluLut]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(lut + kEluLut);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tq = lane & 3, jm = lane >> 3;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < HID * (K1 / 8); i += kResThreads) {
+    const int rr = i / (K1 / 8), c8 = i % (K1 / 8);
+    *reinterpret_cast<uint4*>(W1 + rr * (K1 + 8) + c8 * 8) =
+        *reinterpret_cast<const uint4*>(w1 + (int64_t)rr * K1 + c8 * 8);
+  }
+  for (int i = tid; i < COUT * (HID / 8); i += kResThreads) {
+    const int rr = i / (HID / 8), c8 = i % (HID / 8);
+    *reinterpret_cast<uint4*>(W2 + rr * (HID + 8) + c8 * 8) =
+        *reinterpret_cast<const uint4*>(w2 + (int64_t)rr * HID + c8 * 8);
+  }
+  for (int i = tid; i < kEluLut / 8; i += kResThreads)
+    reinterpret_cast<uint4*>(lut)[i] = reinterpret_cast<const uint4*>(elu_lut)[i];
+  // this thread's bias columns: epilogue 1 (columns kk*16 + 2tq (+1), +8), epilogue 2 (columns ni*8 + 2tq (+1))
+  float bias1[HID / 16][4], bias2[NT2][2];
+#pragma unroll
+  for (int kk = 0; kk < HID / 16; ++kk) {
+    const int c0 = kk * 16 + 2 * tq;
+    bias1[kk][0] = to_f(b1[c0]);
+    bias1[kk][1] = to_f(b1[c0 + 1]);
+    bias1[kk][2] = to_f(b1[c0 + 8]);
+    bias1[kk][3] = to_f(b1[c0 + 9]);
+  }
+#pragma unroll
+  for (int ni = 0; ni < NT2; ++ni) {
+    bias2[ni][0] = to_f(b2[ni * 8 + 2 * tq]);
+    bias2[ni][1] = to_f(b2[ni * 8 + 2 * tq + 1]);
+  }
+  __syncthreads();
+  auto issue = [&](int tile, int buf) {
+    const int b = tile / tps, t0 = (tile % tps) * kBM;
+    mbar_expect_tx(&bar[buf], CB * kResRows * 128);
+    for (int cb = 0; cb < CB; ++cb)
+      tma_load_3d(raw + (buf * CB + cb) * kResBox, &umap, cb * 64, t0 - 2, b, &bar[buf]);
+  };
+  if (tid == 0 && blockIdx.x < total) issue(blockIdx.x, 0);
+  int it = 0;
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+    const int buf = it & 1;
+    const bool more = tile + gridDim.x < total;
+    if (tid == 0 && more) issue(tile + gridDim.x, buf ^ 1);
+    const bool ok = mbar_wait(&bar[buf], (it >> 1) & 1, status);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        mbar_wait(&bar[buf], (it >> 1) & 1, nullptr);
+        if (more) mbar_wait(&bar[buf ^ 1], ((it + 1) >> 1) & 1, nullptr);
+      }
+      __syncthreads();
+      return;
+    }
+    const int b = tile / tps, t0 = (tile % tps) * kBM;
+    const unsigned char* rb = raw + buf * CB * kResBox;
+    // ELU of the tile (an elementwise pass: the swizzled layout is the same in both buffers)
+    for (int i = tid; i < CB * kResRows * 8; i += kResThreads) {
+      const int cb = i / (kResRows * 8), off = (i % (kResRows * 8)) * 16;
+      uint4 v = *reinterpret_cast<const uint4*>(rb + cb * kResBox + off);
+      v.x = elu2(v.x, lut);
+      v.y = elu2(v.y, lut);
+      v.z = elu2(v.z, lut);
+      v.w = elu2(v.w, lut);
+      *reinterpret_cast<uint4*>(ea + cb * kResBox + off) = v;
+    }
+    __syncthreads();
+    if (t0 == 0) {  // rows t = -2, -1: the previous frame's ELU'd history
+      for (int i = tid; i < 2 * (COUT / 8); i += kResThreads) {
+        const int rr = i / (COUT / 8), c8 = i % (COUT / 8);
+        *reinterpret_cast<uint4*>(ea + (c8 / 8) * kResBox + sw128(rr, c8 % 8)) =
+            *reinterpret_cast<const uint4*>(hist_in + (int64_t)b * in_row + rr * COUT + c8 * 8);
+      }
+      __syncthreads();
+    }
+    // the new history: ELU(u) rows Lo-2 and Lo-1 of this frame
+    for (int hr = 0; hr < 2; ++hr) {
+      const int t = Lo - 2 + hr;
+      if (t < t0 || t >= t0 + kBM) continue;
+      bf16* dst = state + (int64_t)slot32[b] * state_row + hist_off + hr * COUT;
+      for (int c8 = tid; c8 < COUT / 8; c8 += kResThreads)
+        *reinterpret_cast<uint4*>(dst + c8 * 8) =
+            *reinterpret_cast<const uint4*>(ea + (c8 / 8) * kResBox + sw128(t - t0 + 2, c8 % 8));
+    }
+    // GEMM 1: 16 rows x HID over K1 = 3 taps x COUT
+    const int m0 = warp * 16;
+    float acc1[NT1][4];
+#pragma unroll
+    for (int n = 0; n < NT1; ++n) acc1[n][0] = acc1[n][1] = acc1[n][2] = acc1[n][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int cb = 0; cb < CB; ++cb) {
+        const uint32_t eb = smem_u32(ea + cb * kResBox);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(eb + sw128(m0 + j + (jm & 1) * 8 + (lane & 7), 2 * kk + (jm >> 1)), a0, a1, a2, a3);
+#pragma unroll
+          for (int nj = 0; nj < NT1 / 2; ++nj) {
+            const int n = nj * 16 + ((jm >> 1) << 3) + (lane & 7);
+            uint32_t q0, q1, q2, q3;
+            ldsm_x4(smem_u32(W1 + n * (K1 + 8) + j * COUT + cb * 64 + kk * 16 + (jm & 1) * 8), q0, q1, q2, q3);
+            mma_bf16(acc1[2 * nj], a0, a1, a2, a3, q0, q1);
+            mma_bf16(acc1[2 * nj + 1], a0, a1, a2, a3, q2, q3);
+          }
+        }
+      }
+    // bf16(ELU(bf16(z + b1))) -> the A fragments of GEMM 2 (k = HID)
+    uint32_t a2f[HID / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < HID / 16; ++kk) {
+      const float* lo = acc1[2 * kk];
+      const float* hi = acc1[2 * kk + 1];
+      a2f[kk][0] = elu2(pack_bf2(lo[0] + bias1[kk][0], lo[1] + bias1[kk][1]), lut);
+      a2f[kk][1] = elu2(pack_bf2(lo[2] + bias1[kk][0], lo[3] + bias1[kk][1]), lut);
+      a2f[kk][2] = elu2(pack_bf2(hi[0] + bias1[kk][2], hi[1] + bias1[kk][3]), lut);
+      a2f[kk][3] = elu2(pack_bf2(hi[2] + bias1[kk][2], hi[3] + bias1[kk][3]), lut);
+    }
+    // GEMM 2: 16 rows x COUT over K = HID
+    float acc2[NT2][4];
+#pragma unroll
+    for (int n = 0; n < NT2; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HID / 16; ++kk)
+#pragma unroll
+      for (int nj = 0; nj < NT2 / 2; ++nj) {
+        const int n = nj * 16 + ((jm >> 1) << 3) + (lane & 7);
+        uint32_t q0, q1, q2, q3;
+        ldsm_x4(smem_u32(W2 + n * (HID + 8) + kk * 16 + (jm & 1) * 8), q0, q1, q2, q3);
+        mma_bf16(acc2[2 * nj], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q0, q1);
+        mma_bf16(acc2[2 * nj + 1], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q2, q3);
+      }
+    // y = bf16(u + bf16(z + b2)); e = bf16(ELU(y))
+#pragma unroll
+    for (int ni = 0; ni < NT2; ++ni)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int m = m0 + g + 8 * hf, t = t0 + m;
+        if (t >= Lo) continue;
+        const int co = ni * 8 + 2 * tq;
+        const uint32_t uu =
+            *reinterpret_cast<const uint32_t*>(rb + (co / 64) * kResBox + sw128(m + 2, (co % 64) / 8) + (co % 8) * 2);
+        const uint32_t z = pack_bf2(acc2[ni][2 * hf] + bias2[ni][0], acc2[ni][2 * hf + 1] + bias2[ni][1]);
+        const uint32_t y = pack_bf2(bf_lo_f(uu) + bf_lo_f(z), bf_hi_f(uu) + bf_hi_f(z));
+        *reinterpret_cast<uint32_t*>(e + ((int64_t)b * Lo + t) * COUT + co) = elu2(y, lut);
+      }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ state snapshot
+__global__ void state_snapshot_kernel(const bf16* __restrict__ state, int64_t state_row,
+                                      const int* __restrict__ slot32, StateCopy c, bf16* __restrict__ snap,
+                                      int64_t snap_row) {
+  const int b = blockIdx.x;
+  const bf16* src = state + (int64_t)slot32[b] * state_row;
+  bf16* dst = snap + (int64_t)b * snap_row;
+  for (int q = 0; q < c.n; ++q)
+    for (int i = threadIdx.x; i < c.len[q] / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst + c.dst_off[q])[i] = reinterpret_cast<const uint4*>(src + c.off[q])[i];
+}
+
+__global__ void convt_repack_kernel(const bf16* __restrict__ wt, int r, int cout, int cin, bf16* __restrict__ wc) {
+  const int n = blockIdx.x;  // jj * cout + o
+  const int jj = n / cout, o = n % cout;
+  for (int k = threadIdx.x; k < 2 * cin; k += blockDim.x)
+    wc[(int64_t)n * 2 * cin + k] =
+        k < cin ? wt[((int64_t)(jj + r) * cout + o) * cin + k] : wt[((int64_t)jj * cout + o) * cin + (k - cin)];
+}
+
+// ------------------------------------------------------------------------------------------------ host
+int launch_convt_repack(const bf16* wt, int r, int cout, int cin, bf16* wc, cudaStream_t s) {
+  convt_repack_kernel<<<r * cout, 256, 0, s>>>(wt, r, cout, cin, wc);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+int convt_fused_bn(int N) { return convt_bn(N); }
+
+bool convt_fused_ok(int cin, int cout, int r) {
+  const int N = r * cout, BN = convt_bn(N);
+  return cin % 64 == 0 && cout % 32 == 0 && N % BN == 0 && BN % 16 == 0;
+}
+bool res_fused_ok(int cout, int hid) { return (cout == 64 && hid == 32) || (cout == 128 && hid == 64); }
+
+size_t convt_fused_smem(int cin, int cout, int r) {
+  (void)cin;
+  const int BN = convt_bn(r * cout);
+  return 1024 + (size_t)convt_stages(BN) * (kUM * 128 + BN * 128) + 8 * (2 * 3 + 1) + 16;
+}
+size_t res_fused_smem(int cout, int hid) {
+  return 1024 + 3 * (size_t)(cout / 64) * kResBox + (size_t)hid * (3 * cout + 8) * 2 + (size_t)cout * (hid + 8) * 2 +
+         (size_t)kEluLut * 2 + 16;
+}
+
+int seanet_fused_init() {
+  int dev = 0;
+  M3_CUDA(cudaGetDevice(&dev));
+  M3_CUDA(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev));
+  const int big = 227 * 1024;
+  M3_CUDA(cudaFuncSetAttribute(convt_umma_kernel<128, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaFuncSetAttribute(convt_umma_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<64, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<128, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  if (!g_elu_lut) {
+    M3_CUDA(cudaMalloc(&g_elu_lut, kEluLut * sizeof(uint16_t)));
+    elu_lut_kernel<<<(kEluLut + 255) / 256, 256>>>(g_elu_lut);
+    M3_CUDA(cudaGetLastError());
+    M3_CUDA(cudaDeviceSynchronize());
+  }
+  return M3_OK;
+}
+
+int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status) {
+  const int N = p.r * p.cout, BN = convt_bn(N);
+  const dim3 grid(N / BN, (p.L + 1 + kUM - 1) / kUM, R);
+  const size_t smem = convt_fused_smem(p.cin, p.cout, p.r);
+  if (BN == 256)
+    convt_umma_kernel<256, 2><<<grid, 128, smem, s>>>(p.amap, p.bmap, p.bias, p.tail_in, p.in_row, p.state,
+                                                      p.state_row, p.tail_off, p.slot32, p.u, p.L, p.r, p.cin, p.cout,
+                                                      status);
+  else if (BN == 128)
+    convt_umma_kernel<128, 3><<<grid, 128, smem, s>>>(p.amap, p.bmap, p.bias, p.tail_in, p.in_row, p.state,
+                                                      p.state_row, p.tail_off, p.slot32, p.u, p.L, p.r, p.cin, p.cout,
+                                                      status);
+  else
+    M3_REQUIRE(false, M3_ERR_UNSUPPORTED, "transposed conv of %d columns has no fused form", N);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status) {
+  const int tiles = R * ((p.Lo + kBM - 1) / kBM);
+  const size_t smem = res_fused_smem(p.cout, p.hid);
+  const int per_sm = std::max(1, (int)((228 * 1024) / (smem + 1024)));
+  const dim3 grid(std::max(1, std::min(tiles, g_sms * per_sm)));
+  if (p.cout == 64)
+    res_fused_kernel<64, 32><<<grid, kResThreads, smem, s>>>(p.umap, p.w1, p.b1, p.w2, p.b2, p.hist_in, p.in_row, p.state,
+                                                     p.state_row, p.hist_off, p.slot32, p.e, p.Lo, R, g_elu_lut, status);
+  else
+    res_fused_kernel<128, 64><<<grid, kResThreads, smem, s>>>(p.umap, p.w1, p.b1, p.w2, p.b2, p.hist_in, p.in_row, p.state,
+                                                      p.state_row, p.hist_off, p.slot32, p.e, p.Lo, R, g_elu_lut, status);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+int launch_state_snapshot(const bf16* state, int64_t state_row, const int* slot32, int R, const StateCopy& c,
+                          bf16* snap, int64_t snap_row, cudaStream_t s) {
+  if (R <= 0 || c.n == 0) return M3_OK;
+  state_snapshot_kernel<<<R, 128, 0, s>>>(state, state_row, slot32, c, snap, snap_row);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+}  // namespace m3

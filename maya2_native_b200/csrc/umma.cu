@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "tma.cuh"
+#include "umma.cuh"
 
 namespace m3 {
 
@@ -21,59 +22,6 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;               // bf16 elements per stage along K = one 128-byte swizzle row
 constexpr int kUmmaK = 16;
 constexpr int kUmmaThreads = 128;
-
-// ------------------------------------------------------------------------------------------------ PTX wrappers
-// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
-  const uint64_t addr = smem_u32(p);
-  uint64_t d = 0;
-  d |= (addr >> 4) & 0x3FFFull;              // start address
-  d |= (uint64_t)1 << 16;                     // leading byte offset (16 B units; unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset: next 8-row group
-  d |= (uint64_t)1 << 46;                     // descriptor version (sm100)
-  d |= (uint64_t)2 << 61;                     // layout: SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M = 128, N = BN.
-__host__ __device__ constexpr uint32_t umma_idesc(int n) {
-  return (1u << 4)                     // D format F32
-         | (1u << 7)                   // A format BF16
-         | (1u << 10)                  // B format BF16
-         | ((uint32_t)(n >> 3) << 17)  // N / 8
-         | ((uint32_t)(kBM >> 4) << 24);  // M / 16
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns of the accumulator into 32 registers of each lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 // ------------------------------------------------------------------------------------------------ kernel
 // OUT: 0 = bf16 rows of Y, 1 = fp32 rows of Y, 2 = fp32 split-K partial tile at Y + blockIdx.z * M * ldy.

@@ -7,6 +7,7 @@ attention: the backbone step over `seats` decode rows at the configs[2] KV-lengt
            benchmark width, `layers` layers (2 layers x 64 seats ~ 1 GB of K/V); run under
            `ncu -k regex:attn_split -c 3`.
 tick:      the full engine tick at the benchmark geometry with fewer seats.
+mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
 """
 from __future__ import annotations
 
@@ -67,6 +68,24 @@ def tick(a):
     print(f"tick case: {a.seats} seats, {a.steps} ticks")
 
 
+@torch.inference_mode()
+def mimi(a):
+    """StaticMimi.decode at the benchmark geometry over `seats` streams (codes U[0, 2048)), `steps` frames."""
+    from . import weights as WG
+    from .codec import StaticMimi
+    from .config import BASELINE
+    dev = torch.device("cuda", 0)
+    g = BASELINE.mimi
+    shapes = {k: v for k, v in WG.all_shapes(BASELINE).items() if k.startswith("mimi.")}
+    codec = StaticMimi(WG.generate(shapes, device=dev), a.seats, batch_buckets=(a.seats,), geom=g, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    slots = torch.arange(a.seats, device=dev)
+    for _ in range(a.steps):
+        codec.decode(slots, torch.randint(0, g.codebook_size, (a.seats, g.n_q), device=dev, generator=gen))
+    torch.cuda.synchronize()
+    print(f"mimi case: {a.seats} streams, {a.steps} frames")
+
+
 # (label, M, N, K) of the linear layers of one configs[2] tick
 TICK_GEMMS = [("bb.qkv", 256, 4096, 1024), ("bb.o", 256, 1024, 2048), ("bb.gu", 256, 6144, 1024),
               ("bb.down", 256, 1024, 3072), ("bb.qkv+pf", 768, 4096, 1024), ("depth.qkv n8", 2048, 3072, 1024),
@@ -118,12 +137,12 @@ def gemm(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("attention", "tick", "gemm"))
+    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi"))
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
     a = ap.parse_args()
-    {"attention": attention, "tick": tick, "gemm": gemm}[a.case](a)
+    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi}[a.case](a)
 
 
 if __name__ == "__main__":
