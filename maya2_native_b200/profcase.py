@@ -8,6 +8,7 @@ attention: the backbone step over `seats` decode rows at the configs[2] KV-lengt
            `ncu -k regex:attn_split -c 3`.
 tick:      the full engine tick at the benchmark geometry with fewer seats.
 mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
+gaps:      per-node cost of a CUDA graph of dependent tiny kernels.
 """
 from __future__ import annotations
 
@@ -86,6 +87,33 @@ def mimi(a):
     print(f"mimi case: {a.seats} streams, {a.steps} frames")
 
 
+@torch.inference_mode()
+def gaps(a):
+    """Per-node cost of a CUDA graph of dependent tiny kernels (one-element adds on one stream): the launch and
+    dependency overhead that every small kernel of the tick pays."""
+    dev = torch.device("cuda", 0)
+    x = torch.zeros(1, device=dev)
+    for n in (100, 400):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            x.add_(1)
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(n):
+                x.add_(1)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"graph of {n} dependent tiny kernels: {e0.elapsed_time(e1) / 10 / n * 1e3:.3f} us per node")
+
+
 # (label, M, N, K) of the linear layers of one configs[2] tick
 TICK_GEMMS = [("bb.qkv", 256, 4096, 1024), ("bb.o", 256, 1024, 2048), ("bb.gu", 256, 6144, 1024),
               ("bb.down", 256, 1024, 3072), ("bb.qkv+pf", 768, 4096, 1024), ("depth.qkv n8", 2048, 3072, 1024),
@@ -137,12 +165,12 @@ def gemm(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi"))
+    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi", "gaps"))
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
     a = ap.parse_args()
-    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi}[a.case](a)
+    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps}[a.case](a)
 
 
 if __name__ == "__main__":
