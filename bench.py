@@ -59,6 +59,9 @@ def args_():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seats", type=int, default=16)
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] TTFA and configs[3] Mimi runs")
+    ap.add_argument("--tick-breakdown", action="store_true",
+                    help="time each tick of the device-resident run and print the mean for ticks with and without "
+                         "admissions (inline prefill rows), then exit")
     ap.add_argument("--stages", action="store_true",
                     help="print the device time of each stage of a decode tick (backbone, cb0, depth, Mimi) at the "
                          "configs[2] steady state, each stage called through its own mirror object, and exit")
@@ -250,6 +253,15 @@ def run_native(a, rank, world, local):
         launches += lib.m3_launch_count() - c0          # eager launches in the region (slot resets)
     dev_ms = ev[0].elapsed_time(ev[-1])
     tick_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(len(plans))]
+    if a.tick_breakdown:
+        adm = [k for k, tp in enumerate(plans) if tp.new]
+        dec = [k for k, tp in enumerate(plans) if not tp.new]
+        eng.close()
+        return {"ticks": len(plans), "decode_only": {"n": len(dec), "mean_ms": float(np.mean([tick_ms[k] for k in dec]))},
+                "with_admission": {"n": len(adm), "mean_ms": float(np.mean([tick_ms[k] for k in adm])) if adm else None,
+                                   "rows": [int(plans[k].rows) for k in adm],
+                                   "prefill_rows": [int(sum(len(s.prompt) for s in plans[k].new)) for k in adm],
+                                   "ms": [round(tick_ms[k], 3) for k in adm]}}
     status = eng.device_status()
 
     # ---- end to end through the public tick: H2D plan + D2H readout + sync every tick, wall clock
