@@ -225,13 +225,6 @@ __global__ void kv_store_kernel(const bf16* __restrict__ qkv, int T, bf16* __res
   for (int i = threadIdx.x; i < 2 * D / 8; i += blockDim.x) dst[i] = src[i];
 }
 
-// keep only the last position of each row block: out[b] = x[b*T + T-1]  (x = x[:, -1:], serve/fast_depth.py:181)
-__global__ void take_last_kernel(const bf16* __restrict__ x, int T, bf16* __restrict__ out, int D) {
-  const int b = blockIdx.x;
-  const uint4* src = reinterpret_cast<const uint4*>(x + ((int64_t)b * T + T - 1) * D);
-  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)b * D);
-  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
-}
 
 // act = bf16(gelu_erf(f))   (F.gelu on the depth dtype)
 __global__ void gelu_kernel(bf16* __restrict__ f, int64_t n8) {
@@ -501,16 +494,19 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       else
         depth_attn_kernel<1><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
       M3_LAUNCHED();
-      if (Tq != Tr) {  // the last layer keeps only each seat's final position
-        take_last_kernel<<<R, 128, 0, s>>>(d->x, Tr, d->x2, D);
-        M3_LAUNCHED();
+      M3_TRY(gemm({d->a, D, d->o[gl + li], D, d->ob, D, R * Tq, D, D, false}, s));
+      if (Tq != Tr) {
+        // the last layer keeps only each seat's final position (x = x[:, -1:], serve/fast_depth.py:181): the
+        // residual add reads row Tr-1 of each seat's block and writes the compact stream
+        M3_TRY(launch_add_ln(R, d->x + (int64_t)(Tr - 1) * D, 1, (int64_t)Tr * D, 0, d->ob, nullptr, 0, nullptr, d->x2,
+                             d->y, d->n2_w[gl + li], d->n2_b[gl + li], c.ln_eps, D, s));
         std::swap(d->x, d->x2);
         Tr = Tq;
+      } else {
+        // x, y2 = add_ln(x, o(a), n2)
+        M3_TRY(launch_add_ln(R * Tr, d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
+                             d->n2_b[gl + li], c.ln_eps, D, s));
       }
-      M3_TRY(gemm({d->a, D, d->o[gl + li], D, d->ob, D, R * Tr, D, D, false}, s));
-      // x, y2 = add_ln(x, o(a), n2)
-      M3_TRY(launch_add_ln(R * Tr, d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
-                    d->n2_b[gl + li], c.ln_eps, D, s));
       M3_TRY(gemm({d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
       const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
       gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);

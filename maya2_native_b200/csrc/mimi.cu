@@ -691,6 +691,8 @@ struct m3_mimi {
   std::vector<ConvTFused> ct;
   std::vector<ResFused> rs;
   StateCopy snap_regions{};
+  FinalFused fin{};
+  bool fin_fused = false;
   int64_t snap_row = 0;
   void* fws = nullptr;  // repacked transposed-conv weights + the state snapshot
   bf16* snap = nullptr;
@@ -839,6 +841,19 @@ static int setup_fused_seanet(m3_mimi* m) {
     rs.hid = sd.cout / c.compress;
     m->ct.push_back(ct);
     m->rs.push_back(rs);
+  }
+  if (first < n && final_fused_ok(c.num_filters, c.last_kernel) && m->final_off % 8 == 0) {
+    const StageDims& ls = m->stages.back();
+    M3_TRY(map3(&m->fin.xmap, m->act0, c.num_filters, ls.L * ls.r, 128 + c.last_kernel - 1));
+    m->fin.taps = c.last_kernel;
+    m->fin.w = m->final_w;
+    m->fin.bias = m->final_b;
+    m->fin.state = m->state;
+    m->fin.state_row = m->state_row;
+    m->fin.hist_off = m->final_off;
+    m->fin.slot32 = m->slot32;
+    m->fin.L = ls.L * ls.r;
+    m->fin_fused = true;
   }
   M3_CUDA(cudaDeviceSynchronize());  // the weight repack finished before the first decode
   m->first_fused = first;
@@ -1203,10 +1218,16 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   const size_t fsmem = ((size_t)(kFinalTile + c.last_kernel - 1) * (c.num_filters + 1) +
                         (size_t)c.last_kernel * c.num_filters) * sizeof(float);
   const int elu_x = first_fused < nst ? 0 : 1;  // the fused stages hand over ELU(y)
-  final_conv_kernel<<<dim3(R, cdiv(Lf, kFinalTile)), kFinalTile, fsmem, s>>>(
-      x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32, m->state, m->state_row, m->final_off,
-      pcm, elu_x);
-  M3_LAUNCHED();
+  if (m->fin_fused) {
+    FinalFused fp = m->fin;
+    fp.pcm = pcm;
+    M3_TRY(launch_final_fused(fp, R, s, m->status));
+  } else {
+    final_conv_kernel<<<dim3(R, cdiv(Lf, kFinalTile)), kFinalTile, fsmem, s>>>(
+        x, Lf, c.num_filters, c.last_kernel, m->final_w, m->final_b, m->slot32, m->state, m->state_row,
+        m->final_off, pcm, elu_x);
+    M3_LAUNCHED();
+  }
   conv_hist_kernel<<<dim3(R, cdiv(c.num_filters / 8, 128)), 128, 0, s>>>(x, Lf, c.num_filters, c.last_kernel, elu_x,
                                                                           m->slot32, m->state, m->state_row,
                                                                           m->final_off);

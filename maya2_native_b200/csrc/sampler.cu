@@ -46,25 +46,62 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 constexpr int kSampThreads = 256;
 constexpr int kMaxPer = 16;  // up to 4096 entries per row
 
-// Largest key T with #(key >= T) >= k, i.e. the k-th largest key (1 <= k <= n).
-__device__ uint32_t kth_largest_key(const uint32_t (&key)[kMaxPer], int per, int k, int* red) {
-  uint32_t T = 0;
-  for (int b = 31; b >= 0; --b) {
-    const uint32_t cand = T | (1u << b);
-    int cnt = 0;
+// The k-th largest key (1 <= k <= n), exactly: a radix select over four 8-bit digits, most significant first.  Each
+// pass histograms the digit of the keys that match the digits chosen so far (one private histogram per warp), then one
+// warp scans the 256 bins from the top to find the bin holding the rank-th largest and the rank inside it.
+__device__ uint32_t kth_largest_key(const uint32_t (&key)[kMaxPer], int per, int k) {
+  constexpr int kWarps = kSampThreads / 32;
+  __shared__ int hist[kWarps][256];
+  __shared__ int s_digit, s_rank;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t prefix = 0, mask = 0;
+  int rank = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < kWarps * 256; i += kSampThreads) (&hist[0][0])[i] = 0;
+    __syncthreads();
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i)
-      if (i < per) cnt += key[i] >= cand;
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (i < per && (key[i] & mask) == prefix) atomicAdd(&hist[warp][(key[i] >> shift) & 255u], 1);
     __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = cnt;
-    __syncthreads();
-    int tot = 0;
+    for (int b = tid; b < 256; b += kSampThreads) {
+      int sum = 0;
 #pragma unroll
-    for (int w = 0; w < kSampThreads / 32; ++w) tot += red[w];
-    if (tot >= k) T = cand;
+      for (int w = 0; w < kWarps; ++w) sum += hist[w][b];
+      hist[0][b] = sum;
+    }
+    __syncthreads();
+    if (warp == 0) {  // lane l holds digits 255 - 8l .. 248 - 8l
+      int c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[0][255 - 8 * lane - j];
+        tot += c[j];
+      }
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int run = incl - tot;
+      if (run < rank && rank <= incl) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (run + c[j] >= rank) {
+            s_digit = 255 - 8 * lane - j;
+            s_rank = rank - run;
+            break;
+          }
+          run += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)s_digit << shift;
+    mask |= 0xFFu << shift;
+    rank = s_rank;
   }
-  return T;
+  return prefix;
 }
 
 // Block argmax with the smallest index among equal maxima (torch / Triton argmax).
@@ -96,7 +133,6 @@ __global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
     const int32_t* __restrict__ ctr, const int* __restrict__ slot32, int level, float inv_temp, int k, int greedy,
     int64_t* __restrict__ codes, int64_t code_stride, const bf16* __restrict__ embed, int D,
     bf16* __restrict__ next_row, int64_t next_stride) {
-  __shared__ int red[32];
   __shared__ float redv[32];
   __shared__ int redi[32];
   __shared__ int s_code;
@@ -116,7 +152,7 @@ __global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
     }
   }
   float kth = 0.f;
-  if (k >= 1 && k <= V) kth = key_value(kth_largest_key(key, per, k, red));
+  if (k >= 1 && k <= V) kth = key_value(kth_largest_key(key, per, k));
   float best = -INFINITY;
   int bidx = 0x7fffffff;
   const int32_t sd = greedy ? 0 : seed[sl];
@@ -126,7 +162,7 @@ __global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
     const int c = tid + i * kSampThreads;
     if (i < per && c < V) {
       float sc = x[i] >= kth ? x[i] : -INFINITY;
-      if (!greedy) {
+      if (!greedy && sc != -INFINITY) {  // masked entries cannot win: their noise is never drawn
         const float u = fmaxf(philox_uniform(sd, base + (uint32_t)c), 1e-12f);
         sc = sc - logf(-logf(u));
       }
@@ -215,7 +251,6 @@ __global__ void __launch_bounds__(kSampThreads) cb0_sample_kernel(const TL* __re
                                                                   int64_t* __restrict__ code_out,
                                                                   int64_t* __restrict__ cb0_out, int* status) {
   __shared__ float redf[32];
-  __shared__ int red[32];
   __shared__ float redv[32];
   __shared__ int redi[32];
   __shared__ unsigned char pen[kSortN];
@@ -260,7 +295,7 @@ __global__ void __launch_bounds__(kSampThreads) cb0_sample_kernel(const TL* __re
   // top-k: keep x >= k-th largest, k clamped to [1, V]   maya3/engine.py:666-668
   int64_t k = st.top_k[slot];
   k = k < 1 ? 1 : (k > V ? V : k);
-  const float kth = key_value(kth_largest_key(key, per, (int)k, red));
+  const float kth = key_value(kth_largest_key(key, per, (int)k));
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i)
     if (x[i] < kth) x[i] = -INFINITY;
@@ -370,9 +405,11 @@ __global__ void __launch_bounds__(kSampThreads) cb0_sample_kernel(const TL* __re
   for (int i = 0; i < kMaxPer; ++i) {
     const int c = tid + i * kSampThreads;
     if (i < per && c < V) {
-      const float u = fmaxf(philox_uniform(sd, base + (uint32_t)c), 1e-12f);
-      const float e = -logf(u);
-      const float r = (p[i] / qs) / e;
+      float r = 0.f;  // p = 0: the ratio is 0 whatever the exponential draw (finite, u >= 1e-12)
+      if (p[i] != 0.f) {
+        const float u = fmaxf(philox_uniform(sd, base + (uint32_t)c), 1e-12f);
+        r = (p[i] / qs) / -logf(u);
+      }
       if (r > best || bidx == 0x7fffffff) best = r, bidx = c;
     }
   }

@@ -339,6 +339,75 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
   }
 }
 
+// ------------------------------------------------------------------------------------------------ final conv
+// PCM[t] = bf16(bias + sum_{j<KT, c<64} W[j][c] e[t - (KT-1) + j][c]) on the tensor cores: the tile of 128 + KT-1 rows
+// (rows before the stream's start are the stored history) arrives by TMA, the KT taps are row-shifted ldmatrix reads
+// of it, and the single output column is the first of an 8-column mma (the weights are the B operand, zero in the
+// other columns).  Warp w computes rows 32w .. 32w+31.
+__host__ __device__ constexpr uint32_t fin_box(int kt) { return ((128 + kt - 1) * 128 + 1023) / 1024 * 1024; }
+
+template <int KT>
+__global__ void __launch_bounds__(128) final_mma_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                        const bf16* __restrict__ w, const bf16* __restrict__ bias,
+                                                        const bf16* __restrict__ state, int64_t state_row,
+                                                        int64_t hist_off, const int* __restrict__ slot32,
+                                                        float* __restrict__ pcm, int L, int* status) {
+  constexpr int P = KT - 1, KS = KT * 4;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* xs = align1024(smem_raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xs + fin_box(KT));
+  const int b = blockIdx.x, t0 = blockIdx.y * 128;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tq = lane & 3, jm = lane >> 3;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_expect_tx(bar, (128 + P) * 128);
+    tma_load_3d(xs, &xmap, 0, t0 - P, b, bar);
+  }
+  // B fragments (k = tap * 64 + channel, n = output column): column 0 holds the weights
+  uint32_t wb[KS][2];
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(w + ks * 16);
+    wb[ks][0] = g == 0 ? wp[tq] : 0u;
+    wb[ks][1] = g == 0 ? wp[4 + tq] : 0u;
+  }
+  const float bv = to_f(bias[0]);
+  const bool ok = mbar_wait(bar, 0, status);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) mbar_wait(bar, 0, nullptr);
+    __syncthreads();
+    return;
+  }
+  if (t0 == 0) {  // rows t = -P .. -1: the stream's history
+    const bf16* hist = state + (int64_t)slot32[b] * state_row + hist_off;
+    for (int i = tid; i < P * 8; i += 128)
+      *reinterpret_cast<uint4*>(xs + sw128(i / 8, i % 8)) = *reinterpret_cast<const uint4*>(hist + i * 8);
+    __syncthreads();
+  }
+  const uint32_t xb = smem_u32(xs);
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi) {
+    const int m0 = warp * 32 + mi * 16;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int j = ks >> 2, kk = ks & 3;
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(xb + sw128(m0 + j + (jm & 1) * 8 + (lane & 7), 2 * kk + (jm >> 1)), a0, a1, a2, a3);
+      mma_bf16(acc, a0, a1, a2, a3, wb[ks][0], wb[ks][1]);
+    }
+    if (tq == 0) {
+      const int ta = t0 + m0 + g, tb = ta + 8;
+      if (ta < L) pcm[(int64_t)b * L + ta] = rbf(acc[0] + bv);
+      if (tb < L) pcm[(int64_t)b * L + tb] = rbf(acc[2] + bv);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ state snapshot
 __global__ void state_snapshot_kernel(const bf16* __restrict__ state, int64_t state_row,
                                       const int* __restrict__ slot32, StateCopy c, bf16* __restrict__ snap,
@@ -372,6 +441,20 @@ bool convt_fused_ok(int cin, int cout, int r) {
   const int N = r * cout, BN = convt_bn(N);
   return cin % 64 == 0 && cout % 32 == 0 && N % BN == 0 && BN % 16 == 0;
 }
+bool final_fused_ok(int channels, int taps) { return channels == 64 && (taps == 3 || taps == 7); }
+
+int launch_final_fused(const FinalFused& p, int R, cudaStream_t s, int* status) {
+  const dim3 grid(R, (p.L + 127) / 128);
+  if (p.taps == 3)
+    final_mma_kernel<3><<<grid, 128, fin_box(3) + 1024 + 16, s>>>(p.xmap, p.w, p.bias, p.state, p.state_row,
+                                                                   p.hist_off, p.slot32, p.pcm, p.L, status);
+  else
+    final_mma_kernel<7><<<grid, 128, fin_box(7) + 1024 + 16, s>>>(p.xmap, p.w, p.bias, p.state, p.state_row,
+                                                                   p.hist_off, p.slot32, p.pcm, p.L, status);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
 bool res_fused_ok(int cout, int hid) { return (cout == 64 && hid == 32) || (cout == 128 && hid == 64); }
 
 size_t convt_fused_smem(int cin, int cout, int r) {

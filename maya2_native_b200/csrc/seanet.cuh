@@ -42,6 +42,21 @@ struct ResFused {
   int Lo, cout, hid;
 };
 
+// Final ELU -> conv (64 channels -> 1, 3 or 7 taps, causal) over the last stage's e = ELU(y) (bf16 [R][L][64]) ->
+// fp32 PCM [R][L] = bf16(conv + bias) as the reference's bf16 model rounds it.
+struct FinalFused {
+  CUtensorMap xmap;          // e as [R][L][64], box {64 channels, 128 + taps - 1 rows, 1}, 128-byte swizzle
+  const bf16* w;             // [taps * 64], tap-major
+  const bf16* bias;          // [1]
+  const bf16* state;         // the taps - 1 ELU'd history rows at state[slot][hist_off ..]
+  int64_t state_row, hist_off;
+  const int* slot32;
+  float* pcm;
+  int L, taps;
+};
+bool final_fused_ok(int channels, int taps);
+int launch_final_fused(const FinalFused& p, int R, cudaStream_t s, int* status);
+
 // Kernel shapes supported by the fused forms (other stages use the GEMM + elementwise path), and the transposed
 // conv's output columns per CTA (its weight map's box height).
 int convt_fused_bn(int N);
