@@ -63,6 +63,7 @@ class Seat:
     frames: int = 0
     new: bool = True
     stop: Optional[str] = None
+    inline: Optional[np.ndarray] = None   # the part of the prompt prefilled inline in the admission tick
 
 
 @dataclasses.dataclass
@@ -81,6 +82,65 @@ def _bucket(values, need, what):
         if b >= need:
             return b
     raise ValueError(f"{what} {need} exceeds largest bucket {values[-1]}")
+
+
+def admission_cap(n_active: int, cfg: "TickConfig") -> int:
+    """How many pending requests one tick may admit (maya3/engine.py:451-454): max_admit_per_tick, or busy_admit once
+    more than busy_frac of the seats are taken."""
+    cap = cfg.max_admit_per_tick
+    if n_active > cfg.busy_frac * cfg.max_seats:
+        cap = min(cap, cfg.busy_admit)
+    return cap
+
+
+def frame_budget(prompt_len: int, max_frames: int, capacity: int) -> int:
+    """A request's frame budget inside the KV capacity (maya3/engine.py:465-472): prompt + frames + 2 must fit; a
+    budget clipped below 8 frames rejects the request."""
+    if prompt_len + max_frames + 2 > capacity:
+        max_frames = capacity - prompt_len - 2
+        if max_frames < 8:
+            raise ValueError(f"prompt of {prompt_len} tokens leaves no room in KV capacity {capacity}")
+    return max_frames
+
+
+def plan_layout(dec, new, lengths, row_buckets, seat_buckets, ctx_buckets, dummy):
+    """The m3_tick_run plan of one tick: rows = one decode row per `dec` slot, then each admitted seat's inline prompt
+    rows at consecutive offsets; then per seat (decode seats first) its slot and the row holding its last position.
+
+    dec: decode slots; new: [(slot, inline token ids)]; lengths: the slots' current KV lengths (host mirror).
+    Returns (plan int64 [4 * rb + 2 * sb], rb, sb, cb, keys): the row / seat / context buckets and the number of keys
+    one attention launch reads (decode rows: length + 1; prefill row at offset o: o + 1; padding rows: 1)."""
+    nd = len(dec)
+    n_rows = nd + sum(len(t) for _, t in new)
+    rb = _bucket(row_buckets, max(n_rows, 1), "rows")
+    sb = _bucket(seat_buckets, max(nd + len(new), 1), "seats")
+    need = max([lengths[s] + 1 for s in dec] + [lengths[s] + len(t) for s, t in new] + [1])
+    cb = _bucket(ctx_buckets, need, "context")
+    keys = (sum(lengths[s] + 1 for s in dec) + sum(lengths[s] * len(t) + len(t) * (len(t) + 1) // 2 for s, t in new)
+            + (rb - n_rows))
+    p = np.zeros(4 * rb + 2 * sb, np.int64)
+    r_slot, r_off, r_real, r_src = p[:rb], p[rb:2 * rb], p[2 * rb:3 * rb], p[3 * rb:4 * rb]
+    s_slot, s_row = p[4 * rb:4 * rb + sb], p[4 * rb + sb:]
+    r_slot[:] = dummy
+    r_src[:] = -1
+    s_slot[:] = dummy
+    if nd:
+        r_slot[:nd] = dec
+        r_real[:nd] = 1
+        r_src[:nd] = FROM_FEEDBACK
+        s_slot[:nd] = dec
+        s_row[:nd] = np.arange(nd)
+    at = nd
+    for j, (slot, toks) in enumerate(new):
+        P = len(toks)
+        r_slot[at:at + P] = slot
+        r_off[at:at + P] = np.arange(P)
+        r_real[at:at + P] = 1
+        r_src[at:at + P] = toks
+        at += P
+        s_slot[nd + j] = slot
+        s_row[nd + j] = at - 1
+    return p, rb, sb, cb, keys
 
 
 class _Graph:
@@ -130,7 +190,8 @@ class TickEngine:
         self.pool = None
         self._host = torch.empty(self.buckets[-1], 2 + self.spf // 4, dtype=torch.int64).pin_memory()
         self._evt = torch.cuda.Event()
-        self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0}
+        self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0,
+                      "eager_prefill_rows": 0}
 
     def close(self):
         if getattr(self, "_handle", None):
@@ -147,16 +208,14 @@ class TickEngine:
 
     # ---------------------------------------------------------------- requests
     def submit(self, prompt_ids, max_frames, rid=None, seed=None) -> Seat:
-        """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False)."""
+        """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False), clipped
+        to the KV capacity as the reference does (a budget below 8 frames rejects the request)."""
         prompt = np.asarray(prompt_ids, np.int64)
         if prompt.ndim != 1 or len(prompt) == 0:
             raise ValueError("prompt must be a non-empty 1-D array of token ids")
-        if len(prompt) > self.cfg.max_inline_rows:
-            raise ValueError(f"prompt of {len(prompt)} tokens exceeds max_inline_rows {self.cfg.max_inline_rows}")
-        if len(prompt) + int(max_frames) + 2 > self.cfg.capacity:
-            raise ValueError(f"prompt of {len(prompt)} tokens + {max_frames} frames exceeds the KV capacity")
+        frames = frame_budget(len(prompt), int(max_frames), self.cfg.capacity)
         seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
-        s = Seat(rid if rid is not None else next(self._ids), prompt, int(max_frames), seed)
+        s = Seat(rid if rid is not None else next(self._ids), prompt, frames, seed)
         self.pending.append(s)
         return s
 
@@ -195,61 +254,47 @@ class TickEngine:
 
     def _admit(self, device=True):
         """maya3/engine.py:449-510 without prompt building: pending requests enter free slots while the tick's row
-        budget allows their inline prefill.  device=False only claims the slots (the caller resets them later, in
-        stream order, with reset_slot)."""
+        budget allows their inline prefill.  A prompt longer than the whole budget is admitted first in its tick:
+        its head is prefilled eagerly (chunked backbone steps, the reference's fallback prefill) and its tail rides
+        the tick inline.  device=False only claims the slots (the caller resets them later, in stream order, with
+        reset_slot) and admits inline prompts only."""
         new, rows = [], len(self.active)
-        cap = self.cfg.max_admit_per_tick
-        if len(self.active) > self.cfg.busy_frac * self.cfg.max_seats:
-            cap = min(cap, self.cfg.busy_admit)
+        cap = admission_cap(len(self.active), self.cfg)
         while self.pending and self.free and len(new) < cap:
             s = self.pending[0]
-            if rows + len(s.prompt) > self.max_rows:
-                break
-            self.pending.pop(0)
-            self._bind(s) if device else self._claim(s)
+            budget = min(self.max_rows - rows, self.cfg.max_inline_rows)
+            if len(s.prompt) > budget:
+                if new or not device or budget < 1:
+                    break  # admit next tick
+                self.pending.pop(0)
+                self._bind(s)
+                self._prefill_head(s, len(s.prompt) - budget)
+            else:
+                self.pending.pop(0)
+                self._bind(s) if device else self._claim(s)
+                s.inline = s.prompt
             new.append(s)
-            rows += len(s.prompt)
+            rows += len(s.inline)
             self.stats["admitted"] += 1
         return new
 
+    @torch.inference_mode()
+    def _prefill_head(self, s: Seat, head: int):
+        """Prefill the first `head` prompt tokens of a bound seat with eager backbone steps of at most
+        max_inline_rows rows; the rest of the prompt becomes its inline part."""
+        x = self.embed[torch.from_numpy(s.prompt[:head]).to(self.device)]
+        step = self.cfg.max_inline_rows
+        for c0 in range(0, head, step):
+            self.backbone.step_mixed([], None, [(s.slot, x[c0:c0 + step])])
+        s.inline = s.prompt[head:]
+        self.stats["eager_prefill_rows"] += head
+
     # ---------------------------------------------------------------- plan
     def make_plan(self, dec: list, new: list) -> TickPlan:
-        """Host plan of one tick (layout of m3_tick_run): rows = decode rows then each new seat's prompt rows."""
-        dummy = self.cfg.max_seats
-        n_rows = len(dec) + sum(len(s.prompt) for s in new)
-        seats = dec + new
-        rb = _bucket(self.row_buckets, max(n_rows, 1), "rows")
-        sb = _bucket(self.buckets, max(len(seats), 1), "seats")
-        lc = self.backbone.lengths_cpu
-        need = max([lc[s.slot] + 1 for s in dec] + [lc[s.slot] + len(s.prompt) for s in new] + [1])
-        cb = _bucket(self.ctx_buckets, need, "context")
-        # keys attended per layer by this step's rows (decode rows: length + 1; prefill row at offset o: o + 1;
-        # padding rows: 1), the algorithmic KV traffic of one attention launch
-        keys = (sum(lc[s.slot] + 1 for s in dec) + sum(len(s.prompt) * (len(s.prompt) + 1) // 2 for s in new)
-                + (rb - n_rows))
-        p = np.zeros(4 * rb + 2 * sb, np.int64)
-        r_slot, r_off, r_real, r_src = p[:rb], p[rb:2 * rb], p[2 * rb:3 * rb], p[3 * rb:4 * rb]
-        s_slot, s_row = p[4 * rb:4 * rb + sb], p[4 * rb + sb:]
-        r_slot[:] = dummy
-        r_src[:] = -1
-        s_slot[:] = dummy
-        nd = len(dec)
-        if nd:
-            r_slot[:nd] = [s.slot for s in dec]
-            r_real[:nd] = 1
-            r_src[:nd] = FROM_FEEDBACK
-            s_slot[:nd] = r_slot[:nd]
-            s_row[:nd] = np.arange(nd)
-        at = nd
-        for j, s in enumerate(new):
-            P = len(s.prompt)
-            r_slot[at:at + P] = s.slot
-            r_off[at:at + P] = np.arange(P)
-            r_real[at:at + P] = 1
-            r_src[at:at + P] = s.prompt
-            at += P
-            s_slot[nd + j] = s.slot
-            s_row[nd + j] = at - 1
+        """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows, then each new seat's inline rows."""
+        p, rb, sb, cb, keys = plan_layout([s.slot for s in dec], [(s.slot, s.inline) for s in new],
+                                          self.backbone.lengths_cpu, self.row_buckets, self.buckets,
+                                          self.ctx_buckets, self.cfg.max_seats)
         return TickPlan(p, rb, sb, cb, list(dec), list(new), keys)
 
     def commit(self, tp: TickPlan):
@@ -258,8 +303,8 @@ class TickEngine:
         for s in tp.dec:
             lc[s.slot] += 1
         for s in tp.new:
-            lc[s.slot] += len(s.prompt)
-            self.stats["prefill_rows"] += len(s.prompt)
+            lc[s.slot] += len(s.inline)
+            self.stats["prefill_rows"] += len(s.inline)
 
     # ---------------------------------------------------------------- graphs
     def graph_for(self, rb, sb, cb) -> _Graph:
@@ -387,4 +432,5 @@ class TickEngine:
         return out
 
 
-__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "FRAME", "FROM_FEEDBACK"]
+__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "FRAME", "FROM_FEEDBACK", "admission_cap", "frame_budget",
+           "plan_layout"]

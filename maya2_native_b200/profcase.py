@@ -9,6 +9,7 @@ attention: the backbone step over `seats` decode rows at the configs[2] KV-lengt
 tick:      the full engine tick at the benchmark geometry with fewer seats.
 mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
 gaps:      per-node cost of a CUDA graph of dependent tiny kernels.
+overlap:   backbone step and Mimi decode timed back to back and concurrently on two streams.
 """
 from __future__ import annotations
 
@@ -114,6 +115,78 @@ def gaps(a):
         print(f"graph of {n} dependent tiny kernels: {e0.elapsed_time(e1) / 10 / n * 1e3:.3f} us per node")
 
 
+@torch.inference_mode()
+def overlap(a):
+    """Could the Mimi decode of one frame hide under the next frame's backbone step?  Graph-captured backbone step
+    (decode rows of `seats` seats, configs[2] KV-length distribution, benchmark width, all layers) and Mimi decode
+    (`seats` streams), timed back to back on one stream and concurrently on two."""
+    from . import weights as WG
+    from .backbone import StaticBackbone
+    from .codec import StaticMimi
+    from .config import BASELINE
+    dev = torch.device("cuda", 0)
+    g = BASELINE
+    W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
+    sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats,), ctx_buckets=(2048,), use_graphs=True,
+                        geom=g.backbone, device=dev)
+    codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
+    for k, v in zip(sb.k, sb.v):
+        k.normal_()
+        v.normal_()
+    rng = np.random.default_rng(0)
+    L = _lengths(a.seats, rng)
+    sb.lengths[:a.seats] = torch.from_numpy(L).to(dev)
+    for s, n in enumerate(L):
+        sb.lengths_cpu[s] = int(n)
+    slots = list(range(a.seats))
+    x = torch.randn(a.seats, g.backbone.hidden, device=dev, dtype=torch.bfloat16)
+    codes = torch.randint(0, 2048, (a.seats, g.mimi.n_q), device=dev)
+    idx = torch.arange(a.seats, device=dev)
+    sb.step(slots, x)
+    codec.decode(idx, codes)
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def run(concurrent, reps=10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        cur = torch.cuda.current_stream()
+        for _ in range(reps):
+            s1.wait_stream(cur)
+            s2.wait_stream(cur)
+            with torch.cuda.stream(s1):
+                sb.step(slots, x)
+            with torch.cuda.stream(s2 if concurrent else s1):
+                codec.decode(idx, codes)
+            cur.wait_stream(s1)
+            cur.wait_stream(s2)
+        e1.record()
+        torch.cuda.synchronize()
+        for s in range(a.seats):
+            sb.lengths_cpu[s] -= reps
+        sb.lengths[:a.seats] -= reps
+        return e0.elapsed_time(e1) / reps
+
+    def alone(fn, reps=10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    t_bb = alone(lambda: sb.step(slots, x))
+    sb.lengths[:a.seats] -= 10
+    for s in range(a.seats):
+        sb.lengths_cpu[s] -= 10
+    t_mimi = alone(lambda: codec.decode(idx, codes))
+    print(f"backbone step {t_bb:.3f} ms, mimi decode {t_mimi:.3f} ms, sequential {run(False):.3f} ms, "
+          f"concurrent {run(True):.3f} ms")
+
+
 # (label, M, N, K) of the linear layers of one configs[2] tick
 TICK_GEMMS = [("bb.qkv", 256, 4096, 1024), ("bb.o", 256, 1024, 2048), ("bb.gu", 256, 6144, 1024),
               ("bb.down", 256, 1024, 3072), ("bb.qkv+pf", 768, 4096, 1024), ("depth.qkv n8", 2048, 3072, 1024),
@@ -165,12 +238,12 @@ def gemm(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi", "gaps"))
+    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi", "gaps", "overlap"))
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
     a = ap.parse_args()
-    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps}[a.case](a)
+    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap}[a.case](a)
 
 
 if __name__ == "__main__":

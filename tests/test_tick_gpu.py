@@ -26,13 +26,14 @@ def snr_db(ref, x):
     return 10 * np.log10((ref ** 2).sum() / max(((ref - x) ** 2).sum(), 1e-30))
 
 
-def run_stage_parity(g, cuda, lens, ticks, capacity):
+def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
     Wt = WG.generate(WG.all_shapes(g), seed=0)
     Wn = {k: v.float().numpy() for k, v in Wt.items()}
     Wd = {k: v.to(cuda) for k, v in Wt.items()}
     del Wt
     n = len(lens)
-    cfg = TickConfig(max_seats=n, capacity=capacity, stops=False, seed=7, max_inline_rows=max(64, sum(lens)))
+    cfg = TickConfig(max_seats=n, capacity=capacity, stops=False, seed=7,
+                     max_inline_rows=max_inline or max(64, sum(lens)))
     eng = TickEngine(g, Wd, cfg, device=cuda)
     del Wd
     ora = OracleTick(Wn, g, n, capacity, "bf16", temp=cfg.temp, top_k=cfg.top_k, cb0_temp=cfg.cb0_temp,
@@ -80,6 +81,7 @@ def run_stage_parity(g, cuda, lens, ticks, capacity):
         res["snr"].append(float(snr_db(pcm_o, pcm_gpu)))
         fb_prev = fb_gpu
     assert eng.device_status() == 0
+    res["eager_prefill_rows"] = eng.stats["eager_prefill_rows"]
     eng.close()
     return res
 
@@ -105,3 +107,13 @@ def test_tick_benchmark_geometry_stage_by_stage(cuda):
     assert r["code_hit"] / r["code_n"] >= 0.85, r
     assert max(r["fb_err"]) < 1e-1, r
     assert min(r["snr"]) > 25, r
+
+
+def test_tick_eager_prefill_of_a_long_prompt(cuda):
+    """A prompt longer than the tick's row budget: its head is prefilled by eager chunked backbone steps and its tail
+    rides the admission tick inline (the reference's fallback prefill); the oracle prefills the whole prompt at once."""
+    r = run_stage_parity(TINY, cuda, (40, 7), 6, 256, max_inline=16)
+    assert r["eager_prefill_rows"] == 24, r
+    assert max(r["h_err"]) < 2e-2, r
+    assert r["cb0_hit"] / r["cb0_n"] >= 0.9, r
+    assert min(r["snr"]) > 30, r
