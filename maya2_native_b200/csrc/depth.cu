@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "mma.cuh"
 #include "ops.cuh"
 #include "sampler.cuh"
 
@@ -215,6 +216,112 @@ __global__ void depth_attn_kernel(const bf16* __restrict__ qkv, int T, int q0, i
   bf16* dst = out + ((int64_t)b * Tq + i) * D + (int64_t)h * HD + lane * PER;
 #pragma unroll
   for (int e = 0; e < PER; ++e) dst[e] = to_bf(o[e] / l);
+}
+
+// The same attention on the tensor cores for head dim 128 and at most 16 queries and 16 keys: one warp per
+// (seat, head).  K and V rows are staged in shared memory (row stride padded to 272 B, so ldmatrix reads are
+// conflict-free; rows past the last key are zero), Q fragments come straight from global memory; S = Q K^T is 8
+// mma (queries as rows), an exact softmax per query over its visible keys, O = P V with P split into bf16 hi + lo
+// (fp32-accurate weights) is 32 mma, O / sum rounded once.
+constexpr int kDaRow = 128 + 8;  // staged row stride in elements
+
+__global__ void __launch_bounds__(32) depth_attn_mma_kernel(const bf16* __restrict__ qkv, int T, int q0, int Tq,
+                                                            KeySrc ks, int H, float scale, bf16* __restrict__ out) {
+  __shared__ __align__(16) bf16 Ks[16 * kDaRow];
+  __shared__ __align__(16) bf16 Vs[16 * kDaRow];
+  const int b = blockIdx.x, h = blockIdx.y, lane = threadIdx.x, g = lane >> 2, t = lane & 3;
+  const int D = H * 128;
+  const int nk = q0 + Tq;  // keys 0 .. q0 + Tq - 1 (the last query sees them all)
+  const bf16* kb = ks.k + (int64_t)b * ks.sb + (int64_t)h * 128;
+  const bf16* vb = ks.v + (int64_t)b * ks.sb + (int64_t)h * 128;
+  for (int i = lane; i < 16 * 16; i += 32) {  // 16 rows x 16 chunks of 16 B
+    const int j = i >> 4, c = i & 15;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+    if (j < nk) {
+      kv = reinterpret_cast<const uint4*>(kb + (int64_t)j * ks.sj)[c];
+      vv = reinterpret_cast<const uint4*>(vb + (int64_t)j * ks.sj)[c];
+    }
+    *reinterpret_cast<uint4*>(Ks + j * kDaRow + c * 8) = kv;
+    *reinterpret_cast<uint4*>(Vs + j * kDaRow + c * 8) = vv;
+  }
+  // Q fragments: rows g and g + 8 are queries (zero past Tq)
+  const bool va = g < Tq, vbq = g + 8 < Tq;
+  const uint32_t* qa = reinterpret_cast<const uint32_t*>(qkv + ((int64_t)b * T + (T - Tq) + (va ? g : 0)) * 3 * D +
+                                                         (int64_t)h * 128);
+  const uint32_t* qb = reinterpret_cast<const uint32_t*>(qkv + ((int64_t)b * T + (T - Tq) + (vbq ? g + 8 : 0)) * 3 *
+                                                         D + (int64_t)h * 128);
+  __syncwarp();
+  const int jm = lane >> 3;
+  float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t a0 = va ? qa[8 * kk + t] : 0u, a2 = va ? qa[8 * kk + 4 + t] : 0u;
+    const uint32_t a1 = vbq ? qb[8 * kk + t] : 0u, a3 = vbq ? qb[8 * kk + 4 + t] : 0u;
+    uint32_t k0, k1, k2, k3;  // B = K^T: matrices (keys 0-7 | 8-15) x (dims 16kk.. | 16kk+8..)
+    ldsm_x4(smem_u32(Ks + (((jm >> 1) << 3) + (lane & 7)) * kDaRow + 16 * kk + (jm & 1) * 8), k0, k1, k2, k3);
+    mma_bf16(sc[0], a0, a1, a2, a3, k0, k1);
+    mma_bf16(sc[1], a0, a1, a2, a3, k2, k3);
+  }
+  // exact softmax per query row over its visible keys (key j visible to query i iff j <= q0 + i)
+  float p[2][4], mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = nt * 8 + 2 * t + e;
+      p[nt][e] = (va && j <= q0 + g) ? sc[nt][e] * scale : -INFINITY;
+      p[nt][2 + e] = (vbq && j <= q0 + g + 8) ? sc[nt][2 + e] * scale : -INFINITY;
+      mxa = fmaxf(mxa, p[nt][e]);
+      mxb = fmaxf(mxb, p[nt][2 + e]);
+    }
+  mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+  mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+  mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+  mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+  float la = 0.f, lb = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      p[nt][e] = p[nt][e] == -INFINITY ? 0.f : expf(p[nt][e] - mxa);
+      p[nt][2 + e] = p[nt][2 + e] == -INFINITY ? 0.f : expf(p[nt][2 + e] - mxb);
+      la += p[nt][e];
+      lb += p[nt][2 + e];
+    }
+  la += __shfl_xor_sync(0xffffffffu, la, 1);
+  la += __shfl_xor_sync(0xffffffffu, la, 2);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+  // A = P (queries x keys): a0 = (g, keys 2t..) n-tile 0 c0c1; a1 = (g+8, ..) c2c3; a2/a3 the same of n-tile 1
+  uint32_t ph[4], pl[4];
+  const float pv[4][2] = {{p[0][0], p[0][1]}, {p[0][2], p[0][3]}, {p[1][0], p[1][1]}, {p[1][2], p[1][3]}};
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    ph[r] = pack_bf2(pv[r][0], pv[r][1]);
+    pl[r] = pack_bf2(pv[r][0] - bf_lo_f(ph[r]), pv[r][1] - bf_hi_f(ph[r]));
+  }
+  const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+  bf16* oa = out + ((int64_t)b * Tq + g) * D + (int64_t)h * 128;
+  bf16* ob = out + ((int64_t)b * Tq + g + 8) * D + (int64_t)h * 128;
+#pragma unroll
+  for (int dt = 0; dt < 8; ++dt) {  // 16 dims per ldmatrix.trans x4: B = V (keys x dims)
+    uint32_t v0, v1, v2, v3;  // matrices (keys 0-7 | 8-15) x (dims 16dt.. | 16dt+8..)
+    ldsm_x4_t(smem_u32(Vs + ((jm & 1) * 8 + (lane & 7)) * kDaRow + 16 * dt + (jm >> 1) * 8), v0, v1, v2, v3);
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_bf16(o0, ph[0], ph[1], ph[2], ph[3], v0, v1);
+    mma_bf16(o0, pl[0], pl[1], pl[2], pl[3], v0, v1);
+    mma_bf16(o1, ph[0], ph[1], ph[2], ph[3], v2, v3);
+    mma_bf16(o1, pl[0], pl[1], pl[2], pl[3], v2, v3);
+    const int d0 = 16 * dt + 2 * t, d1 = d0 + 8;
+    if (va) {
+      *reinterpret_cast<uint32_t*>(oa + d0) = pack_bf2(o0[0] * ia, o0[1] * ia);
+      *reinterpret_cast<uint32_t*>(oa + d1) = pack_bf2(o1[0] * ia, o1[1] * ia);
+    }
+    if (vbq) {
+      *reinterpret_cast<uint32_t*>(ob + d0) = pack_bf2(o0[2] * ib, o0[3] * ib);
+      *reinterpret_cast<uint32_t*>(ob + d1) = pack_bf2(o1[2] * ib, o1[3] * ib);
+    }
+  }
 }
 
 // kvbuf[b, p0 + t] = (k, v) of qkv rows t of b  (serve/fast_depth.py:170,176)
@@ -487,7 +594,9 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
         }
       }
       const dim3 ag(R, H);
-      if (HD == 128)
+      if (HD == 128 && Tq <= 16 && q0 + Tq <= 16)
+        depth_attn_mma_kernel<<<ag, 32, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
+      else if (HD == 128)
         depth_attn_kernel<4><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
       else if (HD == 64)
         depth_attn_kernel<2><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
