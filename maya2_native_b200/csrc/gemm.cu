@@ -193,7 +193,15 @@ int gemm_impl(const GemmDesc& g, int impl, cudaStream_t s) {
   switch (impl) {
     case kGemmGemv: return gemv_only(g, s);
     case kGemmCublas: return g.M == 0 ? M3_OK : launch_cublas(g, s);
-    case kGemmUmma: return g.M == 0 ? M3_OK : umma_gemm(g, g.N >= 4096 ? 128 : 64, 1, false, s);
+    case kGemmUmma:
+    case kGemmUmmaGelu: {
+      if (g.M == 0) return M3_OK;
+      M3_REQUIRE(impl == kGemmUmma || !g.y_f32, M3_ERR_ARG, "the GELU epilogue writes bf16");
+      // widest tile that still gives most SMs a tile: fewer re-reads of A and B through L2
+      const int tiles256 = cdiv(g.M, 128) * cdiv(g.N, 256), tiles128 = cdiv(g.M, 128) * cdiv(g.N, 128);
+      const int bn = (tiles256 >= 120 && g.N % 256 == 0) ? 256 : (tiles128 >= 148 ? 128 : 64);
+      return umma_gemm_persistent(g, bn, impl == kGemmUmmaGelu ? 2 : (g.y_f32 ? 1 : 0), s);
+    }
     default: return gemm(g, s);
   }
 }

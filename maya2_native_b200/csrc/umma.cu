@@ -9,6 +9,8 @@
 // Every wait is bounded (kSpinLimit polls) and reports M3_DEV_TIMEOUT instead of hanging.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -132,6 +134,158 @@ __global__ void __launch_bounds__(kUmmaThreads) umma_gemm_kernel(const __grid_co
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------ persistent kernel
+// Persistent, warp-specialised form: one CTA per SM walks the output tiles (M fastest, so the CTAs running at the
+// same time share B tiles in L2).  Warp 0 (one lane) streams A and B tiles by TMA into a STAGES-deep ring; warp 1
+// (one lane) issues the tcgen05 MMAs into one of two TMEM accumulators and commits the stage's "empty" barrier after
+// each K step and the accumulator's "full" barrier after the last; warps 2-5 (each reads the 32 TMEM lanes its warp
+// index allows) drain the other accumulator meanwhile -- so the epilogue of tile i overlaps the main loop of tile
+// i+1 -- and re-arm it.  EPI: 0 bf16 rows, 1 fp32 rows, 2 bf16(GELU_erf(bf16(z))) (the depth / Mimi feed-forward
+// activation, rounded where the reference rounds).  Every wait is bounded.
+constexpr int kPThreads = 192;
+
+template <int EPI>
+__device__ __forceinline__ void epi_store(void* Y, int64_t ldy, int row, int col, int N, const uint32_t (&r)[32]) {
+  if (EPI == 1) {
+    float* yr = reinterpret_cast<float*>(Y) + (int64_t)row * ldy + col;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      if (col + j + 4 <= N)
+        *reinterpret_cast<float4*>(yr + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                          __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+  } else {
+    bf16* yr = reinterpret_cast<bf16*>(Y) + (int64_t)row * ldy + col;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      if (col + j + 8 > N) continue;
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        f[e] = __uint_as_float(r[j + e]);
+        if (EPI == 2) {
+          const float v = rbf(f[e]);
+          f[e] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+        }
+      }
+      *reinterpret_cast<uint4*>(yr + j) = pack8(f);
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1) umma_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                       const __grid_constant__ CUtensorMap tmB,
+                                                                       void* __restrict__ Y, int64_t ldy, int M,
+                                                                       int N, int K, int* status) {
+  constexpr int kABytes = kBM * kBK * 2, kBBytes = BN * kBK * 2, kStage = kABytes + kBBytes;
+  constexpr int kCols = 2 * BN;  // two accumulators
+  static_assert(kCols == 64 || kCols == 128 || kCols == 256 || kCols == 512, "TMEM allocation is a power of 2");
+  extern __shared__ __align__(1024) unsigned char umma_smem[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(umma_smem) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * kStage);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = cdiv(M, kBM), tiles = mt * cdiv(N, BN), kts = cdiv(K, kBK);
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+        for (int kt = 0; kt < kts; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, status)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = base + s * kStage;
+          mbar_expect_tx(&full[s], kStage);
+          tma_load_2d(st, &tmA, kt * kBK, m0, &full[s]);
+          tma_load_2d(st + kABytes, &tmB, kt * kBK, n0, &full[s]);
+        }
+      }
+      // let every copy in flight land before the CTA can exit (bounded; only matters after a timeout)
+      for (int i = max(0, it - STAGES); i < it; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = umma_idesc(BN);
+      bool ok = true;
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        if (lt >= 2 && !mbar_wait(&tempty[acc], ((lt >> 1) - 1) & 1, status)) break;
+        tmem_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kt = 0; kt < kts; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1, status)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const unsigned char* st = base + s * kStage;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            umma_f16(d, sw128_desc(st + kk * kUmmaK * 2), sw128_desc(st + kABytes + kk * kUmmaK * 2), idesc,
+                     (kt | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {  // epilogue warps
+    const int lane_base = (warp & 3) * 32;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const bool got = mbar_wait(&tfull[acc], (lt >> 1) & 1, status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tmem_fence_after();
+      const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+      const int row = m0 + lane_base + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
+        if (row < M && n0 + c0 < N) epi_store<EPI>(Y, ldy, row, n0 + c0, N, r);
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ host
 namespace {
 EncodeTiled g_encode = nullptr;
@@ -190,6 +344,58 @@ int launch_umma(const CUtensorMap& a, const CUtensorMap& b, void* y, int64_t ldy
   return M3_OK;
 }
 }  // namespace
+
+int umma_status_ptr(int** out);
+
+namespace {
+int g_sm_count = 0;
+
+template <int BN, int STAGES, int EPI>
+int launch_persistent(const CUtensorMap& a, const CUtensorMap& b, void* y, int64_t ldy, int M, int N, int K,
+                      cudaStream_t s, int* st) {
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 256;
+  static bool attr = false;
+  if (!attr) {
+    M3_CUDA(cudaFuncSetAttribute(umma_persistent_kernel<BN, STAGES, EPI>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  if (!g_sm_count) {
+    int dev = 0;
+    M3_CUDA(cudaGetDevice(&dev));
+    M3_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int tiles = cdiv(M, kBM) * cdiv(N, BN);
+  umma_persistent_kernel<BN, STAGES, EPI><<<std::min(tiles, g_sm_count), kPThreads, smem, s>>>(a, b, y, ldy, M, N,
+                                                                                             K, st);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+}  // namespace
+
+// Y = X W^T (epi 0 bf16, 1 fp32, 2 bf16 GELU) with the persistent tcgen05 kernel; bn = 64, 128 or 256.
+int umma_gemm_persistent(const GemmDesc& g, int bn, int epi, cudaStream_t s) {
+  M3_REQUIRE(g.M > 0 && g.N > 0 && g.K > 0 && g.N % 8 == 0 && g.ldy % 8 == 0, M3_ERR_ARG,
+             "umma_gemm_persistent: M=%d N=%d K=%d ldy=%lld", g.M, g.N, g.K, (long long)g.ldy);
+  int* st;
+  M3_TRY(umma_status_ptr(&st));
+  CUtensorMap a, b;
+  M3_TRY(make_map(&a, g.X, g.M, g.K, g.ldx, kBM));
+  M3_TRY(make_map(&b, g.W, g.N, g.K, g.ldw, bn));
+#define M3_PERS(BN_, ST_)                                                                                       \
+  if (epi == 0) return launch_persistent<BN_, ST_, 0>(a, b, g.Y, g.ldy, g.M, g.N, g.K, s, st);                \
+  if (epi == 1) return launch_persistent<BN_, ST_, 1>(a, b, g.Y, g.ldy, g.M, g.N, g.K, s, st);                \
+  return launch_persistent<BN_, ST_, 2>(a, b, g.Y, g.ldy, g.M, g.N, g.K, s, st);
+  switch (bn) {
+    case 64: { M3_PERS(64, 8) }
+    case 128: { M3_PERS(128, 6) }
+    case 256: { M3_PERS(256, 4) }
+    default: break;
+  }
+#undef M3_PERS
+  set_error("umma_gemm_persistent: BN %d unsupported", bn);
+  return M3_ERR_UNSUPPORTED;
+}
 
 int umma_status_ptr(int** out) {
   if (!g_umma_status) {

@@ -207,6 +207,8 @@ def gemm(a):
     lib = L.load()
     print(f"{'layer':16s} {'M':>7s} {'N':>5s} {'K':>5s}   cublas us  tcgen05 us   TF/s(tc)")
     for name, M, N, K in TICK_GEMMS:
+        if a.shape and name != a.shape:
+            continue
         x = torch.randn(M, K, device=dev).to(torch.bfloat16)
         w = torch.randn(N, K, device=dev).to(torch.bfloat16)
         y = torch.empty(M, N, device=dev, dtype=torch.float32)
@@ -242,6 +244,7 @@ def main():
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     a = ap.parse_args()
     {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap}[a.case](a)
 

@@ -6,7 +6,7 @@ import torch
 from maya2_native_b200 import _lib as L
 
 pytestmark = pytest.mark.gpu
-GEMV, CUBLAS, UMMA = 1, 2, 3
+GEMV, CUBLAS, UMMA, UMMA_GELU = 1, 2, 3, 4
 
 
 def run(impl, x, w, y_f32=False):
@@ -45,3 +45,16 @@ def test_gemv_matches_fp32(cuda, M):
     ref = x.float() @ w.float().T
     y = run(GEMV, x, w, y_f32=True)
     assert (y - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 3072, 1024), (2048, 3072, 1024), (300, 520, 136)])
+def test_tensor_core_gemm_gelu_epilogue(cuda, M, N, K):
+    """The fused feed-forward activation: bf16(GELU_erf(bf16(x w^T))), the rounding points of the depth / Mimi MLPs."""
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    z = (x.float() @ w.float().T).to(torch.bfloat16).float()
+    ref = torch.nn.functional.gelu(z)
+    y = run(UMMA_GELU, x, w)
+    torch.cuda.synchronize()
+    assert (y.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
