@@ -71,3 +71,37 @@ def test_geometry_constants():
     assert BASELINE.mimi.samples_per_frame == 1920
     assert BASELINE.depth.group_of_level == (None, 0, 1, 2, 3, 4, 5, 6)
     assert BASELINE.depth.head_dim == 128
+
+
+# ---- argument validation at the boundary: these calls return their status before touching the device, so they
+# run on CPU; the binding raises what the reference raises (ValueError for shapes/arguments, IndexError for slots).
+def test_bad_arguments_map_to_reference_exceptions(lib):
+    with pytest.raises(ValueError, match="bad shape"):
+        L.check(lib.m3_gemm_bf16(None, 8, None, 8, None, 8, 4, 0, 8, 0, None), "m3_gemm_bf16")
+    with pytest.raises(ValueError, match="null argument"):
+        L.check(lib.m3_topk_sample(None, 1, 4, 2048, None, None, 1, 1.0, 50, 0, None, None), "m3_topk_sample")
+    with pytest.raises(ValueError, match="null argument"):
+        L.check(lib.m3_tick_create(None, L.vp()), "m3_tick_create")
+    with pytest.raises(ValueError):
+        L.check(lib.m3_backbone_step(None, None, None, None, None, None, 1, 1, None), "m3_backbone_step")
+
+
+def test_unsupported_geometries_are_rejected(lib):
+    g = BASELINE.backbone
+    cfg = L.BackboneConfig(g.layers, g.hidden, g.heads, g.kv_heads, 64, g.ffn, 4, 512, 16, g.eps)  # head_dim 64
+    w = L.BackboneWeights()
+    h = L.vp()
+    rc = lib.m3_backbone_create(cfg, w, h)
+    assert rc == L.M3_ERR_UNSUPPORTED and b"head_dim" in lib.m3_last_error()
+    bad = _mimi_cfg(BASELINE.mimi)
+    bad.n_ratios = 0
+    assert lib.m3_mimi_state_elems(bad) == -1
+    assert lib.m3_mimi_create(bad, L.MimiWeights(), L.vp()) == L.M3_ERR_ARG
+
+
+def test_status_codes_of_the_binding():
+    assert L.DEV_STATUS[4] == "kernel wait timed out"
+    with pytest.raises(IndexError):
+        L.check(L.M3_ERR_RANGE, "x")
+    with pytest.raises(L.M3Error):
+        L.check(L.M3_ERR_CUDA, "x")
