@@ -144,20 +144,29 @@ __global__ void __launch_bounds__(kUmmaThreads) umma_gemm_kernel(const __grid_co
 // activation, rounded where the reference rounds).  Every wait is bounded.
 constexpr int kPThreads = 192;
 
+// Epilogue of one warp's 32 rows x 32 columns: the values go through a padded shared-memory block so that the
+// global stores are whole 64-byte (bf16) or 128-byte (fp32) row segments, 4 or 8 lanes per row.
+constexpr int kStgStride = 36;  // words per staged row (32 + 4 pad): conflict-free row writes and segment reads
+
 template <int EPI>
-__device__ __forceinline__ void epi_store(void* Y, int64_t ldy, int row, int col, int N, const uint32_t (&r)[32]) {
-  if (EPI == 1) {
-    float* yr = reinterpret_cast<float*>(Y) + (int64_t)row * ldy + col;
+__device__ __forceinline__ void epi_store(void* Y, int64_t ldy, int row0, int M, int col, int N, const uint32_t (&r)[32],
+                                          uint32_t* stg, int lane) {
+  if (EPI == 1) {  // fp32: row = lane, 32 words
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
-      if (col + j + 4 <= N)
-        *reinterpret_cast<float4*>(yr + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                          __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-  } else {
-    bf16* yr = reinterpret_cast<bf16*>(Y) + (int64_t)row * ldy + col;
+      *reinterpret_cast<uint4*>(stg + lane * kStgStride + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // 32 rows x 8 chunks of 16 B
+      const int i = lane + 32 * q, rr = i >> 3, c = i & 7;
+      const int row = row0 + rr;
+      if (row < M && col + c * 4 + 4 <= N)
+        *reinterpret_cast<uint4*>(reinterpret_cast<float*>(Y) + (int64_t)row * ldy + col + c * 4) =
+            *reinterpret_cast<const uint4*>(stg + rr * kStgStride + c * 4);
+    }
+  } else {  // bf16 (optionally GELU): row = lane, 16 words
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
-      if (col + j + 8 > N) continue;
       float f[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -167,9 +176,19 @@ __device__ __forceinline__ void epi_store(void* Y, int64_t ldy, int row, int col
           f[e] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
         }
       }
-      *reinterpret_cast<uint4*>(yr + j) = pack8(f);
+      *reinterpret_cast<uint4*>(stg + lane * kStgStride + j / 2) = pack8(f);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 32 rows x 4 chunks of 16 B
+      const int i = lane + 32 * q, rr = i >> 2, c = i & 3;
+      const int row = row0 + rr;
+      if (row < M && col + c * 8 + 8 <= N)
+        *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(Y) + (int64_t)row * ldy + col + c * 8) =
+            *reinterpret_cast<const uint4*>(stg + rr * kStgStride + c * 4);
     }
   }
+  __syncwarp();
 }
 
 template <int BN, int STAGES, int EPI>
@@ -188,6 +207,7 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_persistent_kernel(const __g
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* stage_out = tmem_slot + 4;  // [4 epilogue warps][32 rows][kStgStride] words
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = cdiv(M, kBM), tiles = mt * cdiv(N, BN), kts = cdiv(K, kBK);
   if (warp == 1) {
@@ -261,6 +281,7 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_persistent_kernel(const __g
     }
   } else {  // epilogue warps
     const int lane_base = (warp & 3) * 32;
+    uint32_t* stg = stage_out + (warp - 2) * 32 * kStgStride;
     int lt = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
       const int acc = lt & 1;
@@ -268,12 +289,11 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_persistent_kernel(const __g
       if (!__all_sync(0xffffffffu, got)) break;
       tmem_fence_after();
       const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
-      const int row = m0 + lane_base + lane;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
-        if (row < M && n0 + c0 < N) epi_store<EPI>(Y, ldy, row, n0 + c0, N, r);
+        if (n0 + c0 < N) epi_store<EPI>(Y, ldy, m0 + lane_base, M, n0 + c0, N, r, stg, lane);
       }
       tmem_fence_before();
       __syncwarp();
@@ -353,7 +373,7 @@ int g_sm_count = 0;
 template <int BN, int STAGES, int EPI>
 int launch_persistent(const CUtensorMap& a, const CUtensorMap& b, void* y, int64_t ldy, int M, int N, int K,
                       cudaStream_t s, int* st) {
-  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 256;
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 256 + 4 * 32 * kStgStride * 4;
   static bool attr = false;
   if (!attr) {
     M3_CUDA(cudaFuncSetAttribute(umma_persistent_kernel<BN, STAGES, EPI>,
