@@ -58,7 +58,7 @@ def args_():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seats", type=int, default=16)
-    ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] TTFA and configs[3] Mimi runs")
+    ap.add_argument("--no-extra", action="store_true", help="skip the configs[4] box, configs[1] TTFA and configs[3] Mimi runs")
     ap.add_argument("--tick-breakdown", action="store_true",
                     help="time each tick of the device-resident run and print the mean for ticks with and without "
                          "admissions (inline prefill rows), then exit")
@@ -75,18 +75,19 @@ def args_():
 class Workload:
     """The closed-loop request stream of configs[2]: a finished seat is refilled immediately."""
 
-    def __init__(self, vocab, seed):
+    def __init__(self, vocab, seed, prompt=PROMPT):
         self.rng = np.random.default_rng(seed)
         self.vocab = vocab
+        self.prompt = prompt
 
     def request(self):
-        P = int(self.rng.integers(PROMPT[0], PROMPT[1] + 1))
+        P = int(self.rng.integers(self.prompt[0], self.prompt[1] + 1))
         T = int(self.rng.integers(TARGET[0], TARGET[1] + 1))
         return self.rng.integers(0, self.vocab, P), T
 
     def steady_state(self):
         """A seat observed at a random time: its request's length is length-biased (density ~ T), its age uniform."""
-        P = int(self.rng.integers(PROMPT[0], PROMPT[1] + 1))
+        P = int(self.rng.integers(self.prompt[0], self.prompt[1] + 1))
         lo, hi = TARGET
         T = int(np.sqrt(self.rng.uniform(lo * lo, hi * hi)))
         age = int(self.rng.integers(0, T))
@@ -337,6 +338,8 @@ def run_native(a, rank, world, local):
         "clocks": clocks,
         "gpu_launches": int(launches),
     }
+    if not a.no_extra:
+        line["box"] = run_box(eng, a, rank, world, dev, value / world)
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -344,6 +347,104 @@ def run_native(a, rank, world, local):
         line["ttfa"] = run_ttfa(dev, a.seed)
         line["mimi"] = run_mimi(dev, a.seed)
     return line
+
+
+BOX_PROMPT = (20, 400)
+BOX_LOAD = 0.9
+
+
+def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=6.0, warm=1.5):
+    """open-loop Poisson arrivals at 90% of the measured capacity (cap_per_gpu audio-s/s per replica,
+    from the configs[2] run just before), routed round-robin over the `world` replicas (maya2_native_b200.router),
+    prompts of U[20,400] random token ids, frame budgets U[100,1500].  Each replica restarts in the steady state of
+    that load (90% of its seats busy, length-biased ages) and runs its engine loop against the wall clock: before
+    every tick it submits the arrivals whose time has come, and a stream's TTFA is its arrival -> the end of the
+    TickEngine.tick that returns its first PCM frame (queueing for a free seat included).  `warm` seconds run first
+    (graphs for the buckets this load reaches are captured up front); the next `duration` seconds are measured.
+    Reported: aggregate audio-s/s (frames delivered over all replicas / the longest replica's window), TTFA p50/p99
+    over all replicas' arrivals."""
+    import torch
+    import torch.distributed as dist
+
+    from maya2_native_b200.router import poisson_arrivals, requests, share
+    mean_frames = (TARGET[0] + TARGET[1]) / 2
+    lam = BOX_LOAD * cap_per_gpu / (mean_frames * FRAME_S)          # streams per second per replica
+    arr = poisson_arrivals(lam * world, warm + duration, seed=a.seed + 4)
+    mine = requests(arr, eng.geom.backbone.vocab, indices=share(len(arr), rank, world), prompt=BOX_PROMPT,
+                    frames=TARGET, seed=a.seed + 4)
+    for s in list(eng.active):
+        eng._release(s)
+    eng.active, eng.pending = [], []
+    wl = Workload(eng.geom.backbone.vocab, a.seed * 7919 + 17 * rank + 4, prompt=BOX_PROMPT)
+    n0 = int(round(BOX_LOAD * a.seats))
+    init_steady_state(eng, wl, n0)
+    # graphs of the buckets this load reaches (seat counts near n0, any admission rows; the oldest seats keep the
+    # context bucket at the capacity), captured before the clock starts
+    tc = time.perf_counter()
+    cb = eng.ctx_buckets[-1]
+    for sb in (b for b in eng.buckets if b >= 0.7 * n0):
+        for rb in (r for r in eng.row_buckets if r >= sb):
+            eng.graph_for(rb, sb, cb)
+    print(f"box: rank {rank} captured {len(eng.graphs)} graphs in {time.perf_counter() - tc:.2f} s", file=sys.stderr)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    k, arrived, ttfa, frames, occ = 0, {}, [], 0, []
+    t_start = None
+    while True:
+        now = time.perf_counter() - t0
+        if now >= warm + duration:
+            break
+        if t_start is None and now >= warm:
+            t_start, frames, occ, n_graphs = now, 0, [], len(eng.graphs)
+        while k < len(mine) and mine[k].t <= now:
+            r = mine[k]
+            s = eng.submit(r.prompt, r.frames)
+            arrived[id(s)] = (r.t, s)
+            k += 1
+        out = eng.tick()
+        t = time.perf_counter() - t0
+        occ.append(len(out))
+        for s, _, _, pcm in out:
+            if pcm is not None:
+                frames += 1
+                ta = arrived.pop(id(s), None)
+                if ta is not None and ta[0] >= warm:
+                    ttfa.append((t - ta[0]) * 1e3)
+    torch.cuda.synchronize()
+    window = time.perf_counter() - t0 - t_start
+    if len(eng.graphs) > n_graphs:
+        print(f"box: rank {rank} captured {len(eng.graphs) - n_graphs} graphs in the window: "
+              f"{list(eng.graphs)[n_graphs:]}", file=sys.stderr)
+    local = (ttfa, frames, window, float(np.mean(occ)) if occ else 0.0, len(eng.pending), len(mine),
+             len(eng.graphs) - n_graphs)
+    return summarize_box(local, world, a.seats, cap_per_gpu)
+
+
+def summarize_box(local, world, seats, cap_per_gpu):
+    """Combine the replicas' configs[4] results (every rank passes its own; all ranks get the summary): local =
+    (TTFA ms list, frames delivered, window s, mean busy seats, streams still queued, arrivals routed here, graphs
+    captured inside the window)."""
+    if world > 1:
+        import torch.distributed as dist
+        got = [None] * world
+        dist.all_gather_object(got, local)
+    else:
+        got = [local]
+    all_ttfa = [x for g in got for x in g[0]]
+    agg = sum(g[1] for g in got) * FRAME_S / max(g[2] for g in got)
+    return {"workload": f"configs[4]: Poisson arrivals at {BOX_LOAD:.0%} of the measured capacity, routed "
+                        f"round-robin over {world} replicas ({seats} seats each), prompts U[20,400] ids, targets "
+                        "U[100,1500] frames",
+            "audio_s_per_s": round(agg, 1), "offered_audio_s_per_s": round(BOX_LOAD * cap_per_gpu * world, 1),
+            "ttfa_p50_ms": round(float(np.percentile(all_ttfa, 50)), 2) if all_ttfa else None,
+            "ttfa_p99_ms": round(float(np.percentile(all_ttfa, 99)), 2) if all_ttfa else None,
+            "first_frames": len(all_ttfa), "arrivals": int(sum(g[5] for g in got)),
+            "mean_busy_seats_per_gpu": round(float(np.mean([g[3] for g in got])), 1),
+            "queued_at_end": int(sum(g[4] for g in got)), "window_s": round(max(g[2] for g in got), 3),
+            "graphs_captured_in_window": int(sum(g[6] for g in got)),
+            "measured": "arrival -> end of the TickEngine.tick returning the stream's first PCM frame (host clock)"}
 
 
 def reduce_over_ranks(dev_ms, e2e_ms, frames, e2e_frames, world, device):

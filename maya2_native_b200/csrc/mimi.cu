@@ -750,13 +750,16 @@ extern "C" int64_t m3_mimi_state_elems(const m3_mimi_config* cfg) {
 static int setup_fused_seanet(m3_mimi* m) {
   const m3_mimi_config& c = m->c;
   const int n = (int)m->stages.size();
-  auto fusable = [&](const StageDims& sd) {
+  auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  auto fusable = [&](int i) {
+    const StageDims& sd = m->stages[i];
     const int hid = sd.cout / c.compress;
     return c.res_kernel == 3 && sd.L >= 16 && convt_fused_ok(sd.cin, sd.cout, sd.r) && res_fused_ok(sd.cout, hid) &&
-           sd.tail_off % 8 == 0 && sd.hist_off % 8 == 0 && (sd.r * sd.cout) % 8 == 0;
+           sd.tail_off % 8 == 0 && sd.hist_off % 8 == 0 && (sd.r * sd.cout) % 8 == 0 && a16(m->convt_b[i]) &&
+           a16(m->res1_w[i]) && a16(m->res2_w[i]);   // the kernels read these with 16-byte loads
   };
   int first = n;
-  while (first > 0 && fusable(m->stages[first - 1])) --first;
+  while (first > 0 && fusable(first - 1)) --first;
   if (first == n || m->state_row % 8 != 0 || n - first > 8) return M3_OK;
   EncodeTiled enc;
   M3_TRY(tensor_map_encoder(&enc));

@@ -20,11 +20,13 @@ namespace m3 {
 
 namespace {
 constexpr int kUM = 128;                                // transposed conv: output rows per tile (tcgen05 M)
+constexpr int kStgRow = 80;                             // transposed conv epilogue staging: bytes per row (64 + pad)
 constexpr int kBM = 128;                                // residual block: output rows per tile (8 warps x 16)
 constexpr int kResThreads = 256;
 constexpr int kResRows = kBM + 2;                       // residual-block tile rows incl. 2 causal history rows
 constexpr uint32_t kResBox = (kResRows * 128 + 1023) / 1024 * 1024;  // 130-row box, padded to the swizzle atom
 int g_sms = 0;
+int g_res_per_sm[2] = {1, 1};  // resident residual-block CTAs per SM (cout 64, 128), from the occupancy calculator
 uint16_t* g_elu_lut = nullptr;  // bf16 ELU of the negative bf16 patterns (one per process; device of the first init)
 
 __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
@@ -107,33 +109,47 @@ __global__ void __launch_bounds__(128) convt_umma_kernel(
   tmem_fence_after();
   const int t = t0 + warp * 32 + lane;
   bf16* st = state + (int64_t)slot32[b] * state_row + tail_off;
+  // The stage buffers are idle once every MMA has completed: each warp stages its 32 rows x 32 columns there
+  // (lane = row, 64 bytes + 16 of padding so the 16-byte writes are conflict-free) and stores them back as
+  // 64-byte row segments, eight rows per instruction.
+  unsigned char* stg = base + warp * (32 * kStgRow);
   if (ok) {
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       uint32_t acc[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, acc);
-      if (t > L) continue;
       const int n = n0 + c0, co0 = n % cout;  // a 32-column chunk never crosses a cout block (cout % 32 == 0)
+      if (t <= L) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        float bv[8], v[8];
-        unpack8(*reinterpret_cast<const uint4*>(bias + co0 + j), bv);
+        for (int j = 0; j < 32; j += 8) {
+          float bv[8], v[8];
+          unpack8(*reinterpret_cast<const uint4*>(bias + co0 + j), bv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = rbf(__uint_as_float(acc[j + e]) + bv[e]);
-        if (t == L) {
+          for (int e = 0; e < 8; ++e) v[e] = rbf(__uint_as_float(acc[j + e]) + bv[e]);
+          if (t == L) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = v[e] - bv[e];
-          *reinterpret_cast<uint4*>(st + n + j) = pack8(v);
-          continue;
+            for (int e = 0; e < 8; ++e) v[e] = v[e] - bv[e];
+            *reinterpret_cast<uint4*>(st + n + j) = pack8(v);
+            continue;
+          }
+          if (t == 0) {
+            float tv[8];
+            unpack8(*reinterpret_cast<const uint4*>(tail_in + (int64_t)b * in_row + n + j), tv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = v[e] + tv[e];
+          }
+          *reinterpret_cast<uint4*>(stg + lane * kStgRow + j * 2) = pack8(v);
         }
-        if (t == 0) {
-          float tv[8];
-          unpack8(*reinterpret_cast<const uint4*>(tail_in + (int64_t)b * in_row + n + j), tv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = v[e] + tv[e];
-        }
-        *reinterpret_cast<uint4*>(u + ((int64_t)b * L + t) * N + n + j) = pack8(v);
       }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rr = i * 8 + (lane >> 2), tt = t0 + warp * 32 + rr;
+        if (tt < L)
+          *reinterpret_cast<uint4*>(u + ((int64_t)b * L + tt) * N + n + (lane & 3) * 8) =
+              *reinterpret_cast<const uint4*>(stg + rr * kStgRow + (lane & 3) * 16);
+      }
+      __syncwarp();
     }
   }
   tmem_fence_before();
@@ -144,16 +160,18 @@ __global__ void __launch_bounds__(128) convt_umma_kernel(
 
 // ------------------------------------------------------------------------------------------------ residual block
 // ELU of a bf16 value by table: every ELU input in the block is an exact bf16 number, so the rounded result
-// bf16(ELU(x)) is a function of the 16 input bits.  x >= 0 maps to itself; negative x with |x| < 8 (15-bit magnitude
-// pattern below kEluLut) reads the table, filled once from expm1f exactly as the elementwise kernels compute it;
-// |x| >= 8 rounds to -1 (e^x < 2^-9); NaN stays NaN.
-constexpr int kEluLut = 0x4100;
+// bf16(ELU(x)) is a function of the 16 input bits.  x >= 0 maps to itself.  For negative x the table covers the
+// magnitudes 2^-9 <= |x| < 8, filled once from expm1f exactly as the elementwise kernels compute it; below 2^-9,
+// expm1(x) = x (1 + x/2 + ...) differs from x by less than 2^-10 of |x|, under half a bf16 unit in the last place
+// (at least 2^-9 of |x|), so bf16(ELU(x)) = x; at |x| >= 8 it rounds to -1 (e^x < 2^-11); NaN stays NaN.
+constexpr uint32_t kEluLo = 0x3B00u;  // bf16 magnitude pattern of 2^-9
+constexpr uint32_t kEluHi = 0x4100u;  // of 8
+constexpr int kEluLut = (int)(kEluHi - kEluLo);
 
 __device__ __forceinline__ uint32_t elu_bits(uint32_t h, const uint16_t* lut) {
-  if (!(h & 0x8000u)) return h;
-  const uint32_t i = h & 0x7FFFu;
-  if (i < (uint32_t)kEluLut) return lut[i];
-  return i > 0x7F80u ? h : 0xBF80u;
+  const uint32_t j = h - (0x8000u | kEluLo);  // unsigned: below the table's first pattern wraps out of range
+  if (j < (uint32_t)kEluLut) return lut[j];
+  return h - (0x8000u | kEluHi) <= 0xFF80u - (0x8000u | kEluHi) ? 0xBF80u : h;  // -inf <= x <= -8: -1
 }
 __device__ __forceinline__ uint32_t elu2(uint32_t v, const uint16_t* lut) {
   return elu_bits(v & 0xFFFFu, lut) | (elu_bits(v >> 16, lut) << 16);
@@ -162,35 +180,43 @@ __device__ __forceinline__ uint32_t elu2(uint32_t v, const uint16_t* lut) {
 __global__ void elu_lut_kernel(uint16_t* __restrict__ lut) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= kEluLut) return;
-  const float x = __uint_as_float(((uint32_t)i | 0x8000u) << 16);
+  const float x = __uint_as_float((((uint32_t)i + kEluLo) | 0x8000u) << 16);
   const __nv_bfloat16 y = __float2bfloat16_rn(elu(x));
   lut[i] = *reinterpret_cast<const uint16_t*>(&y);
 }
 
 // e = ELU(u + b2 + W2 . ELU(b1 + W1 . [ELU(u)[t-2], ELU(u)[t-1], ELU(u)[t]])) for 128 rows per tile, one warp per
 // 16 rows (8 warps): the first GEMM's accumulators become the second GEMM's A fragments in registers.  Values
-// between the steps stay as packed bf16 pairs, each rounding point is one paired conversion.
+// between the steps stay as packed bf16 pairs, each rounding point is one paired conversion.  The tile is ELU'd in
+// place in shared memory after each thread has kept the raw u values its epilogue adds (the residual); with NBUF = 2
+// the next tile's load goes out when a tile starts, with NBUF = 1 (the wide stage, two CTAs per SM) once the first
+// GEMM has read the tile.
 template <int COUT, int HID>
-__global__ void __launch_bounds__(kResThreads) res_fused_kernel(
+struct ResCfg {
+  static constexpr int NBUF = COUT >= 128 ? 1 : 2;
+  static constexpr int MINB = COUT >= 128 ? 2 : 3;  // CTAs per SM the register budget is sized for
+};
+
+template <int COUT, int HID>
+__global__ void __launch_bounds__(kResThreads, (ResCfg<COUT, HID>::MINB)) res_fused_kernel(
     const __grid_constant__ CUtensorMap umap, const bf16* __restrict__ w1, const bf16* __restrict__ b1,
     const bf16* __restrict__ w2, const bf16* __restrict__ b2, const bf16* __restrict__ hist_in, int64_t in_row,
     bf16* __restrict__ state, int64_t state_row, int64_t hist_off, const int* __restrict__ slot32,
     bf16* __restrict__ e, int Lo, int R, const uint16_t* __restrict__ elu_lut, int* status) {
-  constexpr int CB = COUT / 64, K1 = 3 * COUT, NT1 = HID / 8, NT2 = COUT / 8;
+  constexpr int CB = COUT / 64, K1 = 3 * COUT, NT1 = HID / 8, NT2 = COUT / 8, NBUF = ResCfg<COUT, HID>::NBUF;
   static_assert(COUT % 64 == 0 && HID % 16 == 0, "channel counts");
   const int tps = (Lo + kBM - 1) / kBM;
   const int total = R * tps;
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* raw = align1024(smem_raw);                  // [2][CB][kResBox] u as loaded
-  unsigned char* ea = raw + 2 * CB * kResBox;                // [CB][kResBox] ELU(u), history rows patched in
-  bf16* W1 = reinterpret_cast<bf16*>(ea + CB * kResBox);    // [HID][K1 + 8]
+  unsigned char* raw = align1024(smem_raw);                  // [NBUF][CB][kResBox] u as loaded, then ELU(u)
+  bf16* W1 = reinterpret_cast<bf16*>(raw + NBUF * CB * kResBox);  // [HID][K1 + 8]
   bf16* W2 = W1 + HID * (K1 + 8);                            // [COUT][HID + 8]
   uint16_t* lut = reinterpret_cast<uint16_t*>(W2 + COUT * (HID + 8));  // [kEluLut]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(lut + kEluLut);
+  uint32_t* b2s = reinterpret_cast<uint32_t*>(lut + kEluLut);  // [COUT / 2] b2 as bf16 pairs
+  uint64_t* bar = reinterpret_cast<uint64_t*>(b2s + COUT / 2);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tq = lane & 3, jm = lane >> 3;
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int i = 0; i < NBUF; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   for (int i = tid; i < HID * (K1 / 8); i += kResThreads) {
@@ -205,8 +231,9 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
   }
   for (int i = tid; i < kEluLut / 8; i += kResThreads)
     reinterpret_cast<uint4*>(lut)[i] = reinterpret_cast<const uint4*>(elu_lut)[i];
-  // this thread's bias columns: epilogue 1 (columns kk*16 + 2tq (+1), +8), epilogue 2 (columns ni*8 + 2tq (+1))
-  float bias1[HID / 16][4], bias2[NT2][2];
+  for (int i = tid; i < COUT; i += kResThreads) reinterpret_cast<bf16*>(b2s)[i] = b2[i];
+  // this thread's bias columns of epilogue 1 (columns kk*16 + 2tq (+1), +8)
+  float bias1[HID / 16][4];
 #pragma unroll
   for (int kk = 0; kk < HID / 16; ++kk) {
     const int c0 = kk * 16 + 2 * tq;
@@ -214,11 +241,6 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
     bias1[kk][1] = to_f(b1[c0 + 1]);
     bias1[kk][2] = to_f(b1[c0 + 8]);
     bias1[kk][3] = to_f(b1[c0 + 9]);
-  }
-#pragma unroll
-  for (int ni = 0; ni < NT2; ++ni) {
-    bias2[ni][0] = to_f(b2[ni * 8 + 2 * tq]);
-    bias2[ni][1] = to_f(b2[ni * 8 + 2 * tq + 1]);
   }
   __syncthreads();
   auto issue = [&](int tile, int buf) {
@@ -228,37 +250,51 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
       tma_load_3d(raw + (buf * CB + cb) * kResBox, &umap, cb * 64, t0 - 2, b, &bar[buf]);
   };
   if (tid == 0 && blockIdx.x < total) issue(blockIdx.x, 0);
+  const int m0 = warp * 16;
   int it = 0;
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-    const int buf = it & 1;
+    const int buf = NBUF == 2 ? (it & 1) : 0;
+    const uint32_t parity = (uint32_t)(it / NBUF) & 1u;
     const bool more = tile + gridDim.x < total;
-    if (tid == 0 && more) issue(tile + gridDim.x, buf ^ 1);
-    const bool ok = mbar_wait(&bar[buf], (it >> 1) & 1, status);
+    if (NBUF == 2 && tid == 0 && more) issue(tile + gridDim.x, buf ^ 1);
+    const bool ok = mbar_wait(&bar[buf], parity, status);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) {
-        mbar_wait(&bar[buf], (it >> 1) & 1, nullptr);
-        if (more) mbar_wait(&bar[buf ^ 1], ((it + 1) >> 1) & 1, nullptr);
+        mbar_wait(&bar[buf], parity, nullptr);
+        if (NBUF == 2 && more) mbar_wait(&bar[buf ^ 1], ((it + 1) >> 1) & 1, nullptr);
       }
       __syncthreads();
       return;
     }
     const int b = tile / tps, t0 = (tile % tps) * kBM;
-    const unsigned char* rb = raw + buf * CB * kResBox;
-    // ELU of the tile (an elementwise pass: the swizzled layout is the same in both buffers)
+    unsigned char* rb = raw + buf * CB * kResBox;
+    // the residual: this thread's epilogue elements of u (rows m0 + g (+8), columns ni*8 + 2tq (+1))
+    uint32_t ures[NT2][2];
+#pragma unroll
+    for (int ni = 0; ni < NT2; ++ni)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int co = ni * 8 + 2 * tq;
+        ures[ni][hf] = *reinterpret_cast<const uint32_t*>(rb + (co / 64) * kResBox +
+                                                          sw128(m0 + g + 8 * hf + 2, (co % 64) / 8) + (co % 8) * 2);
+      }
+    __syncthreads();
+    // ELU of the tile in place (an elementwise pass over the swizzled boxes)
     for (int i = tid; i < CB * kResRows * 8; i += kResThreads) {
       const int cb = i / (kResRows * 8), off = (i % (kResRows * 8)) * 16;
-      uint4 v = *reinterpret_cast<const uint4*>(rb + cb * kResBox + off);
+      uint4* p = reinterpret_cast<uint4*>(rb + cb * kResBox + off);
+      uint4 v = *p;
       v.x = elu2(v.x, lut);
       v.y = elu2(v.y, lut);
       v.z = elu2(v.z, lut);
       v.w = elu2(v.w, lut);
-      *reinterpret_cast<uint4*>(ea + cb * kResBox + off) = v;
+      *p = v;
     }
     __syncthreads();
     if (t0 == 0) {  // rows t = -2, -1: the previous frame's ELU'd history
       for (int i = tid; i < 2 * (COUT / 8); i += kResThreads) {
         const int rr = i / (COUT / 8), c8 = i % (COUT / 8);
-        *reinterpret_cast<uint4*>(ea + (c8 / 8) * kResBox + sw128(rr, c8 % 8)) =
+        *reinterpret_cast<uint4*>(rb + (c8 / 8) * kResBox + sw128(rr, c8 % 8)) =
             *reinterpret_cast<const uint4*>(hist_in + (int64_t)b * in_row + rr * COUT + c8 * 8);
       }
       __syncthreads();
@@ -270,10 +306,9 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
       bf16* dst = state + (int64_t)slot32[b] * state_row + hist_off + hr * COUT;
       for (int c8 = tid; c8 < COUT / 8; c8 += kResThreads)
         *reinterpret_cast<uint4*>(dst + c8 * 8) =
-            *reinterpret_cast<const uint4*>(ea + (c8 / 8) * kResBox + sw128(t - t0 + 2, c8 % 8));
+            *reinterpret_cast<const uint4*>(rb + (c8 / 8) * kResBox + sw128(t - t0 + 2, c8 % 8));
     }
     // GEMM 1: 16 rows x HID over K1 = 3 taps x COUT
-    const int m0 = warp * 16;
     float acc1[NT1][4];
 #pragma unroll
     for (int n = 0; n < NT1; ++n) acc1[n][0] = acc1[n][1] = acc1[n][2] = acc1[n][3] = 0.f;
@@ -281,7 +316,7 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
     for (int j = 0; j < 3; ++j)
 #pragma unroll
       for (int cb = 0; cb < CB; ++cb) {
-        const uint32_t eb = smem_u32(ea + cb * kResBox);
+        const uint32_t eb = smem_u32(rb + cb * kResBox);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           uint32_t a0, a1, a2, a3;
@@ -296,6 +331,10 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
           }
         }
       }
+    if (NBUF == 1) {  // every warp has read the tile: the buffer takes the next one while this one finishes
+      __syncthreads();
+      if (tid == 0 && more) issue(tile + gridDim.x, 0);
+    }
     // bf16(ELU(bf16(z + b1))) -> the A fragments of GEMM 2 (k = HID)
     uint32_t a2f[HID / 16][4];
 #pragma unroll
@@ -307,35 +346,41 @@ __global__ void __launch_bounds__(kResThreads) res_fused_kernel(
       a2f[kk][2] = elu2(pack_bf2(hi[0] + bias1[kk][2], hi[1] + bias1[kk][3]), lut);
       a2f[kk][3] = elu2(pack_bf2(hi[2] + bias1[kk][2], hi[3] + bias1[kk][3]), lut);
     }
-    // GEMM 2: 16 rows x COUT over K = HID
-    float acc2[NT2][4];
+    // GEMM 2: 16 rows x COUT over K = HID, 64 output columns at a time
 #pragma unroll
-    for (int n = 0; n < NT2; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
+    for (int c = 0; c < NT2 / 8; ++c) {
+      float acc2[8][4];
 #pragma unroll
-    for (int kk = 0; kk < HID / 16; ++kk)
+      for (int n = 0; n < 8; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
 #pragma unroll
-      for (int nj = 0; nj < NT2 / 2; ++nj) {
-        const int n = nj * 16 + ((jm >> 1) << 3) + (lane & 7);
-        uint32_t q0, q1, q2, q3;
-        ldsm_x4(smem_u32(W2 + n * (HID + 8) + kk * 16 + (jm & 1) * 8), q0, q1, q2, q3);
-        mma_bf16(acc2[2 * nj], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q0, q1);
-        mma_bf16(acc2[2 * nj + 1], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q2, q3);
+      for (int kk = 0; kk < HID / 16; ++kk)
+#pragma unroll
+        for (int nj = 0; nj < 4; ++nj) {
+          const int n = c * 64 + nj * 16 + ((jm >> 1) << 3) + (lane & 7);
+          uint32_t q0, q1, q2, q3;
+          ldsm_x4(smem_u32(W2 + n * (HID + 8) + kk * 16 + (jm & 1) * 8), q0, q1, q2, q3);
+          mma_bf16(acc2[2 * nj], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q0, q1);
+          mma_bf16(acc2[2 * nj + 1], a2f[kk][0], a2f[kk][1], a2f[kk][2], a2f[kk][3], q2, q3);
+        }
+      // y = bf16(u + bf16(z + b2)); e = bf16(ELU(y))
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int ni = c * 8 + n, co = ni * 8 + 2 * tq;
+        const uint32_t bb = b2s[co / 2];
+        const float bl = bf_lo_f(bb), bh = bf_hi_f(bb);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int t = t0 + m0 + g + 8 * hf;
+          if (t >= Lo) continue;
+          const uint32_t uu = ures[ni][hf];
+          const uint32_t z = pack_bf2(acc2[n][2 * hf] + bl, acc2[n][2 * hf + 1] + bh);
+          uint32_t y;  // bf16 + bf16 rounded once: the same as the fp32 sum rounded to bf16
+          asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(y) : "r"(uu), "r"(z));
+          *reinterpret_cast<uint32_t*>(e + ((int64_t)b * Lo + t) * COUT + co) = elu2(y, lut);
+        }
       }
-    // y = bf16(u + bf16(z + b2)); e = bf16(ELU(y))
-#pragma unroll
-    for (int ni = 0; ni < NT2; ++ni)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int m = m0 + g + 8 * hf, t = t0 + m;
-        if (t >= Lo) continue;
-        const int co = ni * 8 + 2 * tq;
-        const uint32_t uu =
-            *reinterpret_cast<const uint32_t*>(rb + (co / 64) * kResBox + sw128(m + 2, (co % 64) / 8) + (co % 8) * 2);
-        const uint32_t z = pack_bf2(acc2[ni][2 * hf] + bias2[ni][0], acc2[ni][2 * hf + 1] + bias2[ni][1]);
-        const uint32_t y = pack_bf2(bf_lo_f(uu) + bf_lo_f(z), bf_hi_f(uu) + bf_hi_f(z));
-        *reinterpret_cast<uint32_t*>(e + ((int64_t)b * Lo + t) * COUT + co) = elu2(y, lut);
-      }
-    __syncthreads();
+    }
+    if (NBUF == 2) __syncthreads();
   }
 }
 
@@ -463,8 +508,9 @@ size_t convt_fused_smem(int cin, int cout, int r) {
   return 1024 + (size_t)convt_stages(BN) * (kUM * 128 + BN * 128) + 8 * (2 * 3 + 1) + 16;
 }
 size_t res_fused_smem(int cout, int hid) {
-  return 1024 + 3 * (size_t)(cout / 64) * kResBox + (size_t)hid * (3 * cout + 8) * 2 + (size_t)cout * (hid + 8) * 2 +
-         (size_t)kEluLut * 2 + 16;
+  const int nbuf = cout >= 128 ? 1 : 2;  // ResCfg::NBUF
+  return 1024 + nbuf * (size_t)(cout / 64) * kResBox + (size_t)hid * (3 * cout + 8) * 2 +
+         (size_t)cout * (hid + 8) * 2 + (size_t)kEluLut * 2 + (size_t)cout * 2 + 16;
 }
 
 int seanet_fused_init() {
@@ -476,6 +522,10 @@ int seanet_fused_init() {
   M3_CUDA(cudaFuncSetAttribute(convt_umma_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
   M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<64, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
   M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<128, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&g_res_per_sm[0], res_fused_kernel<64, 32>, kResThreads,
+                                                        res_fused_smem(64, 32)));
+  M3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&g_res_per_sm[1], res_fused_kernel<128, 64>, kResThreads,
+                                                        res_fused_smem(128, 64)));
   if (!g_elu_lut) {
     M3_CUDA(cudaMalloc(&g_elu_lut, kEluLut * sizeof(uint16_t)));
     elu_lut_kernel<<<(kEluLut + 255) / 256, 256>>>(g_elu_lut);
@@ -506,7 +556,7 @@ int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status) 
 int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status) {
   const int tiles = R * ((p.Lo + kBM - 1) / kBM);
   const size_t smem = res_fused_smem(p.cout, p.hid);
-  const int per_sm = std::max(1, (int)((228 * 1024) / (smem + 1024)));
+  const int per_sm = std::max(1, p.cout == 64 ? g_res_per_sm[0] : g_res_per_sm[1]);
   const dim3 grid(std::max(1, std::min(tiles, g_sms * per_sm)));
   if (p.cout == 64)
     res_fused_kernel<64, 32><<<grid, kResThreads, smem, s>>>(p.umap, p.w1, p.b1, p.w2, p.b2, p.hist_in, p.in_row, p.state,

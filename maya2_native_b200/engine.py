@@ -114,9 +114,10 @@ def plan_layout(dec, new, lengths, row_buckets, seat_buckets, ctx_buckets, dummy
     n_rows = nd + sum(len(t) for _, t in new)
     rb = _bucket(row_buckets, max(n_rows, 1), "rows")
     sb = _bucket(seat_buckets, max(nd + len(new), 1), "seats")
-    need = max([lengths[s] + 1 for s in dec] + [lengths[s] + len(t) for s, t in new] + [1])
+    dl = [lengths[s] for s in dec]
+    need = max(max(dl, default=0) + 1, max((lengths[s] + len(t) for s, t in new), default=1))
     cb = _bucket(ctx_buckets, need, "context")
-    keys = (sum(lengths[s] + 1 for s in dec) + sum(lengths[s] * len(t) + len(t) * (len(t) + 1) // 2 for s, t in new)
+    keys = (sum(dl) + nd + sum(lengths[s] * len(t) + len(t) * (len(t) + 1) // 2 for s, t in new)
             + (rb - n_rows))
     p = np.zeros(4 * rb + 2 * sb, np.int64)
     r_slot, r_off, r_real, r_src = p[:rb], p[rb:2 * rb], p[2 * rb:3 * rb], p[3 * rb:4 * rb]
@@ -405,22 +406,39 @@ class TickEngine:
         return self._deliver(seats, None)
 
     def _deliver(self, seats, hv):
+        """Host bookkeeping after a tick: stop codes, frame counts, finished seats; with a readout, the per-seat
+        (seat, stop code, cb0, int16 PCM view) tuples.  The readout columns are converted once for all seats."""
+        n = len(seats)
         out, finished = [], []
-        for i, s in enumerate(seats):
-            code = int(hv[i, 0]) if hv is not None else 0
-            s.new = False
-            if self.cfg.stops and code:
-                s.stop = REASONS.get(code, str(code))
-                finished.append(s)
-                out.append((s, code, int(hv[i, 1]), None))
-                continue
-            s.frames += 1
-            self.stats["frames"] += 1
-            if hv is not None:
-                out.append((s, code, int(hv[i, 1]), hv[i, 2:].view(np.int16)))
-            if s.frames >= s.max_frames:
-                s.stop = "max_frames"
-                finished.append(s)
+        stops = self.cfg.stops
+        if hv is None:
+            for s in seats:
+                s.new = False
+                s.frames += 1
+                if s.frames >= s.max_frames:
+                    s.stop = "max_frames"
+                    finished.append(s)
+            frames = n
+        else:
+            codes = hv[:n, 0].tolist()
+            cb0s = hv[:n, 1].tolist()
+            pcm = hv[:n, 2:].view(np.int16)
+            frames = 0
+            for i, s in enumerate(seats):
+                s.new = False
+                code = codes[i]
+                if stops and code:
+                    s.stop = REASONS.get(code, str(code))
+                    finished.append(s)
+                    out.append((s, code, cb0s[i], None))
+                    continue
+                s.frames += 1
+                frames += 1
+                out.append((s, code, cb0s[i], pcm[i]))
+                if s.frames >= s.max_frames:
+                    s.stop = "max_frames"
+                    finished.append(s)
+        self.stats["frames"] += frames
         self.active = list(seats)
         if finished:
             gone = {id(s) for s in finished}

@@ -57,3 +57,23 @@ def test_baseline_geometry_wraps_ring_against_oracle(cuda):
     assert snr > 30, snr
     assert sm.tokens[:B].cpu().tolist() == orc.tokens[:B].tolist()
     assert sm.device_status() == 0
+
+
+def test_many_streams_against_oracle_subset(cuda):
+    """160 streams, so the persistent SEANet kernels walk several tiles per CTA (buffer alternation, the next tile's
+    load overlapping the current one); streams are independent, so the oracle decodes a subset of them (first,
+    middle and last slots) from the same codes over three frames (the stage histories and tails cross frames)."""
+    g = BASELINE.mimi
+    W = WG.mimi_weights(g)
+    B = 160
+    pick = [0, 1, 79, 158, 159]
+    sm = StaticMimi(W, B, batch_buckets=(B,), geom=g, device=cuda)
+    orc = MimiOracle({k: v.numpy() for k, v in W.items()}, g, len(pick), "bf16")
+    rng = np.random.default_rng(3)
+    for f in range(3):
+        codes = rng.integers(0, g.codebook_size, (B, g.n_q))
+        got = sm.decode(list(range(B)), torch.from_numpy(codes).to(cuda)).cpu().numpy()
+        ref = orc.decode(np.arange(len(pick)), codes[pick])
+        for i, s in enumerate(pick):
+            assert snr_db(got[s], ref[i]) > 30, (f, s, snr_db(got[s], ref[i]))
+    assert sm.device_status() == 0

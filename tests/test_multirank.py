@@ -49,3 +49,48 @@ def test_reduce_over_ranks_gloo():
 def test_reduce_over_ranks_single():
     import bench
     assert bench.reduce_over_ranks(1.0, 2.0, 3, 4, 1, "cpu") == (1.0, 2.0, 3, 4)
+
+
+def _box_worker(rank, world, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    import bench
+    from maya2_native_b200.router import poisson_arrivals, share
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        # every replica derives its own round-robin share of the same seeded arrival stream
+        arr = poisson_arrivals(100.0, 3.0, seed=5)
+        idx = share(len(arr), rank, world)
+        got = [None] * world
+        dist.all_gather_object(got, idx.tolist())
+        ttfa = [10.0 + rank, 20.0 + rank] if rank == 0 else [30.0]
+        local = (ttfa, 1000 * (rank + 1), 6.0 + rank, 230.0 - rank, rank, len(idx), 0)
+        out[rank] = (len(arr), got, bench.summarize_box(local, world, 256, 2500.0))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_box_router_shares_and_summary_gloo():
+    """configs[4] across two replicas: the round-robin shares partition the arrival stream, and the box summary sums
+    the frames over replicas, divides by the longest window and takes TTFA percentiles over all arrivals."""
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.spawn(_box_worker, args=(world, port, out), nprocs=world, join=True)
+        res = dict(out)
+    n, shares, summ = res[0]
+    assert sorted(shares[0] + shares[1]) == list(range(n)) and not set(shares[0]) & set(shares[1])
+    assert abs(len(shares[0]) - len(shares[1])) <= 1
+    for r in range(world):
+        assert res[r][2] == summ
+    assert summ["audio_s_per_s"] == pytest.approx(3000 * 0.08 / 7.0, abs=0.05)
+    assert summ["offered_audio_s_per_s"] == pytest.approx(0.9 * 2500.0 * 2)
+    assert summ["first_frames"] == 3 and summ["arrivals"] == n and summ["queued_at_end"] == 1
+    assert summ["ttfa_p50_ms"] == pytest.approx(20.0)
+    assert summ["mean_busy_seats_per_gpu"] == pytest.approx(229.5)
