@@ -378,13 +378,14 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=6.0, warm=1.5):
     wl = Workload(eng.geom.backbone.vocab, a.seed * 7919 + 17 * rank + 4, prompt=BOX_PROMPT)
     n0 = int(round(BOX_LOAD * a.seats))
     init_steady_state(eng, wl, n0)
-    # graphs of the buckets this load reaches (seat counts near n0, any admission rows; the oldest seats keep the
-    # context bucket at the capacity), captured before the clock starts
+    # graphs of the buckets this load reaches (seat counts near n0, any admission rows, the two largest context
+    # buckets), captured and uploaded before the clock starts
     tc = time.perf_counter()
-    cb = eng.ctx_buckets[-1]
-    for sb in (b for b in eng.buckets if b >= 0.7 * n0):
-        for rb in (r for r in eng.row_buckets if r >= sb):
-            eng.graph_for(rb, sb, cb)
+    for cb in eng.ctx_buckets[-2:]:
+        for sb in (b for b in eng.buckets if b >= 0.7 * n0):
+            for rb in (r for r in eng.row_buckets if r >= sb):
+                eng.graph_for(rb, sb, cb)
+    torch.cuda.synchronize()
     print(f"box: rank {rank} captured {len(eng.graphs)} graphs in {time.perf_counter() - tc:.2f} s", file=sys.stderr)
     torch.cuda.synchronize()
     if world > 1:

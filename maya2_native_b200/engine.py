@@ -340,6 +340,7 @@ class TickEngine:
             with torch.cuda.graph(g.graph, pool=self.pool):
                 self._launch(g, rb, sb, cb)
             g.launches = L.load().m3_launch_count() - before   # this library's kernels in one replay
+            g.graph.replay()    # the first replay uploads the graph: pay it here, on the idle plan, not in a tick
         else:
             g.launches = None
         self.graphs[key] = g
