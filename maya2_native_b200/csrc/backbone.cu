@@ -109,7 +109,7 @@ __global__ void qk_rope_cache_kernel(const bf16* __restrict__ qkv, bf16* __restr
                                      const bf16* __restrict__ wq, const bf16* __restrict__ wk, float eps, int H,
                                      int KV) {
   const int row = blockIdx.x;
-  const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (head >= H + KV) return;
   const int pos = pos32[row];
   const int D = kHeadDim, half = D / 2;
@@ -643,7 +643,7 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
       M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, bb->y, bb->in_norm[i], c.eps, Hd, s));
     }
     M3_TRY(gemm({bb->y, Hd, bb->wqkv[i], Hd, bb->qkv, qkvw, rows, qkvw, Hd, false}, s));
-    qk_rope_cache_kernel<<<rows, 32 * (c.heads + c.kv_heads), 0, s>>>(
+    qk_rope_cache_kernel<<<dim3(rows, cdiv(c.heads + c.kv_heads, 4)), 128, 0, s>>>(
         bb->qkv, bb->q, bb->kc[i], bb->vc[i], (int64_t)c.kv_heads * c.capacity * c.head_dim,
         (int64_t)c.capacity * c.head_dim, bb->slot32, bb->pos32, bb->cos, bb->sin, bb->q_norm[i], bb->k_norm[i],
         c.eps, c.heads, c.kv_heads);
