@@ -66,7 +66,9 @@ M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
 
 /* m3_gemm_bf16 on a chosen implementation: 0 = automatic (what every stage uses), 1 = the GEMV kernel (m <= 8),
  * 2 = cuBLAS, 3 = this library's tcgen05 tensor-core kernel (persistent, warp-specialised), 4 = the same with the
- * feed-forward activation fused: y = bf16(GELU_erf(bf16(x w^T))) (bf16 output only).  For tests and measurement. */
+ * feed-forward activation fused: y = bf16(GELU_erf(bf16(x w^T))) (bf16 output only), 5 = the cluster split-K
+ * tcgen05 kernel for m <= 256 (bf16 output only; K-slices summed through distributed shared memory).  For tests and
+ * measurement. */
 M3_API int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
                              int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream);
 

@@ -202,6 +202,7 @@ int gemm_impl(const GemmDesc& g, int impl, cudaStream_t s) {
       const int bn = (tiles256 >= 120 && g.N % 256 == 0) ? 256 : (tiles128 >= 148 ? 128 : 64);
       return umma_gemm_persistent(g, bn, impl == kGemmUmmaGelu ? 2 : (g.y_f32 ? 1 : 0), s);
     }
+    case kGemmUmmaSmall: return g.M == 0 ? M3_OK : umma_gemm_small(g, s);
     default: return gemm(g, s);
   }
 }

@@ -306,6 +306,161 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_persistent_kernel(const __g
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------ small-M split-K
+// Y = X W^T for M <= 256 rows (a decode step's batch), where a 128-row tile per CTA leaves most SMs idle and walks
+// all of K.  A cluster of S CTAs owns one BN-column tile: CTA s streams k-tiles [s*KT/S, (s+1)*KT/S) of W and of
+// all 256 rows of X (one 256-row TMA box: rows past M read as zeros) and accumulates both 128-row halves in TMEM
+// (columns [0, BN) and [BN, 2 BN)).  The S partial tiles then meet in shared memory: once the whole cluster is past
+// its main loop, each CTA stores the rows of its fp32 partial that CTA o owns (rows [o*256/S, (o+1)*256/S)) into
+// slot `rank` of CTA o's idle stage buffers through distributed shared memory (remote stores do not stall the
+// sender); after a second cluster barrier each CTA sums its S slots in rank order (a fixed order: reruns are
+// bit-identical), rounds once to bf16 and stores its rows.  Every CTA reaches both barriers on every path (a timed-out
+// wait only skips work), so the cluster never waits on a missing member.
+constexpr int kSmallRows = 256;
+constexpr int kSmallThreads = 128;
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kSmallThreads, 1) umma_small_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                      const __grid_constant__ CUtensorMap tmB,
+                                                                      bf16* __restrict__ Y, int64_t ldy, int M,
+                                                                      int N, int KT, int* status) {
+  constexpr int kABytes = kSmallRows * kBK * 2, kBBytes = BN * kBK * 2, kStage = kABytes + kBBytes;
+  constexpr int kPRow = BN + 4;  // fp32 words per partial row (16 bytes of padding: conflict-free row writes)
+  // S slots of ceil(256 / S) rows each: at most 260 rows for S <= 8
+  static_assert(260 * kPRow * 4 <= STAGES * kStage, "the partial slots must fit in the stage buffers");
+  extern __shared__ __align__(1024) unsigned char umma_smem[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(umma_smem) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * kStage);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  float* part = reinterpret_cast<float*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = gridDim.x, rank = (int)cluster_rank(), n0 = blockIdx.y * BN;
+  const int kt0 = rank * KT / S, kt1 = (rank + 1) * KT / S, nk = kt1 - kt0;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  int issued = 0;
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int kt = 0; kt < nk && ok; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES) ok = mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1, status);
+      if (!ok) break;
+      unsigned char* st = base + s * kStage;
+      mbar_expect_tx(&full[s], kStage);
+      tma_load_2d(st, &tmA, (kt0 + kt) * kBK, 0, &full[s]);
+      tma_load_2d(st + kABytes, &tmB, (kt0 + kt) * kBK, n0, &full[s]);
+      ++issued;
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer: both 128-row halves per k-step
+    constexpr uint32_t idesc = umma_idesc(BN);
+    for (int kt = 0; kt < nk && ok; ++kt) {
+      const int s = kt % STAGES;
+      ok = mbar_wait(&full[s], (kt / STAGES) & 1, status);
+      if (!ok) break;
+      tmem_fence_after();
+      const unsigned char* st = base + s * kStage;
+#pragma unroll
+      for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+        const uint64_t bd = sw128_desc(st + kABytes + kk * kUmmaK * 2);
+        umma_f16(tmem, sw128_desc(st + kk * kUmmaK * 2), bd, idesc, (kt | kk) != 0);
+        umma_f16(tmem + BN, sw128_desc(st + kABytes / 2 + kk * kUmmaK * 2), bd, idesc, (kt | kk) != 0);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);
+  }
+  __syncwarp();
+  ok = mbar_wait(done, 0, status) && ok;
+  if (warp == 0 && lane == 0 && !ok)  // a load may still be landing in the stage buffers: let it finish first
+    for (int kt = 0; kt < issued; ++kt) mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1, nullptr);
+  ok = __syncthreads_and(ok);
+  tmem_fence_after();
+  // Every CTA of the cluster is past its main loop (stage buffers idle): push this CTA's partial rows to the CTA
+  // that owns them (rows [o*256/S, (o+1)*256/S) belong to rank o), into slot `rank` of the owner's buffers.
+  cluster_sync_all();
+  const int rows_max = (kSmallRows + S - 1) / S;
+  if (ok) {
+    const uint32_t pbase = smem_u32(part);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = h * 128 + warp * 32 + lane;
+      int o = r * S / kSmallRows;
+      while (o + 1 < S && (o + 1) * kSmallRows / S <= r) ++o;
+      while (o > 0 && o * kSmallRows / S > r) --o;
+      const uint32_t local = pbase + (uint32_t)(((rank * rows_max + (r - o * kSmallRows / S)) * kPRow) * 4);
+      uint32_t dst;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(local), "r"((uint32_t)o));
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(h * BN + c0), v);
+        if (nk == 0)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0u;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (uint32_t)((c0 + j) * 4)),
+                       "r"(v[j]), "r"(v[j + 1]), "r"(v[j + 2]), "r"(v[j + 3])
+                       : "memory");
+      }
+    }
+  }
+  tmem_fence_before();
+  cluster_sync_all();
+  // rows [r0, r1) of the tile: the sum of the S partials in rank order, rounded once
+  const int r0 = rank * kSmallRows / S, r1 = min((rank + 1) * kSmallRows / S, M);
+  constexpr int kQ = BN / 4;  // float4 columns per row
+  if (ok) {
+    for (int u = threadIdx.x; u < (r1 - r0) * kQ; u += kSmallThreads) {
+      const int lr = u / kQ, q = u % kQ;
+      const float* src = part + lr * kPRow + q * 4;
+      float4 acc = *reinterpret_cast<const float4*>(src);
+      for (int p = 1; p < S; ++p) {
+        const float4 v = *reinterpret_cast<const float4*>(src + p * rows_max * kPRow);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int col = n0 + q * 4;
+      if (col < N)
+        *reinterpret_cast<uint2*>(Y + (int64_t)(r0 + lr) * ldy + col) =
+            make_uint2(pack2(acc.x, acc.y), pack2(acc.z, acc.w));
+    }
+  }
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ host
 namespace {
 EncodeTiled g_encode = nullptr;
@@ -415,6 +570,56 @@ int umma_gemm_persistent(const GemmDesc& g, int bn, int epi, cudaStream_t s) {
 #undef M3_PERS
   set_error("umma_gemm_persistent: BN %d unsupported", bn);
   return M3_ERR_UNSUPPORTED;
+}
+
+namespace {
+template <int BN, int STAGES>
+int launch_small(const CUtensorMap& a, const CUtensorMap& b, bf16* y, int64_t ldy, int M, int N, int K, int S,
+                 cudaStream_t s, int* st) {
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kSmallRows * kBK * 2 + BN * kBK * 2) + 256;
+  static bool attr = false;
+  if (!attr) {
+    M3_CUDA(cudaFuncSetAttribute(umma_small_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S, (unsigned)cdiv(N, BN), 1);
+  cfg.blockDim = dim3(kSmallThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  M3_CUDA(cudaLaunchKernelEx(&cfg, umma_small_kernel<BN, STAGES>, a, b, y, ldy, M, N, cdiv(K, kBK), st));
+  M3_LAUNCHED();
+  return M3_OK;
+}
+}  // namespace
+
+// Y = X W^T (bf16 out) for M <= 256 with the cluster split-K kernel: BN = 128 when 128-column tiles with up to 8
+// K-splits still give ~96+ CTAs, else 64; S = K-splits per tile (cluster size) so that tiles x S fills the SMs.
+int umma_gemm_small(const GemmDesc& g, cudaStream_t s) {
+  M3_REQUIRE(g.M > 0 && g.M <= kSmallRows && g.N > 0 && g.K > 0 && !g.y_f32 && g.N % 8 == 0 && g.ldy % 4 == 0 &&
+                 (reinterpret_cast<uintptr_t>(g.Y) & 7) == 0,
+             M3_ERR_ARG, "umma_gemm_small: M=%d N=%d K=%d ldy=%lld (M <= 256, bf16 out, N %% 8 == 0)", g.M, g.N, g.K,
+             (long long)g.ldy);
+  int* st;
+  M3_TRY(umma_status_ptr(&st));
+  const int KT = cdiv(g.K, kBK);
+  const int bn = (g.N % 128 == 0 && (g.N / 128) * std::min(8, KT) >= 96) ? 128 : 64;
+  const int tiles = cdiv(g.N, bn);
+  const int S = std::max(1, std::min({8, KT, 148 / tiles}));
+  CUtensorMap a, b;
+  M3_TRY(make_map(&a, g.X, g.M, g.K, g.ldx, kSmallRows));
+  M3_TRY(make_map(&b, g.W, g.N, g.K, g.ldw, bn));
+  bf16* y = reinterpret_cast<bf16*>(g.Y);
+  if (bn == 128) return launch_small<128, 3>(a, b, y, g.ldy, g.M, g.N, g.K, S, s, st);
+  return launch_small<64, 4>(a, b, y, g.ldy, g.M, g.N, g.K, S, s, st);
 }
 
 int umma_status_ptr(int** out) {

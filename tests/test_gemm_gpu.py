@@ -6,7 +6,7 @@ import torch
 from maya2_native_b200 import _lib as L
 
 pytestmark = pytest.mark.gpu
-GEMV, CUBLAS, UMMA, UMMA_GELU = 1, 2, 3, 4
+GEMV, CUBLAS, UMMA, UMMA_GELU, UMMA_SMALL = 1, 2, 3, 4, 5
 
 
 def run(impl, x, w, y_f32=False):
@@ -58,3 +58,22 @@ def test_tensor_core_gemm_gelu_epilogue(cuda, M, N, K):
     y = run(UMMA_GELU, x, w)
     torch.cuda.synchronize()
     assert (y.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 64, 64), (37, 1024, 2048), (128, 4096, 1024), (160, 6144, 1024),
+                                   (256, 1024, 3072), (256, 4096, 1024), (200, 520, 136), (256, 64, 4096),
+                                   (256, 3072, 1024), (96, 2048, 1000)])
+def test_small_m_cluster_gemm_matches_fp32(cuda, M, N, K):
+    """The cluster split-K kernel for decode-sized batches (M <= 256): K-slices summed across the cluster through
+    distributed shared memory, one bf16 rounding; ragged M (rows past M read as zeros), N and K tails."""
+    g = torch.Generator(device=cuda).manual_seed(M * 5 + N + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    ref = x.float() @ w.float().T
+    y = run(UMMA_SMALL, x, w)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all()
+    err = (y.float() - ref).abs().max().item()
+    assert err <= 1e-2 * max(1.0, ref.abs().max().item()), err
+    y2 = run(UMMA_SMALL, x, w)                    # fixed summation order: bit-identical on a rerun
+    assert torch.equal(y, y2)
