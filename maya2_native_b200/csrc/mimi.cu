@@ -806,12 +806,23 @@ static int setup_fused_seanet(m3_mimi* m) {
       const int N = sd.r * sd.cout, K = 2 * sd.cin;
       const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
       const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-      const cuuint32_t box[2] = {64, (cuuint32_t)convt_fused_bn(N)};
+      const bool pers = convt_persistent_ok(sd.cin, sd.cout, sd.r);
+      const cuuint32_t box[2] = {64, (cuuint32_t)(pers ? 128 : convt_fused_bn(N))};
       const cuuint32_t estr[2] = {1, 1};
       const CUresult r = enc(&ct.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wc, dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       M3_REQUIRE(r == CUDA_SUCCESS, M3_ERR_CUDA, "SEANet weight tensor map failed (%d)", (int)r);
+      if (pers) {  // the persistent form stores u by TMA: [R][L][N], 32 x 32 boxes, 64-byte swizzle
+        const cuuint64_t ud[3] = {(cuuint64_t)N, (cuuint64_t)sd.L, (cuuint64_t)c.max_rows};
+        const cuuint64_t us[2] = {(cuuint64_t)N * 2, (cuuint64_t)sd.L * N * 2};
+        const cuuint32_t ub[3] = {32, 32, 1};
+        const cuuint32_t ue[3] = {1, 1, 1};
+        const CUresult r2 = enc(&ct.smap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, m->act1, ud, us, ub, ue,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        M3_REQUIRE(r2 == CUDA_SUCCESS, M3_ERR_CUDA, "SEANet output tensor map failed (%d)", (int)r2);
+      }
     }
     wc += (size_t)sd.r * sd.cout * 2 * sd.cin;
     ct.bias = m->convt_b[i];

@@ -158,6 +158,191 @@ __global__ void __launch_bounds__(128) convt_umma_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
+// Persistent form of the same transposed conv for the long stages: a CTA keeps one BN-column slice of the repacked
+// weights resident in shared memory (KT k-tiles, loaded once) and walks a strided list of 128-row tiles of every
+// stream: a TMA producer warp streams the 2-tap A tiles through a STAGES-deep ring, one thread issues the MMAs into
+// two TMEM accumulators (a tile's epilogue overlaps the next tile's MMAs), and eight epilogue warps (two per TMEM
+// lane quarter, each taking half of the columns) apply bias / tail / rounding into a double-buffered per-warp
+// staging block from which one lane issues a TMA bulk store of the 32 x 32 tile (rows past the stream's end are not
+// written).  The bias of the CTA's columns is staged once in shared memory.  Each CTA allocates 2 x 128 TMEM
+// columns: releasing a larger allocation at exit measured several microseconds slower.
+constexpr int kCpEpiWarps = 8;
+constexpr int kCpCtl = 2048;  // barriers, TMEM address and the bias row ahead of the staging blocks
+constexpr int kCpThreads = 64 + 32 * kCpEpiWarps;
+constexpr int kCpStages = 4;
+
+template <int BN, int KT>
+__global__ void __launch_bounds__(kCpThreads, 1) convt_pers_kernel(
+    const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+    const __grid_constant__ CUtensorMap smap, const bf16* __restrict__ bias,
+    const bf16* __restrict__ tail_in, int64_t in_row, bf16* __restrict__ state, int64_t state_row, int64_t tail_off,
+    const int* __restrict__ slot32, bf16* __restrict__ u, int L, int r, int cin, int cout, int R, int* status) {
+  constexpr int kA = kUM * 64 * 2, kBt = BN * 64 * 2, CB = KT / 2;
+  constexpr int kCols = 2 * BN;
+  static_assert(kCols == 256 || kCols == 512, "two accumulators of 128 or 256 columns");
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = align1024(smem_raw);
+  unsigned char* bres = base;                       // [KT][BN rows x 128 B] resident weights
+  unsigned char* astg = bres + KT * kBt;            // [kCpStages][128 rows x 128 B]
+  unsigned char* ctl = astg + kCpStages * kA;     // 256 bytes of barriers and the TMEM address
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(ctl);
+  uint64_t* full = bfull + 1;
+  uint64_t* empty = full + kCpStages;
+  uint64_t* tfull = empty + kCpStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  float* bias_s = reinterpret_cast<float*>(ctl + 256);  // [BN] bias of this CTA's columns
+  unsigned char* stg_all = ctl + kCpCtl;                // [kCpEpiWarps][2 buffers][32 rows x 64 B, 64-byte swizzle]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = r * cout, NC = N / BN, nc = blockIdx.x % NC, cpc = gridDim.x / NC, li = blockIdx.x / NC;
+  const int n0 = nc * BN, TT = (L + 1 + kUM - 1) / kUM, tiles = R * TT;
+  if (li >= cpc) return;  // grid rounding (the host launches NC x cpc CTAs)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(bfull, 1);
+    for (int s = 0; s < kCpStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kCpEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  for (int c = threadIdx.x; c < BN; c += blockDim.x) bias_s[c] = to_f(bias[(n0 + c) % cout]);
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer: the weight slice once, then the A tiles
+      mbar_expect_tx(bfull, KT * kBt);
+      for (int kt = 0; kt < KT; ++kt) tma_load_2d(bres + kt * kBt, &bmap, kt * 64, n0, bfull);
+      bool ok = true;
+      int it = 0;
+      for (int j = li; j < tiles && ok; j += cpc) {
+        const int b = j / TT, t0 = (j % TT) * kUM;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % kCpStages;
+          if (it >= kCpStages && !mbar_wait(&empty[s], ((it / kCpStages) - 1) & 1, status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], kA);
+          tma_load_3d(astg + s * kA, &amap, (kt % CB) * 64, t0 - 1 + kt / CB, b, &full[s]);
+        }
+      }
+      // every copy in flight lands before the CTA can exit (bounded; only matters after a timeout)
+      mbar_wait(bfull, 0, nullptr);
+      for (int i = max(0, it - kCpStages); i < it; ++i) mbar_wait(&full[i % kCpStages], (i / kCpStages) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = umma_idesc(BN);
+      bool ok = mbar_wait(bfull, 0, status);
+      int it = 0, lt = 0;
+      for (int j = li; j < tiles && ok; j += cpc, ++lt) {
+        const int acc = lt & 1;
+        if (lt >= 2 && !mbar_wait(&tempty[acc], ((lt >> 1) - 1) & 1, status)) break;
+        tmem_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % kCpStages;
+          if (!mbar_wait(&full[s], (it / kCpStages) & 1, status)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const unsigned char* a = astg + s * kA;
+          const unsigned char* bt = bres + kt * kBt;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(d, sw128_desc(a + kk * 32), sw128_desc(bt + kk * 32), idesc, (kt | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {  // epilogue warps: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows, columns of half (w - 2) / 4
+    const int lane_base = (warp & 3) * 32, cbeg = ((warp - 2) / 4) * (BN / 2);
+    unsigned char* stg = stg_all + (warp - 2) * 4096;
+    int lt = 0, nst = 0;
+    for (int j = li; j < tiles; j += cpc, ++lt) {
+      const int acc = lt & 1;
+      const bool got = mbar_wait(&tfull[acc], (lt >> 1) & 1, status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tmem_fence_after();
+      const int b = j / TT, t0 = (j % TT) * kUM, t = t0 + lane_base + lane;
+      bf16* st = state + (int64_t)slot32[b] * state_row + tail_off;
+      // one 32-column chunk: bias, the row-0 tail / row-L state special cases, the swizzled staging block, one TMA
+      // store of its 32 rows (the store of the chunk before last must have read its buffer)
+      auto chunk = [&](const uint32_t (&v32)[32], int c0) {
+        const int n = n0 + c0;
+        unsigned char* sb = stg + (nst & 1) * 2048;
+        if (nst >= 2 && lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        if (t <= L) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(v32[q * 8 + e]) + bias_s[c0 + q * 8 + e];
+            if (t == L) {  // the next frame's overlap tail: bf16(bf16(z + b) - b)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = rbf(v[e]) - bias_s[c0 + q * 8 + e];
+              *reinterpret_cast<uint4*>(st + n + q * 8) = pack8(v);
+              continue;
+            }
+            if (t == 0) {  // bf16(bf16(z + b) + previous tail)
+              float tv[8];
+              unpack8(*reinterpret_cast<const uint4*>(tail_in + (int64_t)b * in_row + n + q * 8), tv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = rbf(v[e]) + tv[e];
+            }
+            *reinterpret_cast<uint4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = pack8(v);  // one rounding
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&smap, sb, n, t0 + lane_base, b);
+          bulk_commit();
+        }
+        ++nst;
+      };
+#pragma unroll 1
+      for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += 64) {  // two TMEM loads in flight per step
+        uint32_t va[32], vb[32];
+        const uint32_t ta = tmem + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0);
+        tmem_ld32_async(ta, va);
+        tmem_ld32_async(ta + 32, vb);
+        tmem_wait_ld();
+        chunk(va, c0);
+        chunk(vb, c0 + 32);
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (lane == 0) bulk_wait_all();  // the stores have read their staging blocks and landed before the CTA exits
+    __syncwarp();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+constexpr size_t convt_pers_smem(int bn, int kt) {
+  return 1024 + (size_t)kt * bn * 128 + (size_t)kCpStages * kUM * 128 + kCpCtl + (size_t)kCpEpiWarps * 4096;
+}
+
 // ------------------------------------------------------------------------------------------------ residual block
 // ELU of a bf16 value by table: every ELU input in the block is an exact bf16 number, so the rounded result
 // bf16(ELU(x)) is a function of the 16 input bits.  x >= 0 maps to itself.  For negative x the table covers the
@@ -481,6 +666,11 @@ int launch_convt_repack(const bf16* wt, int r, int cout, int cin, bf16* wc, cuda
 }
 
 int convt_fused_bn(int N) { return convt_bn(N); }
+bool convt_persistent_ok(int cin, int cout, int r) {
+  const int KT = 2 * cin / 64;
+  return convt_fused_ok(cin, cout, r) && (r * cout) % 128 == 0 && (KT == 4 || KT == 8) &&
+         convt_pers_smem(128, KT) <= 227 * 1024;
+}
 
 bool convt_fused_ok(int cin, int cout, int r) {
   const int N = r * cout, BN = convt_bn(N);
@@ -519,6 +709,8 @@ int seanet_fused_init() {
   M3_CUDA(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev));
   const int big = 227 * 1024;
   M3_CUDA(cudaFuncSetAttribute(convt_umma_kernel<128, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaFuncSetAttribute(convt_pers_kernel<128, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  M3_CUDA(cudaFuncSetAttribute(convt_pers_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
   M3_CUDA(cudaFuncSetAttribute(convt_umma_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
   M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<64, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
   M3_CUDA(cudaFuncSetAttribute(res_fused_kernel<128, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
@@ -536,7 +728,22 @@ int seanet_fused_init() {
 }
 
 int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status) {
-  const int N = p.r * p.cout, BN = convt_bn(N);
+  const int N = p.r * p.cout, BN = convt_bn(N), KT = 2 * p.cin / 64;
+  if (convt_persistent_ok(p.cin, p.cout, p.r)) {  // the persistent, weight-resident form (128-column slices)
+    const int NC = N / 128, tiles = R * ((p.L + 1 + kUM - 1) / kUM);
+    const int cpc = std::max(1, std::min(tiles, g_sms / NC));
+    const dim3 grid(NC * cpc);
+    if (KT == 4)
+      convt_pers_kernel<128, 4><<<grid, kCpThreads, convt_pers_smem(128, 4), s>>>(
+          p.amap, p.bmap, p.smap, p.bias, p.tail_in, p.in_row, p.state, p.state_row, p.tail_off, p.slot32, p.u, p.L,
+          p.r, p.cin, p.cout, R, status);
+    else
+      convt_pers_kernel<128, 8><<<grid, kCpThreads, convt_pers_smem(128, 8), s>>>(
+          p.amap, p.bmap, p.smap, p.bias, p.tail_in, p.in_row, p.state, p.state_row, p.tail_off, p.slot32, p.u, p.L,
+          p.r, p.cin, p.cout, R, status);
+    M3_LAUNCHED();
+    return M3_OK;
+  }
   const dim3 grid(N / BN, (p.L + 1 + kUM - 1) / kUM, R);
   const size_t smem = convt_fused_smem(p.cin, p.cout, p.r);
   if (BN == 256)

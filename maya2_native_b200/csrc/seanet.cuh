@@ -14,6 +14,7 @@ namespace m3 {
 struct ConvTFused {
   CUtensorMap amap;          // e as [R][L][cin], box {64 channels, 128 rows, 1}, 128-byte swizzle
   CUtensorMap bmap;          // wc as [r * cout][2 * cin], box {64, BN rows}, 128-byte swizzle
+  CUtensorMap smap;          // u as [R][L][r * cout] for the persistent form's stores: box {32, 32, 1}, 64-byte swizzle
   const bf16* wc;            // [r * cout][2 * cin]: row jj*cout + o = [W[:, o, jj + r], W[:, o, jj]]
   const bf16* bias;          // [cout]
   const bf16* tail_in;       // previous frame's tails, [r * cout] per stream at stride in_row (state snapshot)
@@ -60,6 +61,8 @@ int launch_final_fused(const FinalFused& p, int R, cudaStream_t s, int* status);
 // Kernel shapes supported by the fused forms (other stages use the GEMM + elementwise path), and the transposed
 // conv's output columns per CTA (its weight map's box height).
 int convt_fused_bn(int N);
+// The persistent form (weight slice of 128 columns resident, TMA-store epilogue): its weight box is 128 rows.
+bool convt_persistent_ok(int cin, int cout, int r);
 bool convt_fused_ok(int cin, int cout, int r);
 bool res_fused_ok(int cout, int hid);
 size_t convt_fused_smem(int cin, int cout, int r);
