@@ -528,10 +528,30 @@ def run_mimi(dev, seed, streams=256, warm=130, frames=50):
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / frames
     kv = streams * g.layers * 2 * g.heads * g.ring * (g.hidden // g.heads) * 2
+    # the fused SEANet stages' transposed convs alone (m3_mimi_convt re-runs one on the buffers the last frame left)
+    import ctypes
+
+    from maya2_native_b200 import _lib as L
+    lib, convt = L.load(), []
+    for st in range(len(g.ratios)):
+        nb = ctypes.c_int64(0)
+        if lib.m3_mimi_convt(codec._handle, st, streams, ctypes.byref(nb), L.stream_ptr()) != 0:
+            continue                                        # not a fused stage
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(20):
+            L.check(lib.m3_mimi_convt(codec._handle, st, streams, ctypes.byref(nb), L.stream_ptr()))
+        c1.record()
+        torch.cuda.synchronize()
+        us = c0.elapsed_time(c1) / 20 * 1e3
+        convt.append({"stage": st, "us": round(us, 2), "bytes": int(nb.value),
+                      "hbm_gbs": round(nb.value / (us / 1e6) / 1e9, 1)})
     codec.close()
     return {"samples_per_s": round(streams * g.samples_per_frame / (ms / 1e3)),
             "ms_per_frame": round(ms, 4), "hbm_gbs": round((kv + wbytes) / (ms / 1e3) / 1e9, 1),
-            "workload": "configs[3]: 256 streams, codes U[0,2048) x 8, 130 warm frames, StaticMimi.decode"}
+            "convt": convt,
+            "workload": "configs[3]: 256 streams, codes U[0,2048) x 8, 130 warm frames, StaticMimi.decode; convt = "
+                        "each fused transposed-conv stage alone (bf16 input read + output written, bytes / time)"}
 
 
 def run_stages(a):

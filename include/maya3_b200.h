@@ -279,6 +279,10 @@ M3_API int m3_mimi_reset(m3_mimi* m, int32_t slot, int32_t zero_kv, m3_stream st
 M3_API int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* codes, float* pcm, int32_t rows,
                    m3_stream stream);
 M3_API int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear);
+/* Measurement hook: re-run decoder stage `stage`'s fused transposed conv (a stage of the fused SEANet suffix) over
+ * `rows` streams on the activation buffers the last decode left, writing the overlap tails to a scratch row instead
+ * of the streams' state; *bytes = its algorithmic bytes (bf16 stage input read + stage output written). */
+M3_API int m3_mimi_convt(m3_mimi* m, int32_t stage, int32_t rows, int64_t* bytes, m3_stream stream);
 
 /* ---------------------------------------------------------------------------------------------- tick */
 /* The device half of one engine tick (maya3/engine.py:534-561, Engine._tick from the backbone step through the
