@@ -1032,6 +1032,21 @@ extern "C" int m3_mimi_destroy(m3_mimi* m) {
   return M3_OK;
 }
 
+extern "C" int m3_mimi_convt(m3_mimi* m, int32_t stage, int32_t rows, int64_t* bytes, m3_stream stream) {
+  M3_REQUIRE(m, M3_ERR_ARG, "m3_mimi_convt: null handle");
+  const int n = (int)m->stages.size();
+  M3_REQUIRE(stage >= m->first_fused && stage < n && rows > 0 && rows <= m->c.max_rows, M3_ERR_RANGE,
+             "m3_mimi_convt: stage %d is not a fused stage or rows %d out of range", stage, rows);
+  const StageDims& sd = m->stages[stage];
+  ConvTFused ct = m->ct[stage - m->first_fused];
+  // the tails go to the snapshot scratch (re-taken at the start of every decode), not to the streams' state
+  ct.state = m->snap + m->snap_regions.dst_off[2 * (stage - m->first_fused)];
+  ct.state_row = 0;
+  ct.tail_off = 0;
+  if (bytes) *bytes = ((int64_t)rows * sd.L * sd.cin + (int64_t)rows * sd.L * sd.r * sd.cout) * 2;
+  return launch_convt_fused(ct, rows, reinterpret_cast<cudaStream_t>(stream), m->status);
+}
+
 extern "C" int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear) {
   M3_REQUIRE(m && status, M3_ERR_ARG, "m3_mimi_status: null argument");
   M3_CUDA(cudaMemcpy(status, m->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
