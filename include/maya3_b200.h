@@ -56,6 +56,10 @@ M3_API int m3_version(void);
 /* Number of this library's kernel launches issued by this process so far (a launch captured into a CUDA graph
  * counts once at capture; the difference across a capture is the number of library kernels in the graph). */
 M3_API int64_t m3_launch_count(void);
+/* Failure-detection self-test: a kernel waits (at most `polls` polls, <= 2^20) on a barrier that never completes and
+ * takes the bounded-wait exit every kernel of this library has; *status = the device status it recorded
+ * (M3_DEV_TIMEOUT when the wait gave up).  Synchronises with the device; for tests. */
+M3_API int m3_selftest_timeout(int32_t polls, int32_t* status);
 
 /* ---------------------------------------------------------------------------------------------- utilities */
 /* Y[M,N] = X[M,K] . W[N,K]^T, bf16 inputs, fp32 accumulation, Y bf16 (y_f32 = 0) or fp32 (y_f32 = 1).

@@ -48,7 +48,32 @@ __global__ void pack_readout_kernel(const int64_t* __restrict__ code, const int6
   }
 }
 
+// One thread waits, with at most `polls` polls, on an mbarrier that nothing arrives on: the bounded-wait path every
+// kernel of this library takes when a copy or a peer never completes (it records M3_DEV_TIMEOUT and gives up).
+__global__ void selftest_timeout_kernel(int polls, int* status) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  for (int i = 0; i < polls; ++i)
+    if (mbar_try_wait(&bar, 0)) return;
+  report(status, M3_DEV_TIMEOUT);
+  mbar_arrive(&bar);  // complete the phase so the barrier is left in a finished state
+}
+
 }  // namespace m3
+
+extern "C" int m3_selftest_timeout(int32_t polls, int32_t* status) {
+  M3_REQUIRE(status && polls >= 0 && polls <= (1 << 20), M3_ERR_ARG, "m3_selftest_timeout: polls %d", polls);
+  int* d = nullptr;
+  M3_CUDA(cudaMalloc(&d, sizeof(int)));
+  M3_CUDA(cudaMemset(d, 0, sizeof(int)));
+  m3::selftest_timeout_kernel<<<1, 1>>>(polls, d);
+  M3_LAUNCHED();
+  const cudaError_t e = cudaMemcpy(status, d, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  M3_CUDA(e);
+  return M3_OK;
+}
 
 extern "C" const char* m3_last_error(void) { return m3::last_error(); }
 
