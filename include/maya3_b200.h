@@ -76,6 +76,10 @@ M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
 M3_API int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
                              int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream);
 
+/* In place f = bf16(GELU_erf(f)) over n8 groups of 8 bf16 values: the depth and Mimi feed-forward activation
+ * (F.gelu on bf16 tensors) as the stages apply it.  For tests. */
+M3_API int m3_gelu_bf16(void* f, int64_t n8, m3_stream stream);
+
 /* ---------------------------------------------------------------------------------------------- backbone */
 /* Replaces StaticBackbone (serve/fast_backbone.py:111-362): the static-KV Qwen3 decode with per-seat positions. */
 typedef struct m3_backbone m3_backbone;

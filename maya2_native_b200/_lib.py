@@ -109,6 +109,7 @@ SIGNATURES = {
     "m3_mimi_status": (C.c_int, [vp, P(i32), i32]),
     "m3_mimi_convt": (C.c_int, [vp, i32, i32, P(C.c_int64), vp]),
     "m3_selftest_timeout": (C.c_int, [i32, P(i32)]),
+    "m3_gelu_bf16": (C.c_int, [vp, i64, vp]),
     "m3_pack_readout": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
     "m3_tick_create": (C.c_int, [P(TickConfig), P(vp)]),
     "m3_tick_destroy": (C.c_int, [vp]),

@@ -646,3 +646,12 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
   M3_LAUNCHED();
   return M3_OK;
 }
+
+extern "C" int m3_gelu_bf16(void* f, int64_t n8, m3_stream stream) {
+  M3_REQUIRE(f && n8 >= 0, M3_ERR_ARG, "m3_gelu_bf16: bad argument");
+  if (n8 == 0) return M3_OK;
+  m3::gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<m3::bf16*>(f), n8);
+  M3_LAUNCHED();
+  return M3_OK;
+}
