@@ -18,9 +18,6 @@ struct GemmDesc {
 int gemm(const GemmDesc& g, cudaStream_t s);
 // GEMV kernel only (M <= 8, K <= 3072); never calls a library that may allocate.
 int gemv_only(const GemmDesc& g, cudaStream_t s);
-// Tensor-core GEMM (tcgen05, umma.cu): 128 x bn tiles (bn in {64, 128, 256}); partial = fp32 split-K partials
-// [splitk][M][ldy] at Y.
-int umma_gemm(const GemmDesc& g, int bn, int splitk, bool partial, cudaStream_t s);
 // Persistent warp-specialised tcgen05 GEMM; epi 0 = bf16 out, 1 = fp32 out, 2 = bf16(GELU(bf16(z))).
 int umma_gemm_persistent(const GemmDesc& g, int bn, int epi, cudaStream_t s);
 // Cluster split-K tcgen05 GEMM for M <= 256 rows (bf16 out): the S K-slices of a column tile are summed through

@@ -1,12 +1,10 @@
 // Tensor-core linear layers for sm_100a: Y[M,N] = X[M,K] . W[N,K]^T on the 5th-generation tensor cores.
 //
-// One CTA computes a 128 x BN output tile.  Both operands are K-major bf16 and arrive by TMA (2-D tiled copies with
-// 128-byte swizzle, 64 K-elements per stage) into a STAGES-deep shared-memory ring; one elected thread issues
-// tcgen05.mma (kind::f16, fp32 accumulation in tensor memory) four times per stage (UMMA_K = 16) and releases each
-// stage with tcgen05.commit on its "empty" barrier; after the last stage a commit on the "done" barrier hands the
-// accumulator to all four warps, which read their 32 TMEM lanes (= 32 tile rows) with tcgen05.ld and store bf16 or
-// fp32 rows.  Split-K writes fp32 partial tiles [split][M][N] for a consumer that reduces them.
-// Every wait is bounded (kSpinLimit polls) and reports M3_DEV_TIMEOUT instead of hanging.
+// Two kernels: the persistent warp-specialised GEMM (128 x BN output tiles, TMA operand ring, one thread issuing
+// tcgen05.mma into two TMEM accumulators, four epilogue warps) and, for decode-sized batches (M <= 256), a cluster
+// split-K form whose K-slices meet in distributed shared memory.  Both operands are K-major bf16 (2-D tiled TMA
+// copies, 128-byte swizzle, 64 K-elements per stage); MMAs are kind::f16 with fp32 accumulation.  Every wait is
+// bounded (kSpinLimit polls) and reports M3_DEV_TIMEOUT instead of hanging.
 #include <cuda.h>
 
 #include <algorithm>
@@ -23,116 +21,6 @@ namespace m3 {
 constexpr int kBM = 128;
 constexpr int kBK = 64;               // bf16 elements per stage along K = one 128-byte swizzle row
 constexpr int kUmmaK = 16;
-constexpr int kUmmaThreads = 128;
-
-// ------------------------------------------------------------------------------------------------ kernel
-// OUT: 0 = bf16 rows of Y, 1 = fp32 rows of Y, 2 = fp32 split-K partial tile at Y + blockIdx.z * M * ldy.
-template <int BN, int STAGES, int OUT>
-__global__ void __launch_bounds__(kUmmaThreads) umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                                 const __grid_constant__ CUtensorMap tmB,
-                                                                 void* __restrict__ Y, int64_t ldy, int M, int N,
-                                                                 int k_tiles, int* status) {
-  constexpr int kABytes = kBM * kBK * 2;
-  constexpr int kBBytes = BN * kBK * 2;
-  constexpr int kStage = kABytes + kBBytes;
-  extern __shared__ __align__(1024) unsigned char umma_smem[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(umma_smem) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + STAGES * kStage);
-  uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
-  const int kt0 = blockIdx.z * k_tiles;
-
-  if (warp == 0) {  // the whole warp allocates the accumulator columns
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (threadIdx.x == 32) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(done, 1);
-    fence_mbar_init();
-  }
-  tmem_fence_before();
-  __syncthreads();
-  tmem_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  bool ok = true;
-
-  if (warp == 0 && lane == 0) {
-    // producer: TMA both operand tiles of each K stage
-    for (int kt = 0; kt < k_tiles && ok; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES) ok = mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1, status);
-      if (!ok) break;
-      unsigned char* st = base + s * kStage;
-      mbar_expect_tx(&full[s], kStage);
-      tma_load_2d(st, &tmA, (kt0 + kt) * kBK, m0, &full[s]);
-      tma_load_2d(st + kABytes, &tmB, (kt0 + kt) * kBK, n0, &full[s]);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    constexpr uint32_t idesc = umma_idesc(BN);
-    for (int kt = 0; kt < k_tiles && ok; ++kt) {
-      const int s = kt % STAGES;
-      ok = mbar_wait(&full[s], (kt / STAGES) & 1, status);
-      if (!ok) break;
-      tmem_fence_after();
-      const unsigned char* st = base + s * kStage;
-#pragma unroll
-      for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-        umma_f16(tmem, sw128_desc(st + kk * kUmmaK * 2), sw128_desc(st + kABytes + kk * kUmmaK * 2), idesc,
-                 (kt | kk) != 0);
-      umma_commit(&empty[s]);
-    }
-    umma_commit(done);
-  }
-  // epilogue: warp w owns TMEM lanes 32w..32w+31 = tile rows
-  __syncwarp();
-  ok = mbar_wait(done, 0, status) && ok;
-  tmem_fence_after();
-  const int row = m0 + warp * 32 + lane;
-  if (ok) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, r);
-      const int col = n0 + c0;
-      if (row < M && col < N) {
-        if (OUT == 0) {
-          bf16* yr = reinterpret_cast<bf16*>(Y) + (int64_t)row * ldy + col;
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            if (col + j + 8 <= N) {
-              float f[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[j + e]);
-              *reinterpret_cast<uint4*>(yr + j) = pack8(f);
-            }
-          }
-        } else {
-          float* yr = reinterpret_cast<float*>(Y) + (OUT == 2 ? (int64_t)blockIdx.z * M * ldy : 0) +
-                      (int64_t)row * ldy + col;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            if (col + j + 4 <= N)
-              *reinterpret_cast<float4*>(yr + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-        }
-      }
-    }
-  }
-  tmem_fence_before();
-  __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
-}
 
 // ------------------------------------------------------------------------------------------------ persistent kernel
 // Persistent, warp-specialised form: one CTA per SM walks the output tiles (M fastest, so the CTAs running at the
@@ -501,23 +389,6 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int cols, int64_t ld, 
 
 int* g_umma_status = nullptr;  // device status word for the tensor-core GEMM (one per process, device 0 ordinal)
 
-template <int BN, int STAGES, int OUT>
-int launch_umma(const CUtensorMap& a, const CUtensorMap& b, void* y, int64_t ldy, int M, int N, int K, int splitk,
-                cudaStream_t s) {
-  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 256;
-  static bool attr = false;
-  if (!attr) {
-    M3_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, STAGES, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    attr = true;
-  }
-  const int kt_total = cdiv(K, kBK);
-  const int k_tiles = cdiv(kt_total, splitk);
-  dim3 grid(cdiv(N, BN), cdiv(M, kBM), splitk);
-  umma_gemm_kernel<BN, STAGES, OUT><<<grid, kUmmaThreads, smem, s>>>(a, b, y, ldy, M, N, k_tiles, g_umma_status);
-  M3_LAUNCHED();
-  return M3_OK;
-}
 }  // namespace
 
 int umma_status_ptr(int** out);
@@ -631,31 +502,5 @@ int umma_status_ptr(int** out) {
   return M3_OK;
 }
 
-// Y = X W^T on the tensor cores.  splitk > 1 (fp32 partials only) requires K to split into whole 64-wide tiles.
-int umma_gemm(const GemmDesc& g, int bn, int splitk, bool partial, cudaStream_t s) {
-  M3_REQUIRE(g.M > 0 && g.N > 0 && g.K > 0 && g.N % 8 == 0 && g.ldy % 8 == 0, M3_ERR_ARG,
-             "umma_gemm: M=%d N=%d K=%d ldy=%lld", g.M, g.N, g.K, (long long)g.ldy);
-  M3_REQUIRE(splitk >= 1 && (splitk == 1 || (partial && cdiv(g.K, kBK) % splitk == 0)), M3_ERR_ARG,
-             "umma_gemm: split-K %d needs fp32 partials and K tiles divisible by the split", splitk);
-  int* st;
-  M3_TRY(umma_status_ptr(&st));
-  CUtensorMap a, b;
-  M3_TRY(make_map(&a, g.X, g.M, g.K, g.ldx, kBM));
-  M3_TRY(make_map(&b, g.W, g.N, g.K, g.ldw, bn));
-  const int out = partial ? 2 : (g.y_f32 ? 1 : 0);
-#define M3_UMMA(BN_, ST_)                                                                                  \
-  if (out == 0) return launch_umma<BN_, ST_, 0>(a, b, g.Y, g.ldy, g.M, g.N, g.K, 1, s);                     \
-  if (out == 1) return launch_umma<BN_, ST_, 1>(a, b, g.Y, g.ldy, g.M, g.N, g.K, 1, s);                     \
-  return launch_umma<BN_, ST_, 2>(a, b, g.Y, g.ldy, g.M, g.N, g.K, splitk, s);
-  switch (bn) {
-    case 64: { M3_UMMA(64, 4) }
-    case 128: { M3_UMMA(128, 4) }
-    case 256: { M3_UMMA(256, 3) }
-    default: break;
-  }
-#undef M3_UMMA
-  set_error("umma_gemm: BN %d unsupported", bn);
-  return M3_ERR_UNSUPPORTED;
-}
 
 }  // namespace m3
