@@ -568,9 +568,11 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
     const int T = incremental ? 1 : n;
     const int start = incremental ? level : 0;
     const int gl = group * L;
-    // y = n1(x); x (the residual stream) becomes a contiguous copy of the prefix slice
-    M3_TRY(launch_add_ln(R * T, d->prefix + (int64_t)start * D, T, (int64_t)NL * D, D, nullptr, nullptr, 0, nullptr, d->x,
-                  d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D, s));
+    // y = n1(x); x (the residual stream) becomes a contiguous copy of the prefix slice (from level 2 on, the previous
+    // level's sampler did this right after writing the new prefix entry)
+    if (level == 1)
+      M3_TRY(launch_add_ln(R * T, d->prefix + (int64_t)start * D, T, (int64_t)NL * D, D, nullptr, nullptr, 0, nullptr,
+                           d->x, d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D, s));
     int Tr = T;  // rows per seat in the residual stream
     for (int li = 0; li < L; ++li) {
       M3_TRY(gemm({d->y, D, d->qkv[gl + li], D, d->qkvb, 3 * D, R * Tr, 3 * D, D, false}, s));
@@ -632,10 +634,17 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
                  c.n_codes, D, false},
                 s));
     const bool more = n < NL;
+    PrefixLn ln{};
+    if (more) {  // the next level's first LayerNorm (same slice rule as at the top of the loop)
+      const int g2 = c.group_of_level[level + 1];
+      const bool inc2 = g2 == group;
+      ln = PrefixLn{d->prefix, (int64_t)NL * D, inc2 ? level + 1 : 0, inc2 ? 1 : level + 2, d->x, d->y,
+                    d->n1_w[g2 * L], d->n1_b[g2 * L], c.ln_eps};
+    }
     M3_TRY(launch_topk_sample(d->logits, true, c.n_codes, R, c.n_codes, d->row_seed, d->row_ctr, d->slot32, level,
                               c.inv_temp, c.top_k, c.greedy, codes + level, NL,
                               more ? d->embed + (int64_t)level * c.n_codes * D : nullptr, D,
-                              more ? d->prefix + (int64_t)n * D : nullptr, (int64_t)NL * D, s));
+                              more ? d->prefix + (int64_t)n * D : nullptr, (int64_t)NL * D, s, ln));
     previous = group;
   }
   ctr_advance_kernel<<<cdiv(R, 128), 128, 0, s>>>(d->slot32, R, d->row_ctr);

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
     const TL* __restrict__ logits, int64_t ld, int V, const int32_t* __restrict__ seed,
     const int32_t* __restrict__ ctr, const int* __restrict__ slot32, int level, float inv_temp, int k, int greedy,
     int64_t* __restrict__ codes, int64_t code_stride, const bf16* __restrict__ embed, int D,
-    bf16* __restrict__ next_row, int64_t next_stride) {
+    bf16* __restrict__ next_row, int64_t next_stride, PrefixLn ln) {
   __shared__ float redv[32];
   __shared__ int redi[32];
   __shared__ int s_code;
@@ -180,22 +180,56 @@ __global__ void __launch_bounds__(kSampThreads) topk_sample_kernel(
     uint4* dst = reinterpret_cast<uint4*>(next_row + row * next_stride);
     for (int i = tid; i < D / 8; i += kSampThreads) dst[i] = src[i];
   }
+  if (ln.x) {  // the next level's first LayerNorm over this row's prefix (the new entry included)
+    __syncthreads();
+    const int warp = tid >> 5, lane = tid & 31, nv = D / 8;
+    for (int i = warp; i < ln.T; i += kSampThreads / 32) {
+      const uint4* src = reinterpret_cast<const uint4*>(ln.prefix + (int64_t)row * ln.sb + (int64_t)(ln.start + i) * D);
+      uint4* xo = reinterpret_cast<uint4*>(ln.x + ((int64_t)row * ln.T + i) * D);
+      uint4* yo = reinterpret_cast<uint4*>(ln.y + ((int64_t)row * ln.T + i) * D);
+      float v[8], sum = 0.f, sq = 0.f;
+      for (int c = lane; c < nv; c += 32) {
+        unpack8(src[c], v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += v[e];
+      }
+      const float mean = warp_sum(sum) / (float)D;
+      for (int c = lane; c < nv; c += 32) {
+        unpack8(src[c], v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sq = fmaf(v[e] - mean, v[e] - mean, sq);
+      }
+      const float den = sqrtf(warp_sum(sq) / (float)D + ln.eps);
+      for (int c = lane; c < nv; c += 32) {
+        const uint4 raw = src[c];
+        float wv[8], bv[8], o[8];
+        unpack8(raw, v);
+        unpack8(reinterpret_cast<const uint4*>(ln.w)[c], wv);
+        unpack8(reinterpret_cast<const uint4*>(ln.bias)[c], bv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = (v[e] - mean) / den * wv[e] + bv[e];
+        xo[c] = raw;
+        yo[c] = pack8(o);
+      }
+    }
+  }
 }
 
 int launch_topk_sample(const void* logits, bool bf, int64_t ld, int rows, int V, const int32_t* seed,
                        const int32_t* ctr, const int* slot32, int level, float inv_temp, int k, int greedy,
                        int64_t* codes, int64_t code_stride, const bf16* embed, int D, bf16* next_row,
-                       int64_t next_stride, cudaStream_t s) {
+                       int64_t next_stride, cudaStream_t s, const PrefixLn& ln) {
   M3_REQUIRE(V > 0 && V <= kSampThreads * kMaxPer, M3_ERR_UNSUPPORTED, "sampler width %d unsupported", V);
+  M3_REQUIRE(!ln.x || (D % 8 == 0 && ln.y && ln.w && ln.bias && ln.prefix), M3_ERR_ARG, "prefix LayerNorm arguments");
   if (rows == 0) return M3_OK;
   if (bf)
     topk_sample_kernel<bf16><<<rows, kSampThreads, 0, s>>>((const bf16*)logits, ld, V, seed, ctr, slot32, level,
                                                             inv_temp, k, greedy, codes, code_stride, embed, D,
-                                                            next_row, next_stride);
+                                                            next_row, next_stride, ln);
   else
     topk_sample_kernel<float><<<rows, kSampThreads, 0, s>>>((const float*)logits, ld, V, seed, ctr, slot32, level,
                                                              inv_temp, k, greedy, codes, code_stride, embed, D,
-                                                             next_row, next_stride);
+                                                             next_row, next_stride, ln);
   M3_LAUNCHED();
   return M3_OK;
 }
