@@ -117,3 +117,34 @@ def test_tick_eager_prefill_of_a_long_prompt(cuda):
     assert max(r["h_err"]) < 2e-2, r
     assert r["cb0_hit"] / r["cb0_n"] >= 0.9, r
     assert min(r["snr"]) > 30, r
+
+
+def test_stop_code_releases_the_seat(cuda):
+    """Controlled stop through the engine loop (maya3/engine.py:565-635): a seat whose AEOS logit is biased up stops
+    once it has its minimum frames, its last readout row carries the stop code and no PCM, its slot is released and
+    the waiting request takes it on a following tick; the other seat keeps decoding."""
+    W = WG.generate(WG.all_shapes(TINY))
+    cfg = TickConfig(max_seats=2, capacity=64, max_inline_rows=16)
+    eng = TickEngine(TINY, W, cfg, device=cuda)
+    rng = np.random.default_rng(0)
+    a, b, c = (eng.submit(rng.integers(0, TINY.backbone.vocab, 6), 30, seed=11 + i) for i in range(3))
+    eng.tick()
+    assert {a.slot, b.slot} == {0, 1} and c in eng.pending
+    slot_a = a.slot
+    with torch.inference_mode():
+        eng.cb0.aeos_bias[slot_a] = 1e4
+    stop_row = None
+    for _ in range(cfg.min_frames + 4):
+        for s, code, _, pcm in eng.tick():
+            if s is a and code:
+                stop_row = (code, pcm)
+        if stop_row:
+            break
+    assert stop_row is not None and stop_row[1] is None
+    assert a.stop in ("aeos", "aeos_argmax", "aeos_tau", "aeos_hazard") and a.frames >= cfg.min_frames - 1
+    assert a not in eng.active and b in eng.active and b.stop is None
+    for _ in range(2):
+        eng.tick()
+    assert c in eng.active and c.slot == slot_a and c.frames >= 1
+    assert eng.device_status() == 0
+    eng.close()
