@@ -49,7 +49,7 @@ def test_tiny_matches_reference_fixture(cuda, greedy):
     assert fd.device_status() == 0
 
 
-def _oracle_vs_gpu(g, cuda, B, frames, greedy, seed=0):
+def _oracle_vs_gpu(g, cuda, B, frames, greedy, seed=0, forced=False):
     W = WG.depth_weights(g)
     fd = FastDepth(W, B, temp=0.8, top_k=50, batch_buckets=(B,), seed=7, greedy=greedy, geom=g, device=cuda)
     orc = DepthOracle({k: v.numpy() for k, v in W.items()}, g, B, "bf16", temp=0.8, top_k=50, greedy=greedy)
@@ -62,18 +62,29 @@ def _oracle_vs_gpu(g, cuda, B, frames, greedy, seed=0):
     fd.row_seed[:B] = torch.from_numpy(seeds).to(torch.int32)
     orc.row_seed[:B] = seeds
     slots = list(range(B))[::-1]
-    agree, total, fb_err = 0, 0, []
+    agree, total, fb_err, gaps = 0, 0, [], []
     for f in range(frames):
         h = torch.from_numpy(rng.standard_normal((B, g.d_backbone)).astype(np.float32)).to(torch.bfloat16)
         cb0 = rng.integers(0, g.n_codes, B)
         codes, fb = fd(slots, h.to(cuda), torch.from_numpy(cb0).to(cuda))
-        rc, rfb = orc.step(slots, h.float().numpy(), cb0)
-        agree += int((codes.cpu().numpy() == rc).sum())
-        total += rc.size
+        gc = codes.cpu().numpy()
+        # forced: the oracle's prefix follows the GPU's codes, so every level is compared from the same inputs and
+        # one flipped near-tie does not change the levels after it
+        rc, rfb = orc.step(slots, h.float().numpy(), cb0, force=gc if forced else None)
+        c0 = 1 if forced else 0  # forced: count the sampled levels only (column 0 is the given cb0)
+        agree += int((gc[:, c0:] == rc[:, c0:]).sum())
+        total += rc[:, c0:].size
+        if forced and greedy:  # how far apart, in the oracle's own logits, are the two picks of a flipped decision
+            for lv in range(1, rc.shape[1]):
+                for r in np.nonzero(gc[:, lv] != rc[:, lv])[0]:
+                    lg = np.asarray(orc.last_logits[lv - 1][r], np.float64)
+                    gaps.append((lg[rc[r, lv]] - lg[gc[r, lv]]) / max(abs(lg[rc[r, lv]]), 1e-30))
         same = (codes.cpu().numpy() == rc).all(1)
         if same.any():
             fb_err.append(rel_l2(fb.float().cpu().numpy()[same], rfb[same]))
     assert fd.device_status() == 0
+    if forced and greedy:
+        return agree / total, max(fb_err) if fb_err else 0.0, max(gaps) if gaps else 0.0
     return agree / total, max(fb_err) if fb_err else 0.0
 
 
@@ -88,3 +99,16 @@ def test_grouped_levels_incremental_path(cuda):
 def test_baseline_geometry_against_oracle(cuda, greedy):
     acc, err = _oracle_vs_gpu(BASELINE.depth, cuda, B=8, frames=3, greedy=greedy)
     assert acc >= 0.95 and err < 2e-2
+
+
+def test_baseline_geometry_greedy_agreement_over_200_frames(cuda):
+    """Greedy code agreement over 200 frames (2 seats x 7 levels): the GPU's bf16 level loop against the
+    bf16-emulating oracle, every frame from the same hidden state and cb0, each level from the GPU's own prefix.  The
+    logits are bf16 values in the reference too (its heads are bf16 linears), so two correct implementations that
+    accumulate in different orders disagree where the top two logits are within a rounding step: with random-init
+    weights that is about 1.4% of the decisions (98.6% agreement measured), and every disagreement must be such a
+    near tie in the oracle's own logits."""
+    acc, err, gap = _oracle_vs_gpu(BASELINE.depth, cuda, B=2, frames=200, greedy=True, seed=5, forced=True)
+    print("greedy agreement over 200 frames (teacher-forced levels):", acc, "largest flipped gap:", gap)
+    assert acc >= 0.98 and err < 2e-2, (acc, err)
+    assert gap <= 2.0 ** -6, gap          # within a few bf16 steps of each other
