@@ -94,3 +94,38 @@ def test_box_router_shares_and_summary_gloo():
     assert summ["first_frames"] == 3 and summ["arrivals"] == n and summ["queued_at_end"] == 1
     assert summ["ttfa_p50_ms"] == pytest.approx(20.0)
     assert summ["mean_busy_seats_per_gpu"] == pytest.approx(229.5)
+
+
+def _dead_peer_worker(rank, world, port, out):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    import bench
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:          # this replica fails between steps: it never joins the reduction
+        out[rank] = "left"
+        return
+    t0 = time.perf_counter()
+    try:
+        bench.reduce_over_ranks(1.0, 2.0, 3, 4, world, "cpu")
+        out[rank] = "no error"
+    except RuntimeError as e:      # the process group's timeout ends the collective with an error
+        out[rank] = ("error", time.perf_counter() - t0, type(e).__name__)
+
+
+def test_reduction_fails_fast_when_a_replica_dies():
+    """A replica that leaves between steps never joins the timing reduction; the surviving rank's collective ends
+    with an error after the process group's timeout instead of waiting forever (no GPU involved)."""
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        ctx = mp.spawn(_dead_peer_worker, args=(world, port, out), nprocs=world, join=False)
+        ctx.join(60)
+        res = dict(out)
+    assert res.get(1) == "left"
+    assert isinstance(res.get(0), tuple) and res[0][0] == "error" and res[0][1] < 30, res
