@@ -223,7 +223,7 @@ def run_native(a, rank, world, local):
         dec = list(eng.active)
         tp = eng.make_plan(dec, new)
         eng.commit(tp)
-        eng.deliver_forced(dec + new)
+        eng.deliver_forced(tp.dec + tp.new)
         top_up(eng, wl)
         plans.append(tp)
     for tp in plans:

@@ -292,7 +292,11 @@ class TickEngine:
 
     # ---------------------------------------------------------------- plan
     def make_plan(self, dec: list, new: list) -> TickPlan:
-        """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows, then each new seat's inline rows."""
+        """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows, then each new seat's inline rows.
+        Decode seats go longest KV first, so the attention's CTAs with full key chunks are dispatched before the short
+        rows' single partial chunks, which then fill the last wave; the tick's outputs follow the plan's order."""
+        lc = self.backbone.lengths_cpu
+        dec = sorted(dec, key=lambda s: -lc[s.slot])
         p, rb, sb, cb, keys = plan_layout([s.slot for s in dec], [(s.slot, s.inline) for s in new],
                                           self.backbone.lengths_cpu, self.row_buckets, self.buckets,
                                           self.ctx_buckets, self.cfg.max_seats)
@@ -382,7 +386,7 @@ class TickEngine:
         self._evt.record()
         self._evt.synchronize()
         self.commit(tp)
-        return self._deliver(dec + new, host.numpy())
+        return self._deliver(tp.dec + tp.new, host.numpy())
 
     @torch.inference_mode()
     def last_outputs(self, n):

@@ -65,8 +65,8 @@ def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
                 ora.depth.set_speaker(s.slot, null_mem)
             _, last = ora.bb.step_mixed([], None, [(s.slot, embed[s.prompt]) for s in order])
             h_o = np.stack(last)
-        else:
-            h_o = ora.bb.step(list(slots), fb_prev)
+        else:   # the engine orders a tick's seats by KV length, so take each seat's own feedback vector
+            h_o = ora.bb.step(list(slots), np.stack([fb_prev[int(sl)] for sl in slots]))
         res["h_err"].append(float(np.linalg.norm(h_o - h_gpu) / np.linalg.norm(h_o)))
         _, cb0_o, _ = ora.cb0(h_gpu, slots)
         res["cb0_hit"] += int((cb0_o == cb0_gpu).sum())
@@ -79,7 +79,7 @@ def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
         res["fb_err"].append(float(np.abs(fb_o - fb_gpu).max()))
         pcm_o = ora.mimi.decode(slots, codes_gpu)
         res["snr"].append(float(snr_db(pcm_o, pcm_gpu)))
-        fb_prev = fb_gpu
+        fb_prev = {int(sl): fb_gpu[i] for i, sl in enumerate(slots)}
     assert eng.device_status() == 0
     res["eager_prefill_rows"] = eng.stats["eager_prefill_rows"]
     eng.close()
