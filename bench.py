@@ -42,9 +42,9 @@ FRAME_S = 0.08
 PROMPT = (64, 512)
 TARGET = (100, 1500)
 METRIC = "audio-s/s at 256 streams per GPU (continuous batching)"
-# DRAM bytes / algorithmic bytes of attn_mma_kernel from an Nsight Compute capture at 256 seats x 1 layer (894.0 MB
-# read + written for 877.7 MB of K/V, q and o): the whole-block granularity of the last 16 positions of each split.
-ATTN_TRAFFIC_RATIO = 1.0186
+# DRAM bytes / algorithmic bytes of attn_mma_kernel from an Nsight Compute capture at 256 seats x 1 layer (890.9 MB
+# read + written for 877.7 MB of K/V, q and o): the whole-block granularity of the last 16 positions of each row.
+ATTN_TRAFFIC_RATIO = 1.0150
 
 
 def args_():
