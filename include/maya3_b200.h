@@ -125,7 +125,8 @@ M3_API int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t
 M3_API int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clear);
 /* Measurement hook: re-run layer `layer`'s decode attention (split-KV pass + combine) on the queries, slots and
  * positions the last m3_backbone_step left in the handle's scratch (rows and ctx as that step), to time the kernel
- * on the live cache.  Overwrites only the handle's attention output scratch. */
+ * on the live cache (rows beyond any step's are rejected with M3_ERR_RANGE).  Overwrites only the handle's attention
+ * output scratch. */
 M3_API int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream);
 
 /* ---------------------------------------------------------------------------------------------- cb0 sampler */

@@ -17,24 +17,82 @@ constexpr int kHeadDim = 128;
 
 // ------------------------------------------------------------------------------------------------ row setup
 // slot and position of every row, validated once per step (pos = lengths[slot] + offset, read before the step's
-// length update as serve/fast_backbone.py:178-179).
+// length update as serve/fast_backbone.py:178-179), and the order in which the attention visits the rows: longest
+// first (position descending, then row), so the CTAs with the most keys start first and the short rows fill the last
+// wave.  The order is written as one record per visited row, visit[i] = {row, slot, position, 0}, so the attention's
+// CTA finds all three with one 16-byte load.  With `sort` the grid is one CTA of a power of two >= rows threads
+// (<= 1024): rows that already come longest first (as the engine plans a tick) keep the identity order after one block
+// vote, others are sorted in shared memory (bitonic); without `sort` the order is the identity.
+constexpr int kSortRows = 1024;
+
 __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_t* __restrict__ offsets,
                                  const int64_t* __restrict__ lengths, int rows, int max_slots, int capacity,
-                                 int* __restrict__ slot32, int* __restrict__ pos32, int* status) {
+                                 int* __restrict__ slot32, int* __restrict__ pos32, int4* __restrict__ visit,
+                                 int sort, int* status) {
+  __shared__ uint64_t key[kSortRows];
+  __shared__ int slot_of[kSortRows];
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
-  int64_t s = slots[r];
-  if (s < 0 || s > max_slots) {
-    report(status, M3_DEV_BAD_SLOT);
-    s = max_slots;
+  int64_t p = 0;
+  int sl = 0;
+  if (r < rows) {
+    int64_t s = slots[r];
+    if (s < 0 || s > max_slots) {
+      report(status, M3_DEV_BAD_SLOT);
+      s = max_slots;
+    }
+    p = lengths[s] + (offsets ? offsets[r] : 0);
+    if (p < 0 || p >= capacity) {
+      report(status, M3_DEV_BAD_POS);
+      p = p < 0 ? 0 : capacity - 1;
+    }
+    sl = (int)s;
+    slot32[r] = sl;
+    pos32[r] = (int)p;
   }
-  int64_t p = lengths[s] + (offsets ? offsets[r] : 0);
-  if (p < 0 || p >= capacity) {
-    report(status, M3_DEV_BAD_POS);
-    p = p < 0 ? 0 : capacity - 1;
+  if (!sort) {
+    if (r < rows) visit[r] = make_int4(r, sl, (int)p, 0);
+    return;
   }
-  slot32[r] = (int)s;
-  pos32[r] = (int)p;
+  // one CTA, n = blockDim.x: keys (position << 32 | 0x7FFFFFFF - row) sorted descending; padding keys are 0
+  const int t = threadIdx.x, n = blockDim.x;
+  key[t] = t < rows ? ((uint64_t)(uint32_t)p << 32) | (uint32_t)(0x7FFFFFFF - t) : 0ull;
+  slot_of[t] = sl;
+  __syncthreads();
+  if (__syncthreads_and(t + 1 >= rows || key[t] > key[t + 1])) {  // already in order (keys are distinct)
+    if (t < rows) visit[t] = make_int4(t, sl, (int)p, 0);
+    return;
+  }
+  for (int k = 2; k <= n; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int o = t ^ j;
+      if (o > t) {
+        const uint64_t a = key[t], b = key[o];
+        if (((t & k) == 0) == (a < b)) {  // descending within blocks whose bit k is clear, ascending elsewhere
+          key[t] = b;
+          key[o] = a;
+        }
+      }
+      __syncthreads();
+    }
+  if (t < rows) {
+    const int o = 0x7FFFFFFF - (int)(uint32_t)key[t];
+    visit[t] = make_int4(o, slot_of[o], (int)(key[t] >> 32), 0);
+  }
+}
+
+int launch_prep_rows(const int64_t* slots, const int64_t* offsets, const int64_t* lengths, int rows, int max_slots,
+                     int capacity, int* slot32, int* pos32, int4* visit, int* status, cudaStream_t s) {
+  if (rows <= kSortRows) {
+    int n = 32;
+    while (n < rows) n <<= 1;
+    prep_rows_kernel<<<1, n, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, slot32, pos32, visit, 1,
+                                     status);
+  } else {
+    prep_rows_kernel<<<cdiv(rows, 128), 128, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, slot32,
+                                                     pos32, visit, 0, status);
+  }
+  M3_LAUNCHED();
+  return M3_OK;
 }
 
 // lengths.index_add_(0, slots, real) (serve/fast_backbone.py:233); prefill rows of one slot all add.
@@ -252,23 +310,24 @@ constexpr int kMmaAttnSmemBytes = (int)sizeof(MmaAttnSmem) + 1024;  // + alignme
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
-    const int* __restrict__ slot32, const int* __restrict__ pos32, float* __restrict__ part_o,
-    float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out, int nsplit, int chunk, int H,
-    float qscale, int* status) {
+    const int4* __restrict__ visit,
+    float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out,
+    int nsplit, int chunk, int H, float qscale, int* status) {
   static_assert(G <= 8, "the query heads of one kv head fill at most 8 of the 16 mma rows");
   extern __shared__ unsigned char smem_raw[];
   MmaAttnSmem& sm =
       *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const int4 vis = visit[blockIdx.z];  // {row, slot, position}
+  const int split = blockIdx.x, kvh = blockIdx.y, row = vis.x;
   const int KV = gridDim.y;
-  const int pos = pos32[row];
+  const int pos = vis.z;
   const int t0 = split * chunk;
   if (t0 > pos) return;
   const int ntok = min(chunk, pos + 1 - t0);
   const int nblk = cdiv(ntok, kBlkTok);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int zc = slot32[row] * KV + kvh;
+  const int zc = vis.y * KV + kvh;
   const int nmine = warp < nblk ? (nblk - 1 - warp) / 4 + 1 : 0;  // blocks warp, warp + 4, ...
 
   if (tid == 0) {
@@ -451,6 +510,8 @@ struct m3_backbone {
   void* ws = nullptr;
   int* slot32 = nullptr;
   int* pos32 = nullptr;
+  int4* visit = nullptr;   // [max_rows] the attention's rows in visiting order (longest first): {row, slot, pos, 0}
+  int rows_written = 0;     // rows of slot32/pos32/visit some step has written (bounds the measurement hook)
   int* status = nullptr;
   bf16 *h = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *o = nullptr, *a = nullptr, *gu = nullptr,
        *act = nullptr;
@@ -546,7 +607,7 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   const size_t parts = (size_t)R * c.kv_heads * bb->max_split * G;
   size_t bytes = 0;
   auto add = [&](size_t n) { bytes += (n + 255) / 256 * 256; };
-  add(R * 4); add(R * 4); add(256);
+  add(R * 4); add(R * 4); add(R * 16); add(256);
   add((size_t)R * Hd * 2); add((size_t)R * Hd * 2); add((size_t)R * qkvw * 2);
   add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * Hd * 2);
   add((size_t)R * 2 * c.ffn * 2); add((size_t)R * c.ffn * 2);
@@ -560,6 +621,7 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   char* p = (char*)bb->ws;
   bb->slot32 = carve<int>(p, R);
   bb->pos32 = carve<int>(p, R);
+  bb->visit = carve<int4>(p, R);
   bb->status = carve<int>(p, 64);
   bb->h = carve<bf16>(p, (size_t)R * Hd);
   bb->y = carve<bf16>(p, (size_t)R * Hd);
@@ -609,7 +671,8 @@ static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t
   dim3 grid(nsplit, c.kv_heads, rows);
 #define M3_ATTN(GG)                                                                                          \
   attn_mma_kernel<GG><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                         \
-      bb->kmap[layer], bb->vmap[layer], bb->q, bb->slot32, bb->pos32, bb->part_o, bb->part_ml, bb->tickets,    \
+      bb->kmap[layer], bb->vmap[layer], bb->q, bb->visit, bb->part_o, bb->part_ml,    \
+      bb->tickets,                                                                                             \
       bb->o, nsplit, chunk, c.heads, qscale, bb->status);
   if (G == 1) {
     M3_ATTN(1)
@@ -630,11 +693,11 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
   M3_REQUIRE(rows >= 0 && rows <= c.max_rows, M3_ERR_RANGE, "rows %d outside [0, %d]", rows, c.max_rows);
   M3_REQUIRE(ctx > 0 && ctx <= c.capacity, M3_ERR_RANGE, "ctx %d outside (0, %d]", ctx, c.capacity);
   if (rows == 0) return M3_OK;
+  bb->rows_written = std::max(bb->rows_written, (int)rows);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int Hd = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
-  prep_rows_kernel<<<cdiv(rows, 128), 128, 0, s>>>(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity,
-                                                   bb->slot32, bb->pos32, bb->status);
-  M3_LAUNCHED();
+  M3_TRY(launch_prep_rows(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity, bb->slot32, bb->pos32,
+                          bb->visit, bb->status, s));
   const bf16* xin = reinterpret_cast<const bf16*>(x);
   for (int i = 0; i < c.layers; ++i) {
     if (i == 0) {
@@ -672,5 +735,7 @@ extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t row
   M3_REQUIRE(layer >= 0 && layer < bb->c.layers && rows > 0 && rows <= bb->c.max_rows && ctx > 0 &&
                  ctx <= bb->c.capacity,
              M3_ERR_RANGE, "m3_backbone_attention: layer %d rows %d ctx %d out of range", layer, rows, ctx);
+  M3_REQUIRE(rows <= bb->rows_written, M3_ERR_RANGE,
+             "m3_backbone_attention: rows %d beyond the %d rows a backbone step has set up", rows, bb->rows_written);
   return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -293,8 +293,9 @@ class TickEngine:
     # ---------------------------------------------------------------- plan
     def make_plan(self, dec: list, new: list) -> TickPlan:
         """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows, then each new seat's inline rows.
-        Decode seats go longest KV first, so the attention's CTAs with full key chunks are dispatched before the short
-        rows' single partial chunks, which then fill the last wave; the tick's outputs follow the plan's order."""
+        Decode seats go longest KV first, the order in which the backbone step's attention visits rows (it sorts them
+        on the device otherwise), so the step finds them in order and skips its sort; the tick's outputs follow the
+        plan's order."""
         lc = self.backbone.lengths_cpu
         dec = sorted(dec, key=lambda s: -lc[s.slot])
         p, rb, sb, cb, keys = plan_layout([s.slot for s in dec], [(s.slot, s.inline) for s in new],
