@@ -144,7 +144,8 @@ typedef struct {
 } m3_cb0_config;
 
 typedef struct {         /* per-slot state tensors of maya3/engine.py:210-223, each [max_slots + 1] */
-  const void* head;      /* bf16 [n_cls, hidden]  cb0_head.weight */
+  const void* head;      /* bf16 [n_cls, hidden]  cb0_head.weight; copied at create (zero-padded to a multiple of 8
+                          * rows for the head GEMM), so later writes to it are not seen by the handle */
   int64_t* frames;       /* frames generated by the seat */
   const int64_t* min_frames;
   float* hazard;

@@ -481,6 +481,9 @@ struct m3_cb0 {
   const bf16* head = nullptr;
   void* ws = nullptr;
   bf16* logits = nullptr;
+  // n_cls rounded up to 8: the head GEMM runs on a copy of the head padded with zero rows to ldl classes, so the
+  // library GEMM gets a multiple-of-8 output width (an odd width falls to its align-1 split-K kernels, 3x slower)
+  int ldl = 0;
   int* status = nullptr;
 };
 
@@ -491,19 +494,27 @@ extern "C" int m3_cb0_create(const m3_cb0_config* cfg, const m3_cb0_state* s, m3
   M3_REQUIRE(cfg->hidden % 8 == 0, M3_ERR_UNSUPPORTED, "hidden %% 8");
   auto* h = new m3_cb0();
   h->c = *cfg;
-  h->head = (const bf16*)s->head;
   h->st = Cb0Dev{s->frames, s->min_frames, s->hazard, s->aeos_bias, s->temp, s->top_k, s->top_p, s->rep, s->seed,
                  s->ctr, s->hist, cfg->rep_win, cfg->max_slots};
-  const size_t lb = ((size_t)cfg->max_rows * cfg->n_cls * 2 + 255) / 256 * 256;
-  cudaError_t e = cudaMalloc(&h->ws, lb + 256);
+  h->ldl = (cfg->n_cls + 7) / 8 * 8;
+  const size_t lb = ((size_t)cfg->max_rows * h->ldl * 2 + 255) / 256 * 256;
+  const size_t hb = (size_t)h->ldl * cfg->hidden * 2, real = (size_t)cfg->n_cls * cfg->hidden * 2;
+  cudaError_t e = cudaMalloc(&h->ws, lb + 256 + hb);
+  if (e == cudaSuccess) {
+    h->logits = (bf16*)h->ws;
+    h->status = (int*)((char*)h->ws + lb);
+    bf16* head = (bf16*)((char*)h->ws + lb + 256);
+    h->head = head;
+    e = cudaMemset(h->status, 0, 256);
+    if (e == cudaSuccess) e = cudaMemcpy(head, s->head, real, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemset((char*)head + real, 0, hb - real);
+    if (e != cudaSuccess) cudaFree(h->ws);
+  }
   if (e != cudaSuccess) {
     delete h;
-    set_error("m3_cb0_create: cudaMalloc failed: %s", cudaGetErrorString(e));
+    set_error("m3_cb0_create: %s", cudaGetErrorString(e));
     return M3_ERR_CUDA;
   }
-  h->logits = (bf16*)h->ws;
-  h->status = (int*)((char*)h->ws + lb);
-  cudaMemset(h->status, 0, 256);
   *out = h;
   return M3_OK;
 }
@@ -515,14 +526,14 @@ extern "C" int m3_cb0_destroy(m3_cb0* s) {
   return M3_OK;
 }
 
-static int cb0_launch(m3_cb0* s, const void* logits, bool bf, const int64_t* idx, int64_t* code, int64_t* cb0,
-                      int rows, int apply_rep, int apply_top_p, cudaStream_t st) {
+static int cb0_launch(m3_cb0* s, const void* logits, int64_t ld, bool bf, const int64_t* idx, int64_t* code,
+                      int64_t* cb0, int rows, int apply_rep, int apply_top_p, cudaStream_t st) {
   if (rows == 0) return M3_OK;
   if (bf)
-    cb0_sample_kernel<bf16><<<rows, kSampThreads, 0, st>>>((const bf16*)logits, s->c.n_cls, s->c.n_cls, idx,
+    cb0_sample_kernel<bf16><<<rows, kSampThreads, 0, st>>>((const bf16*)logits, ld, s->c.n_cls, idx,
                                                             s->st, apply_rep, apply_top_p, code, cb0, s->status);
   else
-    cb0_sample_kernel<float><<<rows, kSampThreads, 0, st>>>((const float*)logits, s->c.n_cls, s->c.n_cls, idx,
+    cb0_sample_kernel<float><<<rows, kSampThreads, 0, st>>>((const float*)logits, ld, s->c.n_cls, idx,
                                                              s->st, apply_rep, apply_top_p, code, cb0, s->status);
   M3_LAUNCHED();
   return M3_OK;
@@ -534,16 +545,17 @@ extern "C" int m3_cb0_step(m3_cb0* s, const void* h, const int64_t* idx, int64_t
   M3_REQUIRE(rows >= 0 && rows <= s->c.max_rows, M3_ERR_RANGE, "rows %d > max_rows %d", rows, s->c.max_rows);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // cb0_head in the model dtype (bf16 output), read back as fp32 (tts/model/backbone.py:97, engine.py:657)
-  M3_TRY(gemm({(const bf16*)h, s->c.hidden, s->head, s->c.hidden, s->logits, s->c.n_cls, rows, s->c.n_cls,
+  // over the padded head: logits columns n_cls.. are zeros that the sampler never reads
+  M3_TRY(gemm({(const bf16*)h, s->c.hidden, s->head, s->c.hidden, s->logits, s->ldl, rows, s->ldl,
                s->c.hidden, false},
               st));
-  return cb0_launch(s, s->logits, true, idx, code, cb0, rows, apply_rep, apply_top_p, st);
+  return cb0_launch(s, s->logits, s->ldl, true, idx, code, cb0, rows, apply_rep, apply_top_p, st);
 }
 
 extern "C" int m3_cb0_sample_logits(m3_cb0* s, const float* logits, const int64_t* idx, int64_t* code, int64_t* cb0,
                                     int32_t rows, int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
   M3_REQUIRE(s && logits && idx && code && cb0, M3_ERR_ARG, "m3_cb0_sample_logits: null argument");
-  return cb0_launch(s, logits, false, idx, code, cb0, rows, apply_rep, apply_top_p,
+  return cb0_launch(s, logits, s->c.n_cls, false, idx, code, cb0, rows, apply_rep, apply_top_p,
                     reinterpret_cast<cudaStream_t>(stream));
 }
 
