@@ -11,6 +11,7 @@ import pytest
 import torch
 
 from conftest import golden
+from maya2_native_b200 import _lib as L
 from maya2_native_b200 import weights as WG
 from maya2_native_b200.backbone import StaticBackbone
 from maya2_native_b200.config import BASELINE, TINY
@@ -159,3 +160,40 @@ def test_row_validation_matches_reference(cuda):
     sb.lengths_cpu[0] = 16
     with pytest.raises(ValueError):
         sb.step([0], x[:1])
+
+
+def test_row_order_does_not_change_rows(cuda):
+    """The step visits rows longest first whatever order the caller gives (prep_rows_kernel sorts them on the device,
+    or keeps an order that is already longest first): the same seats stepped in a shuffled order and in
+    longest-first order produce the same hidden states and K/V rows per seat (up to accumulation order), and the
+    attention measurement hook refuses rows that no step has set up."""
+    g = dataclasses.replace(BASELINE.backbone, layers=1)
+    W = WG.generate({k: v for k, v in WG.backbone_shapes(g).items() if "embed_tokens" not in k})
+    cap, n = 512, 40
+    kw = dict(capacity=cap, ctx_buckets=(512,), batch_buckets=(64,), geom=g)
+    sbs = [StaticBackbone(W, 48, **kw), StaticBackbone(W, 48, **kw)]
+    lib = L.load()
+    assert lib.m3_backbone_attention(sbs[1]._handle, 0, 1, cap, L.stream_ptr()) == L.M3_ERR_RANGE
+    rng = np.random.default_rng(7)
+    lengths = rng.integers(1, cap - 1, n)
+    gen = torch.Generator().manual_seed(7)
+    for s in range(n):
+        k = torch.randn(1, g.kv_heads, int(lengths[s]), g.head_dim, generator=gen).to(cuda, torch.bfloat16)
+        v = torch.randn(1, g.kv_heads, int(lengths[s]), g.head_dim, generator=gen).to(cuda, torch.bfloat16)
+        for sb in sbs:
+            sb.load_prefix(s, [(k, v)], int(lengths[s]))
+    x = rng.standard_normal((n, g.hidden)).astype(np.float32)
+    shuffled = [int(s) for s in rng.permutation(n)]
+    longest = sorted(range(n), key=lambda s: (-lengths[s], s))
+    ys = [sbs[0].step(shuffled, t(x[shuffled], cuda)).float().cpu().numpy(),
+          sbs[1].step(longest, t(x[longest], cuda)).float().cpu().numpy()]
+    by_slot = [dict(zip(order, y)) for order, y in zip((shuffled, longest), ys)]
+    for s in range(n):
+        assert rel_maxabs(by_slot[0][s], by_slot[1][s]) < 1e-3, s
+        p = int(lengths[s])
+        for c in ("k", "v"):
+            a, b = (getattr(sb, c)[0][s, :, p].float().cpu().numpy() for sb in sbs)
+            assert rel_maxabs(a, b) < 1e-3, (c, s)
+    assert lib.m3_backbone_attention(sbs[1]._handle, 0, n, cap, L.stream_ptr()) == L.M3_OK
+    torch.cuda.synchronize()
+    assert all(sb.device_status() == 0 for sb in sbs)
