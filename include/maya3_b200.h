@@ -325,6 +325,51 @@ M3_API int m3_tick_outputs(m3_tick* t, void** h, int64_t** codes, float** pcm);
 /* First non-zero device status word over the tick and its stage handles; synchronises. */
 M3_API int m3_tick_status(m3_tick* t, int32_t* status, int32_t clear);
 
+/* ---------------------------------------------------------------------------------------------- guards */
+/* The engine's loop guard and frame cap (GuardConfig, maya3/guards.py:49-75; loop_detect_batch, :80-106; the
+ * per-seat update after the readout, maya3/engine.py:571-617), run on the device right after the cb0 sampler
+ * instead of on the host after the tick's sync.  The text-derived parts (the duration prior behind a seat's cap,
+ * the suspend windows of suspend_windows_v2, :128-146) stay on the host and arrive per slot at bind time. */
+typedef struct {
+  int32_t loop;          /* GuardConfig.enabled && GuardConfig.loop: evaluate the loop rule (the cap always applies) */
+  int32_t stall;         /* 32: a stall is the last `stall` codes all equal to the first of them */
+  int32_t period_win;    /* 64: window of the period rule */
+  double period_thr;     /* 0.7: mean of c[t] == c[t-p] over the window at or above which p is a period */
+  int32_t pmin, pmax;    /* 2, 16: periods tried, smallest first; pmax < period_win */
+  int32_t start, every;  /* 32, 2: the rule runs on frames f >= start with f % every == 0 */
+  int32_t mode;          /* 0 = boost (EOS boost, then backstop), 1 = stop at the first loop */
+  float boost;           /* 4.0: AEOS bias while the loop persists */
+  int32_t backstop;      /* 24: frames after the boost began at which a persisting loop stops the seat */
+  int32_t hist;          /* 96: cb0 codes kept per slot; stall, period_win <= hist <= 128 */
+  int32_t max_windows;   /* suspend windows per slot */
+  int32_t max_slots;
+} m3_guard_config;
+
+typedef struct {         /* per-slot state, each [max_slots + 1] unless stated (row max_slots = padding slot) */
+  int32_t* frames;       /* frames delivered in the seat's current piece (_Seat.frames) */
+  const int32_t* cap;    /* the piece's frame cap (_Seat.cap) */
+  int32_t* boost_at;     /* frame at which the current EOS boost began, -1 = none (_Seat.boost_at) */
+  int32_t* n_boost;      /* boosts so far in the piece (_Seat.n_boost) */
+  int32_t* hist;         /* [max_slots + 1, hist] cb0 ring: the code of frame f at (f - 1) % hist (_Seat.hist) */
+  const int32_t* n_windows;  /* suspend windows in use per slot */
+  const int32_t* windows;    /* [max_slots + 1, max_windows, 2] inclusive frame windows (a, b) with no loop action */
+  float* aeos_bias;      /* the cb0 sampler's per-slot AEOS bias (m3_cb0_state.aeos_bias, maya3/engine.py:215) */
+} m3_guard_state;
+
+/* Guard verdicts: the seat's frame is delivered, then the seat finishes (maya3/engine.py:586-614). */
+enum { M3_GUARD_NONE = 0, M3_GUARD_CAP = 1, M3_GUARD_BACKSTOP = 2, M3_GUARD_STALL = 3, M3_GUARD_PERIOD = 4 };
+
+/* One guard update per seat: for a seat whose sampler stop code is 0 (it delivers a frame) the slot's frame count
+ * and cb0 ring advance, the cap is checked, and on due frames outside the suspend windows the loop rule runs and the
+ * EOS boost is set or cleared in aeos_bias (seen by the next tick's sampler, as the reference's host write is).
+ * code: in, the sampler's stop codes [seats]; out, stop | verdict << 8 | n_boost << 16.  Seats on the padding slot
+ * are skipped.  Returns M3_ERR_ARG for a configuration outside the limits above. */
+M3_API int m3_guard_step(const m3_guard_config* cfg, const m3_guard_state* st, const int64_t* slots, int64_t* code,
+                         const int64_t* cb0, int32_t seats, m3_stream stream);
+/* Attach guards to a tick (copied; NULL cfg detaches): m3_tick_run then runs m3_guard_step after the cb0 sampler and
+ * the readout's stop column carries the packed verdicts.  Call before capturing the tick into a graph. */
+M3_API int m3_tick_set_guard(m3_tick* t, const m3_guard_config* cfg, const m3_guard_state* st);
+
 /* ---------------------------------------------------------------------------------------------- readout */
 /* The engine's per-tick readout (maya3/engine.py:557-561): packed [rows, 2 + spf / 4] int64 rows holding
  * (stop code, cb0, PCM as int16 = round(clamp(pcm, -1, 1) * 32767)). */

@@ -42,6 +42,17 @@ class Cb0State(C.Structure):
                 ("top_k", vp), ("top_p", vp), ("rep", vp), ("seed", vp), ("ctr", vp), ("hist", vp)]
 
 
+class GuardConfig(C.Structure):
+    _fields_ = [("loop", i32), ("stall", i32), ("period_win", i32), ("period_thr", C.c_double), ("pmin", i32),
+                ("pmax", i32), ("start", i32), ("every", i32), ("mode", i32), ("boost", f32), ("backstop", i32),
+                ("hist", i32), ("max_windows", i32), ("max_slots", i32)]
+
+
+class GuardState(C.Structure):
+    _fields_ = [("frames", vp), ("cap", vp), ("boost_at", vp), ("n_boost", vp), ("hist", vp), ("n_windows", vp),
+                ("windows", vp), ("aeos_bias", vp)]
+
+
 class DepthConfig(C.Structure):
     _fields_ = [("layers", i32), ("d", i32), ("heads", i32), ("ffn", i32), ("n_q", i32), ("n_codes", i32),
                 ("d_backbone", i32), ("n_groups", i32), ("group_of_level", i32 * 64), ("max_slots", i32),
@@ -116,6 +127,8 @@ SIGNATURES = {
     "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     "m3_tick_outputs": (C.c_int, [vp, P(vp), P(vp), P(vp)]),
     "m3_tick_status": (C.c_int, [vp, P(i32), i32]),
+    "m3_guard_step": (C.c_int, [P(GuardConfig), P(GuardState), vp, vp, vp, i32, vp]),
+    "m3_tick_set_guard": (C.c_int, [vp, P(GuardConfig), P(GuardState)]),
 }
 
 _lock = threading.Lock()

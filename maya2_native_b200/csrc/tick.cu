@@ -9,6 +9,8 @@
 
 namespace m3 {
 
+int guard_check(const m3_guard_config* c, const m3_guard_state* s);  // guard.cu
+
 // x[r] = feedback[slot[r]] for decode rows (token == kFromFeedback), embed[token[r]] for prefill rows, zero for
 // padding rows (token == -1).
 constexpr int64_t kFromFeedback = -2;
@@ -68,6 +70,9 @@ struct m3_tick {
   int64_t *code = nullptr, *cb0 = nullptr, *codes = nullptr;
   float* pcm = nullptr;
   int* status = nullptr;
+  bool guard = false;  // m3_tick_set_guard: run the guards after the cb0 sampler
+  m3_guard_config gc{};
+  m3_guard_state gs{};
 };
 
 extern "C" int m3_tick_create(const m3_tick_config* cfg, m3_tick** out) {
@@ -152,11 +157,27 @@ extern "C" int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_
   gather_rows_kernel<<<seats, 128, 0, s>>>(t->out, s_row, rows > 0 ? rows : 1, t->h, D);
   M3_LAUNCHED();
   M3_TRY(m3_cb0_step(c.cb0, t->h, s_slot, t->code, t->cb0, seats, apply_rep, apply_top_p, stream));
+  if (t->guard) M3_TRY(m3_guard_step(&t->gc, &t->gs, s_slot, t->code, t->cb0, seats, stream));
   M3_TRY(m3_depth_step(c.depth, s_slot, t->h, t->cb0, t->codes, t->fb, seats, stream));
   scatter_rows_kernel<<<seats, 128, 0, s>>>(t->fb, s_slot, seats, c.max_slots - 1, (bf16*)c.feedback, D);
   M3_LAUNCHED();
   M3_TRY(m3_mimi_decode(c.mimi, s_slot, t->codes, t->pcm, seats, stream));
   M3_TRY(m3_pack_readout(t->code, t->cb0, t->pcm, packed, seats, c.spf, stream));
+  return M3_OK;
+}
+
+extern "C" int m3_tick_set_guard(m3_tick* t, const m3_guard_config* cfg, const m3_guard_state* st) {
+  M3_REQUIRE(t, M3_ERR_ARG, "m3_tick_set_guard: null handle");
+  if (!cfg) {
+    t->guard = false;
+    return M3_OK;
+  }
+  M3_TRY(guard_check(cfg, st));
+  M3_REQUIRE(cfg->max_slots == t->c.max_slots, M3_ERR_ARG, "m3_tick_set_guard: guard max_slots %d, tick max_slots %d",
+             cfg->max_slots, t->c.max_slots);
+  t->gc = *cfg;
+  t->gs = *st;
+  t->guard = true;
   return M3_OK;
 }
 

@@ -3,9 +3,11 @@
 What the reference's engine thread does per 80 ms frame for all seats -- admit new requests into free slots with an
 inline prefill of their prompt, one backbone step over decode + prefill rows, the cb0 sampler, the depth loop, the
 Mimi frame, one device->host readout and one sync (maya3/engine.py:514-630) -- is here one ``m3_tick_run`` call
-replayed from a CUDA graph per (row bucket, seat bucket, context bucket), plus the host bookkeeping around it.  Text
-normalisation, prompt building, voices and the loop guards stay above this layer (host-side, outside the decode
-step); a request here is a prompt of backbone token ids and a frame budget.
+replayed from a CUDA graph per (row bucket, seat bucket, context bucket), plus the host bookkeeping around it.  With
+``TickConfig.guards`` set, the loop guard and frame cap (maya3/engine.py:571-617) run inside the tick on the device
+(guards.py); their text-derived inputs (a piece's cap from the duration prior, its suspend windows) come with the
+request.  Text normalisation, prompt building and voices stay above this layer; a request here is a prompt of
+backbone token ids and a frame budget.
 """
 from __future__ import annotations
 
@@ -21,6 +23,7 @@ from .backbone import StaticBackbone
 from .codec import StaticMimi
 from .config import FRAME, Maya3Geom
 from .depth import FastDepth
+from .guards import VERDICTS, DeviceGuards, GuardConfig, merge_windows, split_code
 from .sampler import Cb0Sampler
 
 BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256)        # maya3/engine.py:44
@@ -51,6 +54,7 @@ class TickConfig:
     stops: bool = True                # False: forced lengths, stop codes are ignored
     min_frames: int = 4
     use_graphs: bool = True
+    guards: Optional[GuardConfig] = None   # loop guard + frame cap on the device (maya3/engine.py:69); None = off
 
 
 @dataclasses.dataclass
@@ -64,6 +68,10 @@ class Seat:
     new: bool = True
     stop: Optional[str] = None
     inline: Optional[np.ndarray] = None   # the part of the prompt prefilled inline in the admission tick
+    cap: int = 0                          # frame cap of the piece (_Seat.cap; the frame budget unless the caller's
+    loose_cap: int = 0                    # duration prior lowers it) and the prior-free cap (_Seat.loose_cap)
+    suspend: tuple = ()                   # inclusive frame windows with no loop action (_Seat.suspend)
+    n_boost: int = 0                      # EOS boosts the loop guard applied (_Seat.n_boost)
 
 
 @dataclasses.dataclass
@@ -182,6 +190,10 @@ class TickEngine:
         h = L.vp()
         L.check(L.load().m3_tick_create(tc, h), "m3_tick_create")
         self._handle = h
+        self.guards = None
+        if cfg.guards is not None:
+            self.guards = DeviceGuards(cfg.guards, n, self.cb0.aeos_bias)
+            L.check(L.load().m3_tick_set_guard(h, self.guards.c_cfg, self.guards.c_state), "m3_tick_set_guard")
         self.free = list(range(n))[::-1]
         self.active: list[Seat] = []
         self.pending: list[Seat] = []
@@ -208,15 +220,22 @@ class TickEngine:
         return int(s.value)
 
     # ---------------------------------------------------------------- requests
-    def submit(self, prompt_ids, max_frames, rid=None, seed=None) -> Seat:
+    def submit(self, prompt_ids, max_frames, rid=None, seed=None, cap=None, loose_cap=None, suspend=()) -> Seat:
         """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False), clipped
-        to the KV capacity as the reference does (a budget below 8 frames rejects the request)."""
+        to the KV capacity as the reference does (a budget below 8 frames rejects the request).  With guards on,
+        `cap` is the piece's frame cap from the caller's duration prior and `loose_cap` its prior-free cap
+        (maya3/engine.py:405-411, Engine._plan; both default to the budget), `suspend` its loop-guard suspend windows."""
         prompt = np.asarray(prompt_ids, np.int64)
         if prompt.ndim != 1 or len(prompt) == 0:
             raise ValueError("prompt must be a non-empty 1-D array of token ids")
         frames = frame_budget(len(prompt), int(max_frames), self.cfg.capacity)
         seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
         s = Seat(rid if rid is not None else next(self._ids), prompt, frames, seed)
+        s.loose_cap = frames if loose_cap is None else min(int(loose_cap), frames)
+        s.cap = min(s.loose_cap if cap is None else int(cap), frames)
+        s.suspend = tuple(suspend)
+        if self.guards is not None and len(merge_windows(s.suspend)) > self.guards.cfg.max_windows:
+            raise ValueError(f"more than {self.guards.cfg.max_windows} disjoint suspend windows")
         self.pending.append(s)
         return s
 
@@ -247,6 +266,8 @@ class TickEngine:
         self.depth.cross_const[slot] = self.voice_const
         self.codec._reset_row(slot)
         self.backbone.lengths[slot] = 0
+        if self.guards is not None:
+            self.guards.bind(slot, s.cap, s.suspend)
 
     def _release(self, s: Seat):
         """maya3/engine.py:632-635."""
@@ -411,6 +432,12 @@ class TickEngine:
         """Host bookkeeping of a tick whose readout is not read (stops disabled): every seat got one frame."""
         return self._deliver(seats, None)
 
+    def _cap_reason(self, s: Seat) -> str:
+        """maya3/engine.py:587-592: the caller's frame budget, the duration prior's cap, or the plain cap."""
+        if s.frames >= s.max_frames:
+            return "max_frames"
+        return "cap_guard" if self.guards.cfg.enabled and s.cap < s.loose_cap else "cap"
+
     def _deliver(self, seats, hv):
         """Host bookkeeping after a tick: stop codes, frame counts, finished seats; with a readout, the per-seat
         (seat, stop code, cb0, int16 PCM view) tuples.  The readout columns are converted once for all seats."""
@@ -426,13 +453,16 @@ class TickEngine:
                     finished.append(s)
             frames = n
         else:
-            codes = hv[:n, 0].tolist()
+            stop_c, verdict_c, boosts = (x.tolist() for x in split_code(hv[:n, 0]))
             cb0s = hv[:n, 1].tolist()
             pcm = hv[:n, 2:].view(np.int16)
+            guarded = self.guards is not None
             frames = 0
             for i, s in enumerate(seats):
                 s.new = False
-                code = codes[i]
+                code = stop_c[i]
+                if guarded:
+                    s.n_boost = boosts[i]
                 if stops and code:
                     s.stop = REASONS.get(code, str(code))
                     finished.append(s)
@@ -441,7 +471,11 @@ class TickEngine:
                 s.frames += 1
                 frames += 1
                 out.append((s, code, cb0s[i], pcm[i]))
-                if s.frames >= s.max_frames:
+                v = verdict_c[i] if guarded and stops else 0
+                if v:       # the frame is delivered, then the seat finishes (maya3/engine.py:586-614)
+                    s.stop = self._cap_reason(s) if v == 1 else VERDICTS.get(v, str(v))
+                    finished.append(s)
+                elif s.frames >= s.max_frames:
                     s.stop = "max_frames"
                     finished.append(s)
         self.stats["frames"] += frames

@@ -10,6 +10,7 @@ tick:      the full engine tick at the benchmark geometry with fewer seats.
 mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
 gaps:      per-node cost of a CUDA graph of dependent tiny kernels.
 overlap:   backbone step and Mimi decode timed back to back and concurrently on two streams.
+guard:     the loop guard (m3_guard_step) over `seats` seats on due frames, alone and as a graph node.
 """
 from __future__ import annotations
 
@@ -250,16 +251,64 @@ def gemm(a):
               f"{2 * M * N * K / own / 1e6:8.1f}", flush=True)
 
 
+@torch.inference_mode()
+def guard(a):
+    """m3_guard_step over `seats` seats whose histories are full and whose every update is due (frame 100, the loop
+    rule evaluated for all: the worst case), timed with CUDA events as eager launches and replayed from a graph."""
+    from .guards import DeviceGuards, GuardConfig
+    dev = torch.device("cuda", 0)
+    S = a.seats
+    bias = torch.zeros(S + 1, device=dev)
+    g = DeviceGuards(GuardConfig(every=1), S, bias)
+    for s in range(S):
+        g.bind(s, 10 ** 6)
+    g.frames[:S] = 99
+    g.hist[:S] = torch.randint(0, 2048, (S, g.cfg.hist), device=dev, dtype=torch.int32)
+    slots = torch.arange(S, device=dev)
+    cb0 = torch.randint(0, 2048, (S,), device=dev)
+    code = torch.zeros(S, dtype=torch.long, device=dev)
+    reps = 200
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        g.step(slots, code.zero_(), cb0)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.step(slots, code, cb0)
+    e1.record()
+    torch.cuda.synchronize()
+    eager = e0.elapsed_time(e1) / reps * 1e3
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        g.step(slots, code, cb0, side)
+    torch.cuda.current_stream().wait_stream(side)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(20):
+            g.step(slots, code, cb0, torch.cuda.current_stream())
+    gr.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(10):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    graphed = e0.elapsed_time(e1) / 200 * 1e3
+    print(f"guard over {S} seats (every update due): {eager:.2f} us per eager launch, {graphed:.2f} us per graph node")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi", "gaps", "overlap"))
+    ap.add_argument("case", choices=("attention", "tick", "gemm", "mimi", "gaps", "overlap", "guard"))
     ap.add_argument("--seats", type=int, default=64)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     ap.add_argument("--cold", action="store_true", help="gemm: stream the weights from HBM on every launch")
     a = ap.parse_args()
-    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap}[a.case](a)
+    {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap,
+     "guard": guard}[a.case](a)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,103 @@
+"""CPU: the loop-guard oracle against the reference's own loop detector (golden vectors from maya3/guards.py's
+loop_detect_batch), the per-seat guard update on hand-built cb0 streams whose verdicts follow from the rules of
+maya3/engine.py:571-617, and the host helpers of maya2_native_b200.guards (no GPU calls)."""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from maya2_native_b200.guards import GuardConfig, merge_windows, split_code
+from oracle.guards import BACKSTOP, CAP, NONE, PERIOD, STALL, GuardOracle, loop_detect
+
+
+def _decode(hit):
+    return 0 if hit is None else (-1 if hit == "stall" else int(hit.split(":")[1]))
+
+
+@pytest.mark.parametrize("name", ["default", "alt"])
+def test_loop_detect_matches_reference_vectors(name):
+    z = golden("guards_loop.npz")
+    stall, pw, pmin, pmax, _ = (int(v) for v in z[f"{name}_cfg"])
+    thr = float(z[f"{name}_thr"])
+    W, n, want = z[f"{name}_W"].astype(np.int64), z[f"{name}_n"], z[f"{name}_hit"]
+    got = np.array([_decode(loop_detect(W[i], int(n[i]), stall, pw, thr, pmin, pmax)) for i in range(len(n))])
+    assert (got == want).all(), np.flatnonzero(got != want)[:10]
+    assert (want == -1).any() and (want > 0).any() and (want == 0).any()
+
+
+def run(ora, slot, stream, stops=None):
+    """Feed one seat's cb0 stream through the oracle; returns the packed code per frame."""
+    out = []
+    for t, c in enumerate(stream):
+        stop = 0 if stops is None else stops[t]
+        out.append(int(ora.step([slot], [stop], [c])[0]))
+    return out
+
+
+def cfg(**kw):
+    return dataclasses.replace(GuardConfig(), **kw)
+
+
+def test_stall_boost_then_backstop():
+    ora = GuardOracle(cfg(), 2)
+    ora.bind(0, cap=1000)
+    codes = run(ora, 0, [5] * 60)
+    v = [(c >> 8) & 0xFF for c in codes]
+    # first due frame with a 32-frame stall is frame 32 (start=32, every=2): boost from there, backstop 24 frames on
+    assert ora.boost_at[0] == 32 and ora.n_boost[0] == 1 and ora.aeos_bias[0] == 4.0
+    assert v[:55] == [NONE] * 55 and v[55] == BACKSTOP            # frame 56 = 32 + 24
+    assert codes[31] >> 16 == 1 and codes[30] >> 16 == 0
+
+
+def test_loop_that_clears_removes_the_boost():
+    ora = GuardOracle(cfg(), 1)
+    ora.bind(0, cap=1000)
+    rng = np.random.default_rng(0)
+    stream = [9] * 40 + list(rng.integers(100, 2000, 40))
+    codes = run(ora, 0, stream)
+    assert ora.n_boost[0] == 1 and ora.boost_at[0] == -1 and ora.aeos_bias[0] == 0.0
+    assert all((c >> 8) & 0xFF == NONE for c in codes)
+
+
+def test_period_rule_and_stop_mode():
+    ora = GuardOracle(cfg(mode="stop"), 1)
+    ora.bind(0, cap=1000)
+    stream = [1, 2, 3] * 30
+    v = [(c >> 8) & 0xFF for c in run(ora, 0, stream)]
+    assert v.index(PERIOD) == 63 and v[:63] == [NONE] * 63     # first due frame with a full 64-code window
+    ora.bind(0, cap=1000)
+    v = [(c >> 8) & 0xFF for c in run(ora, 0, [4] * 40)]
+    assert v.index(STALL) == 31
+
+
+def test_cap_precedes_the_loop_rule_and_windows_suspend_it():
+    ora = GuardOracle(cfg(), 1)
+    ora.bind(0, cap=32)
+    v = [(c >> 8) & 0xFF for c in run(ora, 0, [5] * 32)]
+    assert v[31] == CAP and ora.n_boost[0] == 0                 # frame 32 hits the cap: no loop check
+    ora.bind(0, cap=1000, windows=[(20, 45), (46, 50)])
+    run(ora, 0, [5] * 52)
+    assert ora.boost_at[0] == 52                                # first due frame outside [20, 50]
+
+
+def test_sampler_stop_passes_through_with_the_boost_count():
+    ora = GuardOracle(cfg(), 1)
+    ora.bind(0, cap=1000)
+    run(ora, 0, [5] * 34)
+    out = ora.step([0], [3], [5])
+    assert out[0] == 3 | 1 << 16 and ora.frames[0] == 34        # no frame counted for a stopped seat
+    out = ora.step([1], [0], [5])                              # the padding slot is left as is
+    assert out[0] == 0
+
+
+def test_host_helpers():
+    assert merge_windows([(10, 20), (5, 9), (30, 29), (21, 25), (40, 50), (45, 60)]) == [(5, 25), (40, 60)]
+    s, v, nb = split_code(np.array([3, 1 << 8 | 2 << 16, 0]))
+    assert s.tolist() == [3, 0, 0] and v.tolist() == [0, 1, 0] and nb.tolist() == [0, 2, 0]
+    with pytest.raises(ValueError):
+        GuardConfig(mode="warn")
+    with pytest.raises(ValueError):
+        GuardConfig(pmax=64)
+    with pytest.raises(ValueError):
+        GuardConfig(hist=200)
