@@ -123,6 +123,13 @@ M3_API int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t
                      const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream);
 /* Read (and optionally clear) the device status word; synchronises with the device. */
 M3_API int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clear);
+/* Voice prefix KV (maya3/engine.py:276-280, serve/fast_backbone.py:316-322): copy the first `length` positions of
+ * every layer's K and V of `slot` to (save) or from (load) a packed store, bf16 [layers, 2 (K, V), kv_heads, length,
+ * head_dim], 16-byte aligned.  Load also sets lengths[slot] = length (the host mirror is the caller's).  One launch
+ * each, stream-ordered and capturable.  slot outside [0, max_slots) or length outside (0, capacity]: M3_ERR_RANGE. */
+M3_API int m3_backbone_save_prefix(m3_backbone* bb, int32_t slot, void* store, int32_t length, m3_stream stream);
+M3_API int m3_backbone_load_prefix(m3_backbone* bb, int32_t slot, const void* store, int32_t length,
+                                   m3_stream stream);
 /* Measurement hook: re-run layer `layer`'s decode attention (split-KV pass + combine) on the queries, slots and
  * positions the last m3_backbone_step left in the handle's scratch (rows and ctx as that step), to time the kernel
  * on the live cache (rows beyond any step's are rejected with M3_ERR_RANGE).  Overwrites only the handle's attention

@@ -127,6 +127,8 @@ SIGNATURES = {
     "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     "m3_tick_outputs": (C.c_int, [vp, P(vp), P(vp), P(vp)]),
     "m3_tick_status": (C.c_int, [vp, P(i32), i32]),
+    "m3_backbone_save_prefix": (C.c_int, [vp, i32, vp, i32, vp]),
+    "m3_backbone_load_prefix": (C.c_int, [vp, i32, vp, i32, vp]),
     "m3_guard_step": (C.c_int, [P(GuardConfig), P(GuardState), vp, vp, vp, i32, vp]),
     "m3_tick_set_guard": (C.c_int, [vp, P(GuardConfig), P(GuardState)]),
 }

@@ -164,6 +164,59 @@ class StaticBackbone:
         self.lengths[slot] = length
         self.lengths_cpu[slot] = length
 
+    # ---------------------------------------------------------------- voice prefixes (packed store, one launch)
+    def prefix_store(self, length) -> torch.Tensor:
+        """An empty packed prefix store bf16 [layers, 2 (K, V), kv_heads, length, head_dim] (m3_backbone_*_prefix)."""
+        g = self.geom
+        return torch.empty(g.layers, 2, g.kv_heads, int(length), g.head_dim, dtype=torch.bfloat16, device=self.device)
+
+    def _check_store(self, store, length):
+        g = self.geom
+        if tuple(store.shape) != (g.layers, 2, g.kv_heads, int(length), g.head_dim) or store.dtype != torch.bfloat16 \
+                or store.device != self.device or not store.is_contiguous():
+            raise ValueError("prefix store must be contiguous bf16 [layers, 2, kv_heads, length, head_dim] on the "
+                             "backbone's device")
+
+    @torch.inference_mode()
+    def save_prefix(self, slot, length, store=None) -> torch.Tensor:
+        """The slot's first `length` positions of every layer's K/V as a packed store (one launch)."""
+        if not 0 <= slot < self.max_slots:
+            raise IndexError(slot)
+        if not 0 < length <= self.lengths_cpu[slot]:
+            raise ValueError(f"slot {slot} holds {self.lengths_cpu[slot]} positions, asked for {length}")
+        store = self.prefix_store(length) if store is None else store
+        self._check_store(store, length)
+        L.check(L.load().m3_backbone_save_prefix(self._handle, slot, store.data_ptr(), int(length), L.stream_ptr()),
+                "m3_backbone_save_prefix")
+        return store
+
+    @torch.inference_mode()
+    def load_prefix_store(self, slot, store, length):
+        """load_prefix from a packed store (serve/fast_backbone.py:316-322 in one launch): K/V rows [0, length) of the
+        slot and its length (device and host mirror)."""
+        if not 0 <= slot < self.max_slots:
+            raise IndexError(slot)
+        if not 0 < length <= self.capacity:
+            raise ValueError(f"length {length} outside (0, {self.capacity}]")
+        self._check_store(store, length)
+        L.check(L.load().m3_backbone_load_prefix(self._handle, slot, store.data_ptr(), int(length), L.stream_ptr()),
+                "m3_backbone_load_prefix")
+        self.lengths_cpu[slot] = int(length)
+
+    @torch.inference_mode()
+    def build_prefix(self, slot, x, chunk=None) -> torch.Tensor:
+        """A voice's prefix KV computed by this backbone (maya3/engine.py:276-280 runs an eager HF prefill for it): the
+        prefix embeddings x [T, hidden] are prefilled into the free `slot` by inline-prefill steps of at most `chunk`
+        rows, saved as a packed store, and the slot is freed again."""
+        T = int(x.shape[0])
+        chunk = int(chunk or self.max_rows)
+        self.free(slot)
+        for c0 in range(0, T, chunk):
+            self.step_mixed([], None, [(slot, x[c0:c0 + chunk])])
+        store = self.save_prefix(slot, T)
+        self.free(slot)
+        return store
+
     @torch.inference_mode()
     def free(self, slot):
         self.lengths[slot] = 0

@@ -501,6 +501,7 @@ struct m3_backbone {
   m3_backbone_config c{};
   std::vector<const bf16*> in_norm, wqkv, q_norm, k_norm, wo, post_norm, wgu, wdown;
   std::vector<bf16*> kc, vc;
+  bf16** caches = nullptr;  // device [layers * 2]: layer i's K cache at 2i, V cache at 2i + 1 (prefix copies)
   const bf16* final_norm = nullptr;
   const bf16* cos = nullptr;
   const bf16* sin = nullptr;
@@ -528,6 +529,30 @@ T* carve(char*& p, size_t count) {
   T* r = reinterpret_cast<T*>(p);
   p += (count * sizeof(T) + 255) / 256 * 256;
   return r;
+}
+
+// A slot's first `length` positions of every layer's K and V to (save) or from (load) a packed prefix store
+// [layers, 2 (K, V), kv_heads, length, head_dim] bf16: the reference's per-voice prefix KV (maya3/engine.py:276-280,
+// a list of per-layer (k, v) [1, kv_heads, length, head_dim]) as one buffer, installed by one launch instead of a copy
+// per layer and tensor (serve/fast_backbone.py:316-322).  A CTA moves 16 rows (one token of one KV head each) with 16
+// threads per row and 16-byte vectors; grid.y walks (layer, K/V).  Load also sets lengths[slot] = length.
+__global__ void prefix_copy_kernel(bf16* const* __restrict__ caches, bf16* __restrict__ store, int64_t slot,
+                                   int length, int kv_heads, int capacity, int head_dim, int save,
+                                   int64_t* __restrict__ lengths) {
+  const int lk = blockIdx.y;
+  const int64_t rows = (int64_t)kv_heads * length;
+  const int64_t r = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
+  if (!save && blockIdx.x == 0 && lk == 0 && threadIdx.x == 0) lengths[slot] = length;
+  if (r >= rows) return;
+  const int64_t h = r / length, t = r % length;
+  uint4* c = reinterpret_cast<uint4*>(caches[lk] + ((slot * kv_heads + h) * capacity + t) * head_dim);
+  uint4* st = reinterpret_cast<uint4*>(store + ((int64_t)lk * rows + r) * head_dim);
+  for (int i = threadIdx.x & 15; i < head_dim / 8; i += 16) {
+    if (save)
+      st[i] = c[i];
+    else
+      c[i] = st[i];
+  }
 }
 
 // Keys per split: the longest chunk (fewest partial results to merge) that still gives enough CTAs to fill the GPU a
@@ -611,7 +636,7 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   add((size_t)R * Hd * 2); add((size_t)R * Hd * 2); add((size_t)R * qkvw * 2);
   add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * c.heads * c.head_dim * 2); add((size_t)R * Hd * 2);
   add((size_t)R * 2 * c.ffn * 2); add((size_t)R * c.ffn * 2);
-  add(parts * kHeadDim * 4); add(parts * 8); add((size_t)R * c.kv_heads * 4);
+  add(parts * kHeadDim * 4); add(parts * 8); add((size_t)R * c.kv_heads * 4); add((size_t)c.layers * 2 * 8);
   cudaError_t e = cudaMalloc(&bb->ws, bytes);
   if (e != cudaSuccess) {
     delete bb;
@@ -634,8 +659,15 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
   bb->part_o = carve<float>(p, parts * kHeadDim);
   bb->part_ml = carve<float2>(p, parts);
   bb->tickets = carve<int>(p, (size_t)R * c.kv_heads);
+  bb->caches = carve<bf16*>(p, (size_t)c.layers * 2);
+  std::vector<bf16*> cp;
+  for (int i = 0; i < c.layers; ++i) {
+    cp.push_back(bb->kc[i]);
+    cp.push_back(bb->vc[i]);
+  }
   if (cudaMemset(bb->status, 0, 256) != cudaSuccess ||
-      cudaMemset(bb->tickets, 0, (size_t)R * c.kv_heads * 4) != cudaSuccess) {
+      cudaMemset(bb->tickets, 0, (size_t)R * c.kv_heads * 4) != cudaSuccess ||
+      cudaMemcpy(bb->caches, cp.data(), cp.size() * sizeof(bf16*), cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaFree(bb->ws);
     delete bb;
     set_error("m3_backbone_create: memset failed");
@@ -738,4 +770,30 @@ extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t row
   M3_REQUIRE(rows <= bb->rows_written, M3_ERR_RANGE,
              "m3_backbone_attention: rows %d beyond the %d rows a backbone step has set up", rows, bb->rows_written);
   return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
+}
+
+static int prefix_copy(m3_backbone* bb, int32_t slot, void* store, int32_t length, int save, m3_stream stream) {
+  M3_REQUIRE(bb && store, M3_ERR_ARG, "prefix copy: null argument");
+  const m3_backbone_config& c = bb->c;
+  M3_REQUIRE(slot >= 0 && slot < c.max_slots, M3_ERR_RANGE, "prefix copy: slot %d outside [0, %d)", slot,
+             c.max_slots);
+  M3_REQUIRE(length > 0 && length <= c.capacity, M3_ERR_RANGE, "prefix copy: length %d outside (0, %d]", length,
+             c.capacity);
+  M3_REQUIRE((reinterpret_cast<uintptr_t>(store) & 15) == 0 && c.head_dim % 8 == 0, M3_ERR_ARG,
+             "prefix copy: the store must be 16-byte aligned");
+  const dim3 grid(cdiv(c.kv_heads * length, 16), c.layers * 2);
+  prefix_copy_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      bb->caches, reinterpret_cast<bf16*>(store), slot, length, c.kv_heads, c.capacity, c.head_dim, save,
+      bb->lengths);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+extern "C" int m3_backbone_save_prefix(m3_backbone* bb, int32_t slot, void* store, int32_t length, m3_stream stream) {
+  return prefix_copy(bb, slot, store, length, 1, stream);
+}
+
+extern "C" int m3_backbone_load_prefix(m3_backbone* bb, int32_t slot, const void* store, int32_t length,
+                                       m3_stream stream) {
+  return prefix_copy(bb, slot, const_cast<void*>(store), length, 0, stream);
 }

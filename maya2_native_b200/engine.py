@@ -58,6 +58,15 @@ class TickConfig:
 
 
 @dataclasses.dataclass
+class Voice:
+    """A voice's backbone prefix (maya3/engine.py:259-283 prepare_voice): its token ids and the packed K/V store of
+    those positions, computed once and installed into each of its requests' slots with one launch."""
+    ids: np.ndarray
+    store: torch.Tensor
+    length: int
+
+
+@dataclasses.dataclass
 class Seat:
     rid: object
     prompt: np.ndarray
@@ -72,6 +81,7 @@ class Seat:
     loose_cap: int = 0                    # duration prior lowers it) and the prior-free cap (_Seat.loose_cap)
     suspend: tuple = ()                   # inclusive frame windows with no loop action (_Seat.suspend)
     n_boost: int = 0                      # EOS boosts the loop guard applied (_Seat.n_boost)
+    voice: Optional[Voice] = None         # prefix KV installed at bind; the prompt follows it
 
 
 @dataclasses.dataclass
@@ -220,20 +230,38 @@ class TickEngine:
         return int(s.value)
 
     # ---------------------------------------------------------------- requests
-    def submit(self, prompt_ids, max_frames, rid=None, seed=None, cap=None, loose_cap=None, suspend=()) -> Seat:
+    @torch.inference_mode()
+    def prepare_voice(self, prefix_ids) -> Voice:
+        """maya3/engine.py:259-283: compute a voice prefix's backbone K/V once (here with this engine's own prefill,
+        in a free slot, between ticks) for requests that then skip those positions (maya3/engine.py:488-491)."""
+        ids = np.asarray(prefix_ids, np.int64)
+        if ids.ndim != 1 or len(ids) == 0 or len(ids) >= self.cfg.capacity:
+            raise ValueError("a voice prefix is a non-empty 1-D array of token ids shorter than the KV capacity")
+        if not self.free:
+            raise RuntimeError("prepare_voice needs a free slot")
+        slot = self.free[-1]
+        x = self.embed[torch.from_numpy(ids).to(self.device)]
+        store = self.backbone.build_prefix(slot, x, chunk=self.cfg.max_inline_rows)
+        return Voice(ids, store, len(ids))
+
+    def submit(self, prompt_ids, max_frames, rid=None, seed=None, cap=None, loose_cap=None, suspend=(),
+               voice: Optional[Voice] = None) -> Seat:
         """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False), clipped
         to the KV capacity as the reference does (a budget below 8 frames rejects the request).  With guards on,
         `cap` is the piece's frame cap from the caller's duration prior and `loose_cap` its prior-free cap
-        (maya3/engine.py:405-411, Engine._plan; both default to the budget), `suspend` its loop-guard suspend windows."""
+        (maya3/engine.py:405-411, Engine._plan; both default to the budget), `suspend` its loop-guard suspend windows.
+        With a `voice` (prepare_voice), the prompt is what follows the voice prefix."""
         prompt = np.asarray(prompt_ids, np.int64)
         if prompt.ndim != 1 or len(prompt) == 0:
             raise ValueError("prompt must be a non-empty 1-D array of token ids")
-        frames = frame_budget(len(prompt), int(max_frames), self.cfg.capacity)
+        pre = voice.length if voice is not None else 0
+        frames = frame_budget(pre + len(prompt), int(max_frames), self.cfg.capacity)
         seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
         s = Seat(rid if rid is not None else next(self._ids), prompt, frames, seed)
         s.loose_cap = frames if loose_cap is None else min(int(loose_cap), frames)
         s.cap = min(s.loose_cap if cap is None else int(cap), frames)
         s.suspend = tuple(suspend)
+        s.voice = voice
         if self.guards is not None and len(merge_windows(s.suspend)) > self.guards.cfg.max_windows:
             raise ValueError(f"more than {self.guards.cfg.max_windows} disjoint suspend windows")
         self.pending.append(s)
@@ -246,7 +274,7 @@ class TickEngine:
 
     def _claim(self, s: Seat):
         s.slot = self.free.pop()
-        self.backbone.lengths_cpu[s.slot] = 0
+        self.backbone.lengths_cpu[s.slot] = s.voice.length if s.voice is not None else 0
 
     @torch.inference_mode()
     def reset_slot(self, s: Seat):
@@ -266,6 +294,8 @@ class TickEngine:
         self.depth.cross_const[slot] = self.voice_const
         self.codec._reset_row(slot)
         self.backbone.lengths[slot] = 0
+        if s.voice is not None:       # maya3/engine.py:488-491: the prefix KV, then the prompt after it
+            self.backbone.load_prefix_store(slot, s.voice.store, s.voice.length)
         if self.guards is not None:
             self.guards.bind(slot, s.cap, s.suspend)
 
@@ -490,5 +520,5 @@ class TickEngine:
         return out
 
 
-__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "FRAME", "FROM_FEEDBACK", "admission_cap", "frame_budget",
+__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "Voice", "FRAME", "FROM_FEEDBACK", "admission_cap", "frame_budget",
            "plan_layout"]

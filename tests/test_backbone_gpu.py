@@ -197,3 +197,41 @@ def test_row_order_does_not_change_rows(cuda):
     assert lib.m3_backbone_attention(sbs[1]._handle, 0, n, cap, L.stream_ptr()) == L.M3_OK
     torch.cuda.synchronize()
     assert all(sb.device_status() == 0 for sb in sbs)
+
+
+def test_voice_prefix_store(cuda):
+    """Voice prefix KV (maya3/engine.py:259-283, serve/fast_backbone.py:316-322): a prefix built by this backbone's
+    own chunked prefill matches the oracle's one-shot prefill K/V; installing the packed store into another slot (one
+    launch) gives it bit-identical K/V rows and its length; the reference-form load_prefix (per-layer (k, v) list)
+    installs the same rows; a decode step then gives both slots the same hidden state, which matches the oracle
+    stepping its own prefix."""
+    g = dataclasses.replace(BASELINE.backbone, layers=2)
+    W = WG.generate({k: v for k, v in WG.backbone_shapes(g).items() if "embed_tokens" not in k})
+    cap, T = 512, 45
+    sb = StaticBackbone(W, 4, capacity=cap, ctx_buckets=(512,), batch_buckets=(8, 64), geom=g)
+    orc = BackboneOracle({k: v.numpy() for k, v in W.items()}, g, 4, cap, "bf16")
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((T, g.hidden)).astype(np.float32)
+    store = sb.build_prefix(0, t(x, cuda), chunk=20)             # chunks of 20, 20, 5 rows
+    orc.step_mixed([], None, [(0, x)])
+    assert sb.lengths_cpu[0] == 0 and tuple(store.shape) == (2, 2, g.kv_heads, T, g.head_dim)
+    for lay, tol in ((0, 5e-3), (1, 2e-2)):
+        assert rel_l2(store[lay, 0].float().cpu().numpy(), orc.k[lay][0, :, :T]) < tol
+        assert rel_l2(store[lay, 1].float().cpu().numpy(), orc.v[lay][0, :, :T]) < tol
+    sb.load_prefix_store(1, store, T)
+    sb.load_prefix(2, [(store[i, 0][None], store[i, 1][None]) for i in range(g.layers)], T)
+    for i in range(g.layers):
+        for c, kv in ((0, sb.k), (1, sb.v)):
+            assert torch.equal(kv[i][1, :, :T], store[i, c]) and torch.equal(kv[i][2, :, :T], store[i, c])
+    assert sb.lengths.cpu().tolist()[1:3] == [T, T] and sb.lengths_cpu[1:3] == [T, T]
+    x2 = rng.standard_normal((1, g.hidden)).astype(np.float32)
+    y = sb.step([1, 2], t(np.repeat(x2, 2, 0), cuda)).float().cpu().numpy()
+    assert rel_maxabs(y[0], y[1]) < 1e-3
+    assert rel_maxabs(y[0], orc.step([0], x2)[0]) < TOL
+    lib = L.load()
+    assert lib.m3_backbone_load_prefix(sb._handle, 4, store.data_ptr(), T, L.stream_ptr()) == L.M3_ERR_RANGE
+    assert lib.m3_backbone_load_prefix(sb._handle, 0, store.data_ptr(), cap + 1, L.stream_ptr()) == L.M3_ERR_RANGE
+    with pytest.raises(ValueError):
+        sb.save_prefix(3, 5)                                       # slot 3 holds no positions
+    torch.cuda.synchronize()
+    assert sb.device_status() == 0

@@ -148,3 +148,32 @@ def test_stop_code_releases_the_seat(cuda):
     assert c in eng.active and c.slot == slot_a and c.frames >= 1
     assert eng.device_status() == 0
     eng.close()
+
+
+def test_voice_prefix_request(cuda):
+    """prepare_voice + submit(voice=...) (maya3/engine.py:259-283, :488-491): the request's slot starts from the
+    voice's K/V (bit-identical to its store) and the prompt follows it; the first frame's hidden state matches a
+    request that prefills prefix + prompt inline in the same tick."""
+    W = WG.generate(WG.all_shapes(TINY))
+    cfg = TickConfig(max_seats=2, capacity=128, max_inline_rows=64, stops=False)
+    eng = TickEngine(TINY, W, cfg, device=cuda)
+    rng = np.random.default_rng(9)
+    pre, prompt = rng.integers(0, TINY.backbone.vocab, 20), rng.integers(0, TINY.backbone.vocab, 7)
+    v = eng.prepare_voice(pre)
+    a = eng.submit(prompt, 10, seed=5, voice=v)
+    b = eng.submit(np.concatenate([pre, prompt]), 10, seed=5)
+    eng.tick()
+    assert eng.backbone.lengths_cpu[a.slot] == eng.backbone.lengths_cpu[b.slot] == 27
+    assert eng.backbone.lengths.cpu().tolist()[a.slot] == 27
+    for i in range(TINY.backbone.layers):
+        assert torch.equal(eng.backbone.k[i][a.slot, :, :20], v.store[i, 0])
+        assert torch.equal(eng.backbone.v[i][a.slot, :, :20], v.store[i, 1])
+    h, _, _ = eng.last_outputs(2)
+    h = h.float().cpu().numpy()
+    assert np.abs(h[0] - h[1]).max() / max(1.0, np.abs(h[1]).max()) < 2e-2
+    long_prompt = rng.integers(0, TINY.backbone.vocab, 100)
+    eng.submit(long_prompt, 10)                            # fits alone: 100 + 10 + 2 <= 128
+    with pytest.raises(ValueError):
+        eng.submit(long_prompt, 10, voice=v)               # the prefix counts: a budget under 8 frames is refused
+    assert eng.device_status() == 0
+    eng.close()
