@@ -101,3 +101,38 @@ def test_host_helpers():
         GuardConfig(pmax=64)
     with pytest.raises(ValueError):
         GuardConfig(hist=200)
+
+
+def test_engine_delivery_decodes_guard_verdicts():
+    """TickEngine._deliver on a hand-made readout (host logic only, no GPU): a sampler stop ends the seat without a
+    frame; a guard verdict delivers the frame, then ends the seat with the reference's reason (maya3/engine.py:576-614);
+    the boost count rides along."""
+    import types
+    from maya2_native_b200.engine import Seat, TickConfig, TickEngine
+    eng = TickEngine.__new__(TickEngine)
+    eng.cfg = TickConfig(max_seats=6, guards=GuardConfig())
+    eng.guards = types.SimpleNamespace(cfg=eng.cfg.guards)
+    eng.stats = {"frames": 0, "completed": 0, "ticks": 0}
+    eng.active = []
+    released = []
+    eng._release = released.append
+    seats = [Seat(rid=i, prompt=np.zeros(3, np.int64), max_frames=50, seed=1, slot=i) for i in range(6)]
+    for s in seats:
+        s.cap = s.loose_cap = 50
+    seats[0].cap, seats[0].frames = 10, 9          # prior cap below the loose cap -> cap_guard
+    seats[4].frames = 49                           # the request's own budget -> max_frames
+    seats[5].frames = 20
+    hv = np.zeros((6, 2 + 4), np.int64)
+    hv[0, 0] = 1 << 8
+    hv[1, 0] = 2 << 8 | 1 << 16
+    hv[2, 0] = 3 | 2 << 16
+    hv[3, 0] = 1 << 16
+    hv[4, 0] = 1 << 8
+    hv[5, 0] = 4 << 8 | 1 << 16
+    out = eng._deliver(seats, hv)
+    assert [s.stop for s in seats] == ["cap_guard", "loop_backstop", "aeos_tau", None, "max_frames", "loop_period"]
+    assert [s.frames for s in seats] == [10, 1, 0, 1, 50, 21]
+    assert [s.n_boost for s in seats] == [0, 1, 2, 1, 0, 1]
+    assert [o[3] is None for o in out] == [False, False, True, False, False, False]
+    assert released == [seats[i] for i in (0, 1, 2, 4, 5)] and eng.active == [seats[3]]
+    assert eng.stats["frames"] == 5 and eng.stats["completed"] == 5
