@@ -343,12 +343,9 @@ class TickEngine:
 
     # ---------------------------------------------------------------- plan
     def make_plan(self, dec: list, new: list) -> TickPlan:
-        """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows, then each new seat's inline rows.
-        Decode seats go longest KV first, the order in which the backbone step's attention visits rows (it sorts them
-        on the device otherwise), so the step finds them in order and skips its sort; the tick's outputs follow the
-        plan's order."""
-        lc = self.backbone.lengths_cpu
-        dec = sorted(dec, key=lambda s: -lc[s.slot])
+        """Host plan of one tick (layout of m3_tick_run, plan_layout): decode rows in seat order, then each new seat's
+        inline rows; the tick's outputs follow the plan's order.  The backbone step orders the attention's rows
+        longest first on the device, so the host does not sort them."""
         p, rb, sb, cb, keys = plan_layout([s.slot for s in dec], [(s.slot, s.inline) for s in new],
                                           self.backbone.lengths_cpu, self.row_buckets, self.buckets,
                                           self.ctx_buckets, self.cfg.max_seats)
@@ -483,31 +480,44 @@ class TickEngine:
                     finished.append(s)
             frames = n
         else:
-            stop_c, verdict_c, boosts = (x.tolist() for x in split_code(hv[:n, 0]))
+            stop_a, verdict_a, boost_a = split_code(hv[:n, 0])
+            stop_c = stop_a.tolist()
             cb0s = hv[:n, 1].tolist()
-            pcm = hv[:n, 2:].view(np.int16)
+            pcm = list(hv[:n, 2:].view(np.int16))
             guarded = self.guards is not None
-            frames = 0
-            for i, s in enumerate(seats):
-                s.new = False
-                code = stop_c[i]
-                if guarded:
-                    s.n_boost = boosts[i]
-                if stops and code:
-                    s.stop = REASONS.get(code, str(code))
-                    finished.append(s)
-                    out.append((s, code, cb0s[i], None))
-                    continue
-                s.frames += 1
-                frames += 1
-                out.append((s, code, cb0s[i], pcm[i]))
-                v = verdict_c[i] if guarded and stops else 0
-                if v:       # the frame is delivered, then the seat finishes (maya3/engine.py:586-614)
-                    s.stop = self._cap_reason(s) if v == 1 else VERDICTS.get(v, str(v))
-                    finished.append(s)
-                elif s.frames >= s.max_frames:
-                    s.stop = "max_frames"
-                    finished.append(s)
+            if guarded:
+                for s, b in zip(seats, boost_a.tolist()):
+                    s.n_boost = b
+            verdict_c = verdict_a.tolist() if guarded and stops else None
+            if not (stops and stop_a.any()) and verdict_c is None:   # no stop codes: every seat gets its frame
+                out = list(zip(seats, stop_c, cb0s, pcm))
+                for s in seats:
+                    s.new = False
+                    s.frames += 1
+                    if s.frames >= s.max_frames:
+                        s.stop = "max_frames"
+                        finished.append(s)
+                frames = n
+            else:
+                frames = 0
+                for i, s in enumerate(seats):
+                    s.new = False
+                    code = stop_c[i]
+                    if stops and code:
+                        s.stop = REASONS.get(code, str(code))
+                        finished.append(s)
+                        out.append((s, code, cb0s[i], None))
+                        continue
+                    s.frames += 1
+                    frames += 1
+                    out.append((s, code, cb0s[i], pcm[i]))
+                    v = verdict_c[i] if verdict_c is not None else 0
+                    if v:       # the frame is delivered, then the seat finishes (maya3/engine.py:586-614)
+                        s.stop = self._cap_reason(s) if v == 1 else VERDICTS.get(v, str(v))
+                        finished.append(s)
+                    elif s.frames >= s.max_frames:
+                        s.stop = "max_frames"
+                        finished.append(s)
         self.stats["frames"] += frames
         self.active = list(seats)
         if finished:

@@ -65,7 +65,7 @@ def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
                 ora.depth.set_speaker(s.slot, null_mem)
             _, last = ora.bb.step_mixed([], None, [(s.slot, embed[s.prompt]) for s in order])
             h_o = np.stack(last)
-        else:   # the engine orders a tick's seats by KV length, so take each seat's own feedback vector
+        else:   # each seat's own feedback vector from the previous tick
             h_o = ora.bb.step(list(slots), np.stack([fb_prev[int(sl)] for sl in slots]))
         res["h_err"].append(float(np.linalg.norm(h_o - h_gpu) / np.linalg.norm(h_o)))
         _, cb0_o, _ = ora.cb0(h_gpu, slots)
