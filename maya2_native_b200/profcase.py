@@ -46,7 +46,7 @@ def attention(a):
     for s, n in enumerate(L):
         sb.lengths_cpu[s] = int(n)
     x = torch.randn(a.seats, g.hidden, device=dev, dtype=torch.bfloat16)
-    order = [int(s) for s in np.argsort(-L, kind="stable")]   # longest first, as the engine plans a tick
+    order = [int(s) for s in np.argsort(-L, kind="stable")]   # longest first, the order the step visits rows in
     for _ in range(a.steps):
         sb.step(order, x)
     torch.cuda.synchronize()
