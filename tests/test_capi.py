@@ -105,3 +105,23 @@ def test_status_codes_of_the_binding():
         L.check(L.M3_ERR_RANGE, "x")
     with pytest.raises(L.M3Error):
         L.check(L.M3_ERR_CUDA, "x")
+
+
+def test_guard_and_prefix_entry_points_validate_before_the_device(lib):
+    """m3_guard_step / m3_tick_set_guard refuse configurations outside their limits (stall or period window longer
+    than the history, pmax >= period_win, a history above 128, a bad mode, null state arrays) and the prefix copies
+    refuse a null handle -- all before any device work."""
+    fake = L.GuardState(*([8] * 8))                      # non-null pointers that are never dereferenced
+    ok = dict(loop=1, stall=32, period_win=64, period_thr=0.7, pmin=2, pmax=16, start=32, every=2, mode=0, boost=4.0,
+              backstop=24, hist=96, max_windows=4, max_slots=8)
+    for bad in (dict(hist=200), dict(stall=100), dict(period_win=100), dict(pmax=64), dict(mode=2), dict(every=0),
+                dict(pmin=0), dict(max_slots=0)):
+        cfg = L.GuardConfig(**{**ok, **bad})
+        assert lib.m3_guard_step(cfg, fake, None, None, None, 0, None) == L.M3_ERR_ARG, bad
+    cfg = L.GuardConfig(**ok)
+    assert lib.m3_guard_step(cfg, L.GuardState(), None, None, None, 0, None) == L.M3_ERR_ARG   # null state
+    assert lib.m3_guard_step(cfg, fake, None, None, None, 4, None) == L.M3_ERR_ARG             # null slots
+    assert lib.m3_guard_step(cfg, fake, 8, 8, 8, 0, None) == L.M3_OK                           # nothing to do
+    assert lib.m3_tick_set_guard(None, cfg, fake) == L.M3_ERR_ARG
+    assert lib.m3_backbone_load_prefix(None, 0, 16, 4, None) == L.M3_ERR_ARG
+    assert lib.m3_backbone_save_prefix(None, 0, 16, 4, None) == L.M3_ERR_ARG
