@@ -11,9 +11,10 @@ Restates, per seat and in plain numpy:
                     hit sets the EOS boost (boost mode; a loop persisting `backstop` frames past the boost finishes
                     the seat) or finishes it at once (stop mode); a cleared loop removes the boost.
 
-Pinning: loop_detect against tests/golden/guards_loop.npz, which tests/golden/make_guards_golden.py produced by
-running the reference's own loop_detect_batch on the stream kinds of the reference's maya3/tests/test_guards.py.
-The per-seat state machine has no test in the reference; it is pinned by restatement of engine.py:571-617 only.
+Pinning (both fixtures made by tests/golden/make_guards_golden.py running the reference's own code): loop_detect
+against guards_loop.npz, the reference's loop_detect_batch on the stream kinds of its maya3/tests/test_guards.py;
+GuardOracle against guards_engine.npz, traces of the reference's Engine._tick (maya3/engine.py:514-630) driven on CPU
+with stand-in stages and scripted cb0 streams -- every seat's stop reason, frames, boosts and AEOS bias per tick.
 Outputs use the C ABI's packing (m3_guard_step): stop | verdict << 8 | n_boost << 16.
 """
 from __future__ import annotations

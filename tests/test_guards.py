@@ -136,3 +136,52 @@ def test_engine_delivery_decodes_guard_verdicts():
     assert [o[3] is None for o in out] == [False, False, True, False, False, False]
     assert released == [seats[i] for i in (0, 1, 2, 4, 5)] and eng.active == [seats[3]]
     assert eng.stats["frames"] == 5 and eng.stats["completed"] == 5
+
+
+REF_REASONS = ["", "cap", "cap_guard", "max_frames", "loop_backstop", "loop_stall", "loop_period", "aeos",
+               "aeos_argmax", "aeos_tau", "aeos_hazard"]
+STOPS = {1: "aeos", 2: "aeos_argmax", 3: "aeos_tau", 4: "aeos_hazard"}     # maya3/engine.py:46
+
+
+@pytest.mark.parametrize("name", ["boost", "stop"])
+def test_guard_oracle_matches_reference_engine_trace(name):
+    """The oracle's per-seat update against the reference's own Engine._tick (maya3/engine.py:571-617, with its
+    _release and _finish_piece), recorded by tests/golden/make_guards_golden.py on scripted cb0 streams: every seat's
+    stop reason, frame count, boost count, boost start and AEOS bias after every tick."""
+    z = golden("guards_engine.npz")
+    stall, pw, pmin, pmax, start, every, backstop, hist, stop_mode = (int(v) for v in z[f"{name}_cfg"])
+    thr, boost = (float(v) for v in z[f"{name}_thr"])
+    gc = cfg(stall=stall, period_win=pw, pmin=pmin, pmax=pmax, start=start, every=every, backstop=backstop, hist=hist,
+             mode="stop" if stop_mode else "boost", period_thr=thr, boost=boost)
+    g = {k: z[f"{name}_{k}"] for k in ("bind", "cap", "loose", "maxf", "nwin", "win", "act", "stop", "cb0", "reason",
+                                       "frames", "nboost", "boost_at", "bias")}
+    T, S = g["act"].shape
+    ora = GuardOracle(gc, S)
+    caps = {}
+    seen = set()
+    for t in range(T):
+        for s in np.flatnonzero(g["bind"][t]):
+            ora.bind(s, int(g["cap"][t, s]), [tuple(w) for w in g["win"][t, s, :g["nwin"][t, s]]])
+            caps[s] = (int(g["cap"][t, s]), int(g["loose"][t, s]), int(g["maxf"][t, s]))
+        slots = [int(s) for s in np.flatnonzero(g["act"][t])]
+        packed = ora.step(slots, [int(g["stop"][t, s]) for s in slots], [int(g["cb0"][t, s]) for s in slots])
+        for s, p in zip(slots, packed):
+            stop, verdict, nb = int(p) & 0xFF, (int(p) >> 8) & 0xFF, int(p) >> 16
+            f = int(ora.frames[s])
+            if stop:
+                reason = STOPS[stop]
+            elif verdict == CAP:
+                cap, loose, maxf = caps[s]
+                reason = "max_frames" if maxf and f >= maxf else ("cap_guard" if cap < loose else "cap")
+            else:
+                reason = {NONE: "", BACKSTOP: "loop_backstop", STALL: "loop_stall", PERIOD: "loop_period"}[verdict]
+            assert reason == REF_REASONS[g["reason"][t, s]], (t, s)
+            assert f == g["frames"][t, s] and nb == g["nboost"][t, s] == ora.n_boost[s], (t, s)
+            assert ora.boost_at[s] == g["boost_at"][t, s], (t, s)
+            if reason:
+                ora.aeos_bias[s] = 0.0                  # the reference's _release clears the finished slot's bias
+                seen.add(reason)
+            assert ora.aeos_bias[s] == g["bias"][t, s], (t, s)
+    want = {"cap", "cap_guard", "max_frames", "aeos", "aeos_argmax", "aeos_tau", "aeos_hazard"}
+    want |= {"loop_stall", "loop_period"} if stop_mode else {"loop_backstop"}
+    assert want <= seen, want - seen
