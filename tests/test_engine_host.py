@@ -61,3 +61,33 @@ def test_frame_budget_clips_to_capacity():
     assert frame_budget(100, 1000, 1024) == 1024 - 100 - 2
     with pytest.raises(ValueError, match="leaves no room"):
         frame_budget(1015, 100, 1024)             # 1024 - 1015 - 2 = 7 < 8
+
+
+def test_submit_caps_windows_and_voice_budget():
+    """TickEngine.submit (host only): the piece's cap and prior-free cap are clipped to the frame budget
+    (maya3/engine.py:405-411), suspend windows beyond the device's per-slot room are refused, and a voice prefix
+    counts against the KV capacity like the reference's prompt does (maya3/engine.py:465-472)."""
+    import itertools
+    import types
+
+    from maya2_native_b200.engine import TickEngine, Voice
+    from maya2_native_b200.guards import GuardConfig
+    eng = TickEngine.__new__(TickEngine)
+    eng.cfg = TickConfig(max_seats=4, capacity=128, guards=GuardConfig(max_windows=2))
+    eng.guards = types.SimpleNamespace(cfg=eng.cfg.guards)
+    eng.pending, eng._rng, eng._ids = [], np.random.default_rng(0), itertools.count()
+    s = eng.submit(np.arange(10), 50, cap=20, loose_cap=40, suspend=[(5, 9), (8, 12)])
+    assert (s.max_frames, s.cap, s.loose_cap, s.suspend) == (50, 20, 40, ((5, 9), (8, 12)))
+    s = eng.submit(np.arange(10), 50)
+    assert s.cap == s.loose_cap == 50
+    s = eng.submit(np.arange(10), 30, cap=80)
+    assert s.cap == s.loose_cap == 30
+    with pytest.raises(ValueError):
+        eng.submit(np.arange(10), 50, suspend=[(1, 2), (10, 11), (20, 21)])     # three disjoint windows > 2
+    v = Voice(np.arange(20), None, 20)
+    s = eng.submit(np.arange(10), 200, voice=v)
+    assert s.max_frames == 128 - 30 - 2 and s.voice is v
+    eng.submit(np.arange(100), 10)                                           # fits without the prefix
+    with pytest.raises(ValueError):
+        eng.submit(np.arange(100), 10, voice=v)                              # 6 frames left: refused
+    assert len(eng.pending) == 5
