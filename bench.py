@@ -15,8 +15,10 @@ Numbers (one JSON line on rank 0):
   e2e         the same metric through the engine's public tick (TickEngine.tick): per tick the plan is copied
               host->device and the packed (stop, cb0, PCM) readout device->host, with one sync, wall-clocked;
   roofline    the split-KV decode attention (the dominant kernel) re-timed on the live cache after the run;
-  cpu_baseline the CPU oracle (fp32 numpy port of the reference's eager path) on this host's cores, on a bounded
-              sample (one tick of 16 seats at the same KV-length distribution).
+  reference_gpu the reference's own serving engine (its Engine._tick over its Triton + CUDA-graph StaticBackbone,
+              FastDepth and StaticMimi, installed in baseline/_ref) on the same GPU, same seat mix, wall-clocked;
+  cpu_baseline the reference's own eager CPU path (fp32) on this host's cores, on a bounded sample (decode ticks of
+              8 seats at the same KV-length distribution); `--impl reference` prints that arm's own line.
 The KV cache (~60 GB per replica) is far larger than L2, so consecutive ticks never hit in L2 on the cache.
 Multi-GPU: one process per GPU, each an independent replica with its own 256 seats (weak scaling, no collective on
 the path; torch.distributed only for the start/stop barriers and the max-over-ranks reduction).
@@ -57,7 +59,8 @@ def args_():
     ap.add_argument("--capacity", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seats", type=int, default=16)
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference engine's run on this GPU (baseline/_ref)")
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[4] box, configs[1] TTFA and configs[3] Mimi runs")
     ap.add_argument("--tick-breakdown", action="store_true",
                     help="time each tick of the device-resident run and print the mean for ticks with and without "
@@ -639,27 +642,73 @@ def cpu_tick_sample(seats, seed=0, reps=1):
     return min(times), os.cpu_count()
 
 
+REF_CPU_SEATS = 8
+
+
 def run_reference(a, rank, world):
-    """--impl reference: the reference's algorithm on this host's CPU cores (the numpy oracle port; the reference
-    is Python and cannot travel to this machine), one step = one tick of 8 seats at the configs[2] distribution."""
-    seats = 8
-    t_per = []
-    from maya2_native_b200 import weights as WG   # noqa: F401  (weights are generated inside the sample)
-    ticks = max(1, a.steps)
-    sec, cores = cpu_tick_sample(seats, a.seed, reps=1)
-    t_per.append(sec)
-    for _ in range(min(ticks - 1, 2)):
-        s2, _ = cpu_tick_sample(seats, a.seed, reps=1)
-        t_per.append(s2)
-    sec = float(np.median(t_per))
+    """--impl reference: the reference's own eager CPU path (baseline/_ref: StaticBackbone 'gather', Engine._cb0,
+    FastDepth._compute, StaticMimi._forward, fp32) on this host's cores, one step = one decode tick of 8 seats at the
+    configs[2] KV-length distribution, W untimed ticks then K timed ones.  Without the install, the numpy oracle
+    port of the same path stands in (kind "port")."""
+    from baseline import reference_arm as RA
+    from maya2_native_b200.config import BASELINE
+    seats = REF_CPU_SEATS
+    why = RA.unavailable()
+    if why is None:
+        wl = Workload(BASELINE.backbone.vocab, a.seed * 7919)
+        times, cores = RA.cpu_tick(BASELINE, wl, seats, a.capacity, ticks=max(1, a.steps), warmup=a.warmup,
+                                   seed=a.seed)
+        kind = "reference"
+        sample = (f"one decode tick of {seats} seats at the configs[2] KV-length distribution through the "
+                  "reference's own eager CPU path (fp32)")
+    else:
+        times, cores = [], os.cpu_count()
+        for _ in range(max(1, a.steps)):
+            sec, cores = cpu_tick_sample(seats, a.seed, reps=1)
+            times.append(sec)
+        kind = "port"
+        sample = f"one decode tick of {seats} seats at the configs[2] KV-length distribution, fp32 numpy port ({why})"
+    sec = float(np.mean(times))
     v = seats * FRAME_S / sec
-    return {"metric": METRIC, "value": round(v, 4), "unit": "audio-s/s", "n_gpus": world, "steps": len(t_per),
-            "warmup": 0, "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "configs[2] seat mix, CPU sample: one tick of 8 seats", "seats": seats},
-            "cpu_baseline": {"value": round(v, 4), "unit": "audio-s/s", "cores": cores, "kind": "port",
-                             "sample": f"one decode tick of {seats} seats at the configs[2] KV-length distribution"},
+    return {"metric": METRIC, "value": round(v, 4), "unit": "audio-s/s", "n_gpus": world, "steps": len(times),
+            "warmup": a.warmup if kind == "reference" else 0, "ms_per_step": round(sec * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"configs[2] seat mix, CPU sample: decode ticks of {seats} seats", "seats": seats,
+                       "capacity": a.capacity},
+            "cpu_baseline": {"value": round(v, 4), "unit": "audio-s/s", "cores": cores, "kind": kind,
+                             "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_cpu_line(a):
+    """The --impl reference line for a short CPU sample (2 timed ticks after 1 warm), run in a child process: the
+    reference's CPU path runs its Triton sampler in the interpreter, a process-wide switch."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR",
+                                                            "MASTER_PORT", "LOCAL_WORLD_SIZE")}
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    cmd = [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "1",
+           "--capacity", str(a.capacity), "--seed", str(a.seed)]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
+    for line in r.stdout.splitlines()[::-1]:
+        if line.startswith("{"):
+            return json.loads(line)
+    raise RuntimeError(f"reference CPU sample failed (rc {r.returncode}): {r.stderr[-400:]}")
+
+
+def run_reference_gpu(a, dev, native_e2e, native_value):
+    """The reference's own serving engine (Triton + CUDA graphs, baseline/_ref) on this GPU at configs[2]: same seat
+    mix, steady-state start, W untimed and K timed ticks; reported beside the native arm's numbers."""
+    from baseline import reference_arm as RA
+    from maya2_native_b200.config import BASELINE
+    why = RA.unavailable()
+    if why is not None:
+        return {"unavailable": why}
+    wl = Workload(BASELINE.backbone.vocab, a.seed * 7919)
+    out = RA.gpu_arm(dev, wl, a.seats, a.capacity, steps=a.steps, warmup=a.warmup, seed=a.seed)
+    out["native_e2e_over_reference"] = round(native_e2e / out["value"], 3)
+    out["native_value_over_reference"] = round(native_value / out["value"], 3)
+    return out
 
 
 def main():
@@ -682,11 +731,15 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     with torch.inference_mode():
         line = run_native(a, rank, world, local)
+    if rank == 0 and world == 1 and not a.no_extra and not a.no_reference_gpu:
+        try:
+            line["reference_gpu"] = run_reference_gpu(a, torch.device("cuda", local), line["e2e"]["value"],
+                                                      line["value"])
+        except Exception as exc:                      # reported, not fatal: the native line still stands
+            line["reference_gpu"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        sec, cores = cpu_tick_sample(a.cpu_seats, a.seed)
-        line["cpu_baseline"] = {"value": round(a.cpu_seats * FRAME_S / sec, 4), "unit": "audio-s/s", "cores": cores,
-                                "kind": "port", "sample": f"one decode tick of {a.cpu_seats} seats at the configs[2] "
-                                                          "KV-length distribution, fp32 numpy oracle"}
+        ref = reference_cpu_line(a)
+        line["cpu_baseline"] = ref["cpu_baseline"]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
