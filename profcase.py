@@ -1,11 +1,15 @@
 """Small GPU cases for Nsight Compute captures: a few GB on the device, inputs still far larger than L2.
 
-    python -m maya2_native_b200.profcase attention [--seats 64] [--layers 2] [--steps 3]
-    python -m maya2_native_b200.profcase tick [--seats 64] [--steps 3]
+    python profcase.py attention [--seats 64] [--layers 2] [--steps 3]
+    python profcase.py tick [--seats 64] [--steps 3]
+
+Part of the measurement harness beside bench.py (the summaries under profiles/ name the command that made them);
+not imported by the library.
 
 attention: the backbone step over `seats` decode rows at the configs[2] KV-length distribution (mean ~790 keys),
            benchmark width, `layers` layers (2 layers x 64 seats ~ 1 GB of K/V); run under
-           `ncu -k regex:attn_split -c 3`.
+           `ncu --clock-control none -k regex:attn_mma -c 3` (every ncu command needs --clock-control none: without
+           it ncu locks the GPU's clocks, a setting the GPU's next user would inherit).
 tick:      the full engine tick at the benchmark geometry with fewer seats.
 mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
 gaps:      per-node cost of a CUDA graph of dependent tiny kernels.
@@ -16,9 +20,13 @@ from __future__ import annotations
 
 import argparse
 import dataclasses
+import os
+import sys
 
 import numpy as np
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 
 def _lengths(n, rng):
@@ -29,9 +37,9 @@ def _lengths(n, rng):
 
 @torch.inference_mode()
 def attention(a):
-    from . import weights as WG
-    from .backbone import StaticBackbone
-    from .config import BASELINE
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.backbone import StaticBackbone
+    from maya2_native_b200.config import BASELINE
     g = dataclasses.replace(BASELINE.backbone, layers=a.layers)
     dev = torch.device("cuda", 0)
     W = WG.generate({k: v for k, v in WG.backbone_shapes(g).items() if "embed" not in k}, device=dev)
@@ -55,9 +63,9 @@ def attention(a):
 
 @torch.inference_mode()
 def tick(a):
-    from . import weights as WG
-    from .config import BASELINE
-    from .engine import TickConfig, TickEngine
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.config import BASELINE
+    from maya2_native_b200.engine import TickConfig, TickEngine
     dev = torch.device("cuda", 0)
     W = WG.generate(WG.all_shapes(BASELINE), device=dev)
     eng = TickEngine(BASELINE, W, TickConfig(max_seats=a.seats, capacity=2048, stops=False), device=dev)
@@ -75,9 +83,9 @@ def tick(a):
 @torch.inference_mode()
 def mimi(a):
     """StaticMimi.decode at the benchmark geometry over `seats` streams (codes U[0, 2048)), `steps` frames."""
-    from . import weights as WG
-    from .codec import StaticMimi
-    from .config import BASELINE
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.codec import StaticMimi
+    from maya2_native_b200.config import BASELINE
     dev = torch.device("cuda", 0)
     g = BASELINE.mimi
     shapes = {k: v for k, v in WG.all_shapes(BASELINE).items() if k.startswith("mimi.")}
@@ -122,10 +130,10 @@ def overlap(a):
     """Could the Mimi decode of one frame hide under the next frame's backbone step?  Graph-captured backbone step
     (decode rows of `seats` seats, configs[2] KV-length distribution, benchmark width, all layers) and Mimi decode
     (`seats` streams), timed back to back on one stream and concurrently on two."""
-    from . import weights as WG
-    from .backbone import StaticBackbone
-    from .codec import StaticMimi
-    from .config import BASELINE
+    from maya2_native_b200 import weights as WG
+    from maya2_native_b200.backbone import StaticBackbone
+    from maya2_native_b200.codec import StaticMimi
+    from maya2_native_b200.config import BASELINE
     dev = torch.device("cuda", 0)
     g = BASELINE
     W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
@@ -206,7 +214,7 @@ def gemm(a):
     """Time each implementation of m3_gemm_bf16 on the tick's linear-layer shapes (bf16 out; CUDA events over graph
     replays).  --cold cycles through enough weight copies (> 2x L2) that every launch streams its weights from HBM,
     as the tick's 28 layers do."""
-    from . import _lib as L
+    from maya2_native_b200 import _lib as L
     dev = torch.device("cuda", 0)
     lib = L.load()
     print(f"{'layer':16s} {'M':>7s} {'N':>5s} {'K':>5s}   cublas us  tcgen05 us  small us   TF/s(best own)")
@@ -255,7 +263,7 @@ def gemm(a):
 def guard(a):
     """m3_guard_step over `seats` seats whose histories are full and whose every update is due (frame 100, the loop
     rule evaluated for all: the worst case), timed with CUDA events as eager launches and replayed from a graph."""
-    from .guards import DeviceGuards, GuardConfig
+    from maya2_native_b200.guards import DeviceGuards, GuardConfig
     dev = torch.device("cuda", 0)
     S = a.seats
     bias = torch.zeros(S + 1, device=dev)

@@ -252,7 +252,7 @@ def gen_mimi(dtype, frames=24):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MAYA3_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", required=True, help="path of a reference checkout (read-only; used only here)")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
