@@ -168,6 +168,14 @@ typedef struct {         /* per-slot state tensors of maya3/engine.py:210-223, e
 
 M3_API int m3_cb0_create(const m3_cb0_config* cfg, const m3_cb0_state* st, m3_cb0** out);
 M3_API int m3_cb0_destroy(m3_cb0* s);
+/* Read (and optionally clear) the handle's device status word (a row whose slot was outside [0, max_slots] was
+ * sampled from the padding slot's state: M3_DEV_BAD_SLOT); synchronises with the device.  The reference raises
+ * IndexError on the host for such a slot (maya3/engine.py:652-694 indexes its per-slot tensors with it). */
+M3_API int m3_cb0_status(m3_cb0* s, int32_t* status, int32_t clear);
+/* Inspection: the head output of the handle's last m3_cb0_step (the bf16 logits [rows, n_cls] its sampler read,
+ * before temperature and bias) into dst (bf16 [rows, n_cls], dense), stream-ordered.  The reference's counterpart is
+ * Backbone.cb0_logits(h) (tts/model/backbone.py:97), which Engine._cb0 calls first (maya3/engine.py:657). */
+M3_API int m3_cb0_copy_logits(m3_cb0* s, void* dst, int32_t rows, m3_stream stream);
 /* h [rows, hidden] bf16, idx [rows] slot per row -> stop code [rows] (0 or REASONS 2/3/4, maya3/engine.py:46) and
  * cb0 [rows] in [0, 2047]; advances the per-slot state.  apply_rep / apply_top_p mirror the engine's host flags
  * (`cb0_rep_win > 0 and (cb0_rep > 0 or any_rep)`, `_any_top_p`). */
@@ -178,13 +186,20 @@ M3_API int m3_cb0_step(m3_cb0* s, const void* h, const int64_t* idx, int64_t* co
  * latency-critical serving thread on which cudaMalloc / cudaFree would synchronise the device and stall every seat.
  * This entry point has no counterpart in the reference (which samples with eager torch ops that allocate freely).
  * Same arguments and results as m3_cb0_step, with the configuration and per-slot state passed directly; limits:
- * rows <= 8 per call, n_cls <= 4096, hidden <= 3072 (a multiple of 8); larger calls are rejected with M3_ERR_ARG.
+ * rows <= 8 per call, n_cls <= 4096, hidden <= 3072 (a multiple of 8), h and st->head on 16-byte boundaries; other
+ * calls are rejected with M3_ERR_ARG before any device work.
  * Scratch: a 64 KiB static device array inside the library, held by every GPU that loads it until the process
  * exits.  The first call on a device looks up that array's device address, so make it before any stream capture.
- * Every call shares the one array: calls that overlap on the GPU (different streams without ordering) race. */
+ * Every call shares the one array: calls that overlap on the GPU (different streams without ordering) race.
+ * Problems seen inside the kernel (a slot outside [0, max_slots], sampled from the padding slot's state) go to a
+ * status word in the same array: zero when the library loads, it keeps the first problem of any call until
+ * m3_cb0_noalloc_status clears it. */
 M3_API int m3_cb0_step_noalloc(const m3_cb0_config* cfg, const m3_cb0_state* st, const void* h, const int64_t* idx,
                                int64_t* code, int64_t* cb0, int32_t rows, int32_t apply_rep, int32_t apply_top_p,
                                m3_stream stream);
+/* Read (and optionally clear) the status word of m3_cb0_step_noalloc on the current device; synchronises with the
+ * device and allocates nothing. */
+M3_API int m3_cb0_noalloc_status(int32_t* status, int32_t clear);
 /* The sampler alone on given fp32 logits [rows, n_cls] (the cb0 head output as fp32). */
 M3_API int m3_cb0_sample_logits(m3_cb0* s, const float* logits, const int64_t* idx, int64_t* code, int64_t* cb0,
                          int32_t rows, int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
@@ -243,6 +258,11 @@ M3_API int m3_topk_sample(const void* logits, int32_t logits_bf16, int32_t rows,
                    const int32_t* ctr, int32_t level, float inv_temp, int32_t top_k, int32_t greedy, int64_t* codes,
                    m3_stream stream);
 M3_API int m3_depth_status(m3_depth* d, int32_t* status, int32_t clear);
+/* Inspection: with buf set (bf16 [n_q - 1][max_rows][n_codes], 16-byte aligned), every later m3_depth_step (and every
+ * step captured into a graph after this call) writes level l's head logits to buf[l - 1] instead of its scratch, so
+ * they can be compared with the reference's d.heads[level - 1](y) (serve/fast_depth.py:190-191); NULL restores the
+ * scratch.  bytes < the size above -> M3_ERR_ARG. */
+M3_API int m3_depth_debug_logits(m3_depth* d, void* buf, int64_t bytes);
 
 /* ---------------------------------------------------------------------------------------------- mimi */
 /* Replaces StaticMimi (serve/fast_codec.py:32-277): one 80 ms frame per seat with per-slot streaming state. */

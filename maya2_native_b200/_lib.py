@@ -106,6 +106,10 @@ SIGNATURES = {
     "m3_cb0_step": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "m3_cb0_sample_logits": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "m3_cb0_step_noalloc": (C.c_int, [P(Cb0Config), P(Cb0State), vp, vp, vp, vp, i32, i32, i32, vp]),
+    "m3_cb0_noalloc_status": (C.c_int, [P(i32), i32]),
+    "m3_cb0_status": (C.c_int, [vp, P(i32), i32]),
+    "m3_cb0_copy_logits": (C.c_int, [vp, vp, i32, vp]),
+    "m3_depth_debug_logits": (C.c_int, [vp, vp, i64]),
     "m3_depth_create": (C.c_int, [P(DepthConfig), P(DepthWeights), P(vp)]),
     "m3_depth_destroy": (C.c_int, [vp]),
     "m3_depth_set_speaker": (C.c_int, [vp, i32, vp, f32, vp]),

@@ -526,6 +526,22 @@ extern "C" int m3_cb0_destroy(m3_cb0* s) {
   return M3_OK;
 }
 
+extern "C" int m3_cb0_copy_logits(m3_cb0* s, void* dst, int32_t rows, m3_stream stream) {
+  M3_REQUIRE(s && dst, M3_ERR_ARG, "m3_cb0_copy_logits: null argument");
+  M3_REQUIRE(rows >= 0 && rows <= s->c.max_rows, M3_ERR_RANGE, "rows %d > max_rows %d", rows, s->c.max_rows);
+  if (rows == 0) return M3_OK;
+  M3_CUDA(cudaMemcpy2DAsync(dst, (size_t)s->c.n_cls * 2, s->logits, (size_t)s->ldl * 2, (size_t)s->c.n_cls * 2, rows,
+                            cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(stream)));
+  return M3_OK;
+}
+
+extern "C" int m3_cb0_status(m3_cb0* s, int32_t* status, int32_t clear) {
+  M3_REQUIRE(s && status, M3_ERR_ARG, "m3_cb0_status: null argument");
+  M3_CUDA(cudaMemcpy(status, s->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (clear) M3_CUDA(cudaMemset(s->status, 0, sizeof(int32_t)));
+  return M3_OK;
+}
+
 static int cb0_launch(m3_cb0* s, const void* logits, int64_t ld, bool bf, const int64_t* idx, int64_t* code,
                       int64_t* cb0, int rows, int apply_rep, int apply_top_p, cudaStream_t st) {
   if (rows == 0) return M3_OK;
@@ -617,13 +633,15 @@ extern "C" int m3_cb0_step_noalloc(const m3_cb0_config* cfg, const m3_cb0_state*
              "m3_cb0_step_noalloc: hidden %d must be a multiple of 8 and at most 3072", cfg->hidden);
   M3_REQUIRE(cfg->rep_win >= 0 && cfg->rep_win <= kSampThreads, M3_ERR_ARG,
              "m3_cb0_step_noalloc: rep_win %d exceeds %d", cfg->rep_win, kSampThreads);
+  M3_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(st->head)) & 15) == 0, M3_ERR_ARG,
+             "m3_cb0_step_noalloc: h and the head must start on 16-byte boundaries");
   void* scratch = nullptr;
   M3_TRY(noalloc_scratch(&scratch));
   if (rows == 0) return M3_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   bf16* logits = reinterpret_cast<bf16*>(scratch);
+  // the status word is sticky across calls (zero at load, first problem wins) until m3_cb0_noalloc_status clears it
   int* status = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + kNoAllocLogitsBytes);
-  M3_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));  // the array keeps the previous call's status word
   M3_TRY(gemv_only({(const bf16*)h, cfg->hidden, (const bf16*)st->head, cfg->hidden, logits, cfg->n_cls, rows,
                     cfg->n_cls, cfg->hidden, false},
                    s));
@@ -632,5 +650,15 @@ extern "C" int m3_cb0_step_noalloc(const m3_cb0_config* cfg, const m3_cb0_state*
   cb0_sample_kernel<bf16><<<rows, kSampThreads, 0, s>>>(logits, cfg->n_cls, cfg->n_cls, idx, dev, apply_rep,
                                                          apply_top_p, code, cb0, status);
   M3_LAUNCHED();
+  return M3_OK;
+}
+
+extern "C" int m3_cb0_noalloc_status(int32_t* status, int32_t clear) {
+  M3_REQUIRE(status, M3_ERR_ARG, "m3_cb0_noalloc_status: null argument");
+  void* scratch = nullptr;
+  M3_TRY(noalloc_scratch(&scratch));
+  int* word = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + kNoAllocLogitsBytes);
+  M3_CUDA(cudaMemcpy(status, word, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (clear) M3_CUDA(cudaMemset(word, 0, sizeof(int32_t)));
   return M3_OK;
 }

@@ -126,6 +126,7 @@ extern "C" int m3_tick_status(m3_tick* t, int32_t* status, int32_t clear) {
   M3_TRY(m3_backbone_status(t->c.bb, &s[1], clear));
   M3_TRY(m3_depth_status(t->c.depth, &s[2], clear));
   M3_TRY(m3_mimi_status(t->c.mimi, &s[3], clear));
+  M3_TRY(m3_cb0_status(t->c.cb0, &s[4], clear));
   if (clear) M3_CUDA(cudaMemset(t->status, 0, 4));
   *status = 0;
   for (int i = 0; i < 5 && !*status; ++i) *status = s[i];

@@ -60,6 +60,20 @@ class Cb0Sampler:
         except Exception:
             pass
 
+    def device_status(self, clear=True) -> int:
+        """The handle's device status word (M3_DEV_BAD_SLOT after a row named a slot outside [0, max_slots]);
+        synchronises with the device."""
+        s = L.i32(0)
+        L.check(L.load().m3_cb0_status(self._handle, s, int(clear)), "m3_cb0_status")
+        return int(s.value)
+
+    def copy_logits(self, rows):
+        """The bf16 head logits [rows, 2049] the last step's sampler read (a copy, stream-ordered)."""
+        out = torch.empty(int(rows), self.n_cls, device=self.device, dtype=torch.bfloat16)
+        L.check(L.load().m3_cb0_copy_logits(self._handle, out.data_ptr(), int(rows), L.stream_ptr()),
+                "m3_cb0_copy_logits")
+        return out
+
     def flags(self):
         """The engine's host-side switches: penalty when cb0_rep_win > 0 and (cb0_rep > 0 or any request set one);
         top-p when any request asked for top_p < 1 (maya3/engine.py:660,669)."""

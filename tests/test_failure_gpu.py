@@ -12,6 +12,7 @@ from maya2_native_b200 import _lib as L
 from maya2_native_b200 import weights as WG
 from maya2_native_b200.backbone import StaticBackbone
 from maya2_native_b200.config import TINY
+from maya2_native_b200.sampler import Cb0Sampler
 
 pytestmark = pytest.mark.gpu
 DEV_BAD_SLOT, DEV_BAD_POS, DEV_TIMEOUT = 1, 2, 4
@@ -62,3 +63,24 @@ def test_bad_slot_and_position_are_contained_and_reported(cuda):
     assert sb.device_status() == DEV_BAD_POS
     assert torch.isfinite(out.float()).all()
     sb.close()
+
+
+def test_cb0_bad_slot_is_contained_and_reported(cuda):
+    """The cb0 handle: a row naming a slot past max_slots is sampled from the padding slot's state and reported in
+    the handle's status word; both rows equal a clean call that names the padding slot itself."""
+    g = TINY.backbone
+    head = WG.make("cb0_head.weight", (g.n_cb0, g.hidden))
+    ref = Cb0Sampler(head, 3, max_rows=4, device=cuda)
+    s = Cb0Sampler(head, 3, max_rows=4, device=cuda)
+    for x in (ref, s):
+        x.seed_t[:] = 7
+    h = torch.randn(2, g.hidden, device=cuda).to(torch.bfloat16)
+    code_r, cb0_r = ref(h, torch.tensor([1, 3], device=cuda))           # slot 3 = the padding slot
+    code, cb0 = s(h, torch.tensor([1, 99], device=cuda))
+    torch.cuda.synchronize()
+    assert s.device_status() == DEV_BAD_SLOT
+    assert s.device_status() == 0                               # read-and-clear
+    assert ref.device_status() == 0
+    assert code.tolist() == code_r.tolist() and cb0.tolist() == cb0_r.tolist()
+    s.close()
+    ref.close()
