@@ -420,6 +420,7 @@ struct m3_depth {
   int *slot32 = nullptr, *cb032 = nullptr, *status = nullptr;
   bf16 *prefix = nullptr, *x = nullptr, *x2 = nullptr, *y = nullptr, *qkvb = nullptr, *a = nullptr, *ob = nullptr,
        *ff = nullptr, *logits = nullptr, *proj = nullptr, *kvbuf = nullptr, *spk = nullptr;
+  bf16* dbg_logits = nullptr;  // m3_depth_debug_logits: every level's head output kept for inspection
 };
 
 namespace {
@@ -521,6 +522,16 @@ extern "C" int m3_depth_status(m3_depth* d, int32_t* status, int32_t clear) {
   M3_REQUIRE(d && status, M3_ERR_ARG, "m3_depth_status: null argument");
   M3_CUDA(cudaMemcpy(status, d->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
   if (clear) M3_CUDA(cudaMemset(d->status, 0, sizeof(int32_t)));
+  return M3_OK;
+}
+
+extern "C" int m3_depth_debug_logits(m3_depth* d, void* buf, int64_t bytes) {
+  M3_REQUIRE(d, M3_ERR_ARG, "m3_depth_debug_logits: null handle");
+  const int64_t need = (int64_t)(d->c.n_q - 1) * d->c.max_rows * d->c.n_codes * 2;
+  M3_REQUIRE(!buf || bytes >= need, M3_ERR_ARG, "m3_depth_debug_logits: %lld bytes, need %lld", (long long)bytes,
+             (long long)need);
+  M3_REQUIRE(((uintptr_t)buf & 15) == 0, M3_ERR_ARG, "m3_depth_debug_logits: buffer must be 16-byte aligned");
+  d->dbg_logits = (bf16*)buf;
   return M3_OK;
 }
 
@@ -630,7 +641,8 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
                     d->slot32, d->x, d->y, nw, nb, c.ln_eps, D, s));
     }
     // level head on the final position, then sample and write the next prefix row
-    M3_TRY(gemm({d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, d->logits, c.n_codes, R,
+    bf16* lg = d->dbg_logits ? d->dbg_logits + (int64_t)(level - 1) * c.max_rows * c.n_codes : d->logits;
+    M3_TRY(gemm({d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, lg, c.n_codes, R,
                  c.n_codes, D, false},
                 s));
     const bool more = n < NL;
@@ -641,7 +653,7 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       ln = PrefixLn{d->prefix, (int64_t)NL * D, inc2 ? level + 1 : 0, inc2 ? 1 : level + 2, d->x, d->y,
                     d->n1_w[g2 * L], d->n1_b[g2 * L], c.ln_eps};
     }
-    M3_TRY(launch_topk_sample(d->logits, true, c.n_codes, R, c.n_codes, d->row_seed, d->row_ctr, d->slot32, level,
+    M3_TRY(launch_topk_sample(lg, true, c.n_codes, R, c.n_codes, d->row_seed, d->row_ctr, d->slot32, level,
                               c.inv_temp, c.top_k, c.greedy, codes + level, NL,
                               more ? d->embed + (int64_t)level * c.n_codes * D : nullptr, D,
                               more ? d->prefix + (int64_t)n * D : nullptr, (int64_t)NL * D, s, ln));

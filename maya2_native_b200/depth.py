@@ -103,6 +103,16 @@ class FastDepth:
         L.check(L.load().m3_depth_create(cfg, wts, h), "m3_depth_create")
         return h
 
+    def debug_logits(self):
+        """Keep every level's head logits (bf16 [n_q - 1, max_rows, n_codes]) from the next step on (steps captured
+        into graphs afterwards included); returns the buffer, whose rows [:B] hold the latest step's seats."""
+        g = self.geom
+        buf = torch.zeros(g.n_q - 1, max(self.batch_buckets), g.n_codes, device=self.device, dtype=torch.bfloat16)
+        L.check(L.load().m3_depth_debug_logits(self._handle, buf.data_ptr(), buf.numel() * 2),
+                "m3_depth_debug_logits")
+        self._dbg = buf
+        return buf
+
     def close(self):
         if getattr(self, "_handle", None):
             self.graphs.clear()

@@ -53,6 +53,7 @@ class TickConfig:
     seed: int = 20261024
     stops: bool = True                # False: forced lengths, stop codes are ignored
     min_frames: int = 4
+    greedy: bool = False              # depth levels by argmax (FastDepth greedy); cb0 greedy is cb0_top_k = 1
     use_graphs: bool = True
     guards: Optional[GuardConfig] = None   # loop guard + frame cap on the device (maya3/engine.py:69); None = off
 
@@ -184,7 +185,7 @@ class TickEngine:
                               top_k=cfg.cb0_top_k, top_p=cfg.cb0_top_p, rep=cfg.cb0_rep, rep_win=cfg.cb0_rep_win,
                               device=dev)
         self.depth = FastDepth(weights, n, temp=cfg.temp, top_k=cfg.top_k, batch_buckets=self.buckets,
-                               seed=cfg.seed + 1, geom=g.depth, device=dev)
+                               seed=cfg.seed + 1, greedy=cfg.greedy, geom=g.depth, device=dev)
         self.codec = StaticMimi(weights, n, batch_buckets=self.buckets, geom=g.mimi, device=dev)
         D = g.backbone.hidden
         with torch.inference_mode():

@@ -43,7 +43,8 @@ def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
         eng.submit(rng.integers(0, g.backbone.vocab, m), max_frames=ticks + 4, seed=1000 + i)
     null_mem = Wn["depth.null_mem"]
     embed = ora.bb.rnd(Wn["model.embed_tokens.weight"])
-    res = {"h_err": [], "cb0_hit": 0, "cb0_n": 0, "code_hit": 0, "code_n": 0, "fb_err": [], "snr": []}
+    res = {"h_err": [], "cb0_hit": 0, "cb0_n": 0, "code_hit": 0, "code_n": 0, "fb_err": [], "snr": [],
+           "cb0_logits": []}
     fb_prev = None
     for tick in range(ticks):
         dec = list(eng.active)
@@ -68,7 +69,9 @@ def run_stage_parity(g, cuda, lens, ticks, capacity, max_inline=None):
         else:   # each seat's own feedback vector from the previous tick
             h_o = ora.bb.step(list(slots), np.stack([fb_prev[int(sl)] for sl in slots]))
         res["h_err"].append(float(np.linalg.norm(h_o - h_gpu) / np.linalg.norm(h_o)))
-        _, cb0_o, _ = ora.cb0(h_gpu, slots)
+        lg_gpu = eng.cb0.copy_logits(n).float().cpu().numpy()
+        _, cb0_o, lg_o = ora.cb0(h_gpu, slots)
+        res["cb0_logits"].append(float(np.abs(lg_gpu - lg_o).max() / max(1.0, float(np.abs(lg_o).max()))))
         res["cb0_hit"] += int((cb0_o == cb0_gpu).sum())
         res["cb0_n"] += len(slots)
         ora.st.hist[slots, -1] = cb0_gpu                 # keep the repetition window on the GPU's trajectory
@@ -92,6 +95,7 @@ def test_tick_matches_oracle_stage_by_stage(cuda):
     assert r["cb0_hit"] / r["cb0_n"] >= 0.9, r
     assert r["code_hit"] / r["code_n"] >= 0.9, r
     assert max(r["fb_err"]) < 5e-2, r
+    assert max(r["cb0_logits"]) <= 2e-2, r
     assert min(r["snr"]) > 30, r
 
 
@@ -106,7 +110,8 @@ def test_tick_benchmark_geometry_stage_by_stage(cuda):
     assert r["cb0_hit"] / r["cb0_n"] >= 0.85, r
     assert r["code_hit"] / r["code_n"] >= 0.85, r
     assert max(r["fb_err"]) < 1e-1, r
-    assert min(r["snr"]) > 25, r
+    assert max(r["cb0_logits"]) <= 2e-2, r
+    assert min(r["snr"]) > 30, r
 
 
 def test_tick_eager_prefill_of_a_long_prompt(cuda):
