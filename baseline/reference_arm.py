@@ -46,12 +46,16 @@ def unavailable():
     return None
 
 
-def _use_reference():
+def use_reference():
+    """Put the reference install on sys.path (raises when it is absent)."""
     why = unavailable()
     if why:
         raise RuntimeError(why)
     if REF not in sys.path:
         sys.path.insert(0, REF)
+
+
+_use_reference = use_reference
 
 
 def _patch_depth(g):
@@ -84,10 +88,7 @@ def build_models(geom, device, seed=0, mimi_dtype=None):
     from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
 
     _use_reference()
-    _patch_depth(geom.depth)
-    from tts.model.audio_io import AudioInputEmbed
     from tts.model.backbone import Backbone
-    from tts.model.depth_v2 import DepthV2
 
     gpu = str(device).startswith("cuda")
     dt = torch.bfloat16 if gpu else torch.float32
@@ -111,15 +112,7 @@ def build_models(geom, device, seed=0, mimi_dtype=None):
     _load_named(bb.cb0_head, "cb0_head.", seed, device)
     bb.cb0_head.to(dt)
 
-    d = geom.depth
-    with torch.device("meta"):
-        depth = DepthV2(d_backbone=d.d_backbone, n_q=d.n_q, n_codes=d.n_codes)
-    depth = depth.to_empty(device=device)
-    _load_named(depth, "depth.", seed, device)
-    depth = depth.float().eval()
-    audio_in = AudioInputEmbed(d.d_backbone, n_q=d.n_q, n_codes=d.n_codes).to(device)
-    _load_named(audio_in, "audio_in.", seed, device)
-    audio_in = audio_in.to(dt).eval()
+    depth, audio_in = build_depth(geom, device, seed, dt)
 
     m = geom.mimi
     mcfg = MimiConfig(hidden_size=m.hidden, num_quantizers=m.n_q, num_semantic_quantizers=m.n_semantic,
@@ -140,10 +133,32 @@ def build_models(geom, device, seed=0, mimi_dtype=None):
     return model, mimi
 
 
+def build_depth(geom, device, seed=0, audio_dtype=None):
+    """The reference's ``DepthV2`` (fp32, as the engine keeps it: maya3/engine.py:158) and backbone-width
+    ``AudioInputEmbed`` at `geom` on `device`, from the seeded weights.  Returns (depth, audio_in)."""
+    import torch
+    _use_reference()
+    _patch_depth(geom.depth)
+    from tts.model.audio_io import AudioInputEmbed
+    from tts.model.depth_v2 import DepthV2
+    d = geom.depth
+    with torch.device("meta"):
+        depth = DepthV2(d_backbone=d.d_backbone, n_q=d.n_q, n_codes=d.n_codes)
+    depth = depth.to_empty(device=device)
+    _load_named(depth, "depth.", seed, device)
+    depth = depth.float().eval()
+    audio_in = AudioInputEmbed(d.d_backbone, n_q=d.n_q, n_codes=d.n_codes).to(device)
+    _load_named(audio_in, "audio_in.", seed, device)
+    audio_in = audio_in.to(audio_dtype or (torch.bfloat16 if str(device).startswith("cuda") else torch.float32))
+    return depth, audio_in.eval()
+
+
 # ------------------------------------------------------------------------------------------------ GPU arm
-def _engine(model, mimi, device, seats, capacity, depth_dtype):
+def _engine(model, mimi, device, seats, capacity, depth_dtype, **cfg):
     """A reference ``Engine`` built by its own ``_build_fast`` around the given models (``Engine.__init__`` would load
-    a checkpoint, a tokenizer and a voice registry, none of which the decode path uses)."""
+    a checkpoint, a tokenizer and a voice registry, none of which the decode path uses).  The fp32 depth stack is kept
+    after FastDepth copies it (``free_reference_depth=False``) so further engines can be built from the same models;
+    it is not read by the tick."""
     import torch
     from maya3 import engine as ME
     from maya3 import guards as G
@@ -151,7 +166,7 @@ def _engine(model, mimi, device, seats, capacity, depth_dtype):
     torch.backends.cuda.matmul.allow_tf32 = False
     E = ME.Engine.__new__(ME.Engine)
     E.cfg = ME.EngineConfig(max_seats=seats, capacity=capacity, depth_dtype=depth_dtype,
-                            guards=G.GuardConfig(enabled=False))
+                            guards=G.GuardConfig(enabled=False), free_reference_depth=False, **cfg)
     E.device = device
     E.log = lambda *a, **k: None
     E.model = model
@@ -179,24 +194,23 @@ def _engine(model, mimi, device, seats, capacity, depth_dtype):
     return E
 
 
-def gpu_arm(device, wl, seats=256, capacity=2048, steps=50, warmup=10, seed=0, geom=None, depth_dtype="bf16",
-            mimi_dtype="bf16"):
-    """The configs[2] workload through the reference's own engine tick on one GPU.  `wl` is bench.py's Workload (the
-    same request stream and steady-state start as the native arm).  Returns the measurement as a dict."""
+def _voice(model, device):
+    """A plain voice (no prefix, null speaker memory): the fields Engine._admit/_bind read."""
     import torch
-    from maya2_native_b200.config import BASELINE
-    geom = geom or BASELINE
-    _use_reference()
+    return types.SimpleNamespace(ts=0, kv=None, builder=None,
+                                 mem=model.depth.spk_memory(torch.zeros(1, 1, 192, device=device), "ecapa",
+                                                            null_mask=torch.tensor([True], device=device)),
+                                 rmask=torch.ones(1, 1, dtype=torch.bool, device=device))
+
+
+def _tick_run(model, mimi, device, wl, seats, capacity, steps, warmup, depth_dtype):
+    """configs[2] through one reference engine: steady-state start, W untimed ticks, K ticks wall-clocked."""
+    import torch
     from maya3 import engine as ME
-    mdt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[mimi_dtype]
     t_build = time.perf_counter()
     with torch.inference_mode():
-        model, mimi = build_models(geom, device, seed, mimi_dtype=mdt)
         E = _engine(model, mimi, device, seats, capacity, depth_dtype)
-        voice = types.SimpleNamespace(ts=0, kv=None, builder=None,
-                                      mem=model.depth.spk_memory(torch.zeros(1, 1, 192, device=device), "ecapa",
-                                                                 null_mask=torch.tensor([True], device=device)),
-                                      rmask=torch.ones(1, 1, dtype=torch.bool, device=device))
+        voice = _voice(model, device)
     delivered = [0]
 
     def on_event(kind, payload):
@@ -275,11 +289,66 @@ def gpu_arm(device, wl, seats=256, capacity=2048, steps=50, warmup=10, seed=0, g
            "steps": steps, "warmup": warmup, "frames": int(frames),
            "admitted": E.stats["admitted"] - admitted0,
            "eager_fallback_prefills": E.stats["fallback_prefill"] - fb0,
-           "graphs_captured_in_window": n_graphs() - g0, "build_and_capture_s": round(build_s, 1),
-           "dtypes": {"backbone": "bf16", "depth": depth_dtype, "mimi": mimi_dtype},
-           "measured": "wall clock around the reference's own Engine._tick (one D2H + sync per tick), "
-                       "same seat mix and steady-state start as the native arm"}
-    del E, model, mimi
+           "graphs_captured_in_window": n_graphs() - g0, "build_and_capture_s": round(build_s, 1)}
+    del E
+    torch.cuda.empty_cache()
+    return out
+
+
+def _ttfa_run(model, mimi, device, vocab, n_req, warm, prompt_len=300, capacity=1024):
+    """configs[1] through a one-seat reference engine: a request of `prompt_len` uniform-random token ids (generator
+    seed = request index), temperature 0.8 / top-k 50 for cb0 and depth; TTFA = submit -> the reference's first
+    'audio' event (maya3/bench/bench_engine.py:49-69 measures to the same callback), host clock, warm engine."""
+    import torch
+    from maya3 import engine as ME
+    with torch.inference_mode():
+        E = _engine(model, mimi, device, 1, capacity, "bf16", temp=0.8, top_k=50, cb0_temp=0.8, cb0_top_k=50)
+        voice = _voice(model, device)
+    out = []
+    for i in range(warm + n_req):
+        first = []
+        r = ME.Request(["-"], "en", voice, lambda k, p: first.append(time.perf_counter()) if k == "audio" else None)
+        r.ids, r.target = np.random.default_rng(i).integers(0, vocab, prompt_len), 2
+        t0 = time.perf_counter()
+        E._pending.append(r)
+        for _ in range(8):
+            E._tick()
+            if r.done:
+                break
+        if not first:
+            raise RuntimeError("reference TTFA request produced no audio")
+        if i >= warm:
+            out.append((first[0] - t0) * 1e3)
+    del E
+    torch.cuda.empty_cache()
+    return {"p50_ms": round(float(np.percentile(out, 50)), 3), "p99_ms": round(float(np.percentile(out, 99)), 3),
+            "n": n_req, "workload": f"configs[1]: B=1, capacity {capacity}, {prompt_len}-token prompts, temp 0.8 / "
+                                    "top-k 50, bf16"}
+
+
+def gpu_arm(device, wl, seats=256, capacity=2048, steps=50, warmup=10, seed=0, geom=None, ttfa_requests=50):
+    """The reference's own engine on one GPU: configs[2] (bench.py's Workload `wl`: the same request stream and
+    steady-state start as the native arm) at bf16 throughout and at the engine's default dtypes (depth fp16, Mimi
+    fp32: maya3/engine.py:53,165), and configs[1]'s B=1 TTFA.  Returns the measurements as a dict."""
+    import copy
+
+    import torch
+    from maya2_native_b200.config import BASELINE
+    geom = geom or BASELINE
+    _use_reference()
+    with torch.inference_mode():
+        model, mimi32 = build_models(geom, device, seed, mimi_dtype=torch.float32)
+        mimi16 = copy.deepcopy(mimi32).to(torch.bfloat16)
+    out = _tick_run(model, mimi16, device, wl, seats, capacity, steps, warmup, "bf16")
+    out["dtypes"] = {"backbone": "bf16", "depth": "bf16", "mimi": "bf16"}
+    out["measured"] = ("wall clock around the reference's own Engine._tick (one D2H + sync per tick), same seat mix "
+                       "and steady-state start as the native arm")
+    d = _tick_run(model, mimi32, device, wl, seats, capacity, steps, warmup, "fp16")
+    d["dtypes"] = {"backbone": "bf16", "depth": "fp16", "mimi": "fp32"}
+    out["engine_defaults"] = d
+    if ttfa_requests:
+        out["ttfa"] = _ttfa_run(model, mimi16, device, geom.backbone.vocab, ttfa_requests, 8)
+    del model, mimi16, mimi32
     torch.cuda.empty_cache()
     return out
 

@@ -696,9 +696,10 @@ def reference_cpu_line(a):
     raise RuntimeError(f"reference CPU sample failed (rc {r.returncode}): {r.stderr[-400:]}")
 
 
-def run_reference_gpu(a, dev, native_e2e, native_value):
-    """The reference's own serving engine (Triton + CUDA graphs, baseline/_ref) on this GPU at configs[2]: same seat
-    mix, steady-state start, W untimed and K timed ticks; reported beside the native arm's numbers."""
+def run_reference_gpu(a, dev, line):
+    """The reference's own serving engine (Triton + CUDA graphs, baseline/_ref) on this GPU at configs[2] -- same seat
+    mix, steady-state start, W untimed and K timed ticks -- at bf16 and at its default dtypes, plus its configs[1]
+    TTFA; reported beside the native arm's numbers."""
     from baseline import reference_arm as RA
     from maya2_native_b200.config import BASELINE
     why = RA.unavailable()
@@ -706,8 +707,10 @@ def run_reference_gpu(a, dev, native_e2e, native_value):
         return {"unavailable": why}
     wl = Workload(BASELINE.backbone.vocab, a.seed * 7919)
     out = RA.gpu_arm(dev, wl, a.seats, a.capacity, steps=a.steps, warmup=a.warmup, seed=a.seed)
-    out["native_e2e_over_reference"] = round(native_e2e / out["value"], 3)
-    out["native_value_over_reference"] = round(native_value / out["value"], 3)
+    out["native_e2e_over_reference"] = round(line["e2e"]["value"] / out["value"], 3)
+    out["native_value_over_reference"] = round(line["value"] / out["value"], 3)
+    if "ttfa" in line and "ttfa" in out:
+        out["ttfa"]["reference_p50_over_native"] = round(out["ttfa"]["p50_ms"] / line["ttfa"]["p50_ms"], 3)
     return out
 
 
@@ -733,8 +736,7 @@ def main():
         line = run_native(a, rank, world, local)
     if rank == 0 and world == 1 and not a.no_extra and not a.no_reference_gpu:
         try:
-            line["reference_gpu"] = run_reference_gpu(a, torch.device("cuda", local), line["e2e"]["value"],
-                                                      line["value"])
+            line["reference_gpu"] = run_reference_gpu(a, torch.device("cuda", local), line)
         except Exception as exc:                      # reported, not fatal: the native line still stands
             line["reference_gpu"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
