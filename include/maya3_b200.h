@@ -64,17 +64,11 @@ M3_API int m3_selftest_timeout(int32_t polls, int32_t* status);
 /* ---------------------------------------------------------------------------------------------- utilities */
 /* Y[M,N] = X[M,K] . W[N,K]^T, bf16 inputs, fp32 accumulation, Y bf16 (y_f32 = 0) or fp32 (y_f32 = 1).
  * Row-major with leading dimensions ldx, ldw, ldy (elements).  Replaces F.linear on the serving path
- * (serve/fast_backbone.py:193,200-202; serve/fast_depth.py:150,167,185-191; serve/fast_codec.py:140,168-181). */
+ * (serve/fast_backbone.py:193,200-202; serve/fast_depth.py:150,167,185-191; serve/fast_codec.py:140,168-181).
+ * m <= 8 runs this library's GEMV kernel; larger m runs cuBLAS (cublasGemmEx, fp32 compute), as the reference's
+ * F.linear does. */
 M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
                  int32_t n, int32_t k, int32_t y_f32, m3_stream stream);
-
-/* m3_gemm_bf16 on a chosen implementation: 0 = automatic (what every stage uses), 1 = the GEMV kernel (m <= 8),
- * 2 = cuBLAS, 3 = this library's tcgen05 tensor-core kernel (persistent, warp-specialised), 4 = the same with the
- * feed-forward activation fused: y = bf16(GELU_erf(bf16(x w^T))) (bf16 output only), 5 = the cluster split-K
- * tcgen05 kernel for m <= 256 (bf16 output only; K-slices summed through distributed shared memory).  For tests and
- * measurement. */
-M3_API int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
-                             int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream);
 
 /* In place f = bf16(GELU_erf(f)) over n8 groups of 8 bf16 values: the depth and Mimi feed-forward activation
  * (F.gelu on bf16 tensors) as the stages apply it.  For tests. */

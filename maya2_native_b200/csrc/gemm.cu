@@ -1,7 +1,10 @@
 // Linear layers: Y[M,N] = X[M,K] . W[N,K]^T with bf16 operands and fp32 accumulation.
 //
 // Small M (a handful of seats) is weight-bandwidth bound: a GEMV kernel streams each weight row once with 16-byte
-// loads and keeps the few activation rows in shared memory.  Larger M goes to cuBLAS (a plain library GEMM).
+// loads and keeps the few activation rows in shared memory.  Larger M goes to cuBLAS (a plain library GEMM): three
+// tcgen05 designs of this library's own were built and measured slower than it on the tick's shapes (a persistent
+// warp-specialised kernel, a cluster split-K kernel for M <= 256, and a swap-AB kernel with 128 weight rows per MMA
+// tile and fused norm / RoPE / SwiGLU epilogues), so the choice is a fixed function of M alone.
 #include <cublas_v2.h>
 
 #include <mutex>
@@ -188,29 +191,3 @@ int gemv_only(const GemmDesc& g, cudaStream_t s) {
 }
 }  // namespace m3
 
-namespace m3 {
-int gemm_impl(const GemmDesc& g, int impl, cudaStream_t s) {
-  switch (impl) {
-    case kGemmGemv: return gemv_only(g, s);
-    case kGemmCublas: return g.M == 0 ? M3_OK : launch_cublas(g, s);
-    case kGemmUmma:
-    case kGemmUmmaGelu: {
-      if (g.M == 0) return M3_OK;
-      M3_REQUIRE(impl == kGemmUmma || !g.y_f32, M3_ERR_ARG, "the GELU epilogue writes bf16");
-      // widest tile that still gives most SMs a tile: fewer re-reads of A and B through L2
-      const int tiles256 = cdiv(g.M, 128) * cdiv(g.N, 256), tiles128 = cdiv(g.M, 128) * cdiv(g.N, 128);
-      const int bn = (tiles256 >= 120 && g.N % 256 == 0) ? 256 : (tiles128 >= 148 ? 128 : 64);
-      return umma_gemm_persistent(g, bn, impl == kGemmUmmaGelu ? 2 : (g.y_f32 ? 1 : 0), s);
-    }
-    case kGemmUmmaSmall: return g.M == 0 ? M3_OK : umma_gemm_small(g, s);
-    default: return gemm(g, s);
-  }
-}
-}  // namespace m3
-
-extern "C" int m3_gemm_bf16_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
-                                 int32_t m, int32_t n, int32_t k, int32_t y_f32, int32_t impl, m3_stream stream) {
-  m3::GemmDesc g{reinterpret_cast<const m3::bf16*>(x), ldx, reinterpret_cast<const m3::bf16*>(w), ldw, y, ldy,
-                 m, n, k, y_f32 != 0};
-  return m3::gemm_impl(g, impl, reinterpret_cast<cudaStream_t>(stream));
-}

@@ -116,143 +116,10 @@ __global__ void mimi_rope_kernel(const bf16* __restrict__ qkv, const int64_t* __
 }
 
 // Sliding-window attention of the frame's T queries over the slot's ring: key r is visible to the query at
-// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).  One CTA per (row, head): the
-// head's K and V rings (ring x hd bf16 each, contiguous) arrive by two bulk copies on separate mbarriers, so the
-// scores start as soon as K has landed while V is still in flight.  hd/8 lanes share a ring entry (16 bytes each;
-// a quarter-warp reads whole 128-byte rows, conflict-free); fp32 scores, softmax statistics by one warp per query,
-// weighted sum of V reduced over lanes and warps.  Every wait is bounded.
-constexpr int kRingThreads = 256;
+// position p iff p - window < key_pos[r] <= p (serve/fast_codec.py:158-160,178).
 constexpr float kLazyRescale2 = 8.f;  // raise the running max only when a score exceeds it by 2^8
-constexpr int kRingWarps = kRingThreads / 32;
 
-inline size_t ring_attn_smem(int T, int ring, int hd) {
-  return 128 + 2 * (size_t)ring * hd * 2 + (size_t)ring * 8 +
-         ((size_t)T * ring + (size_t)kRingWarps * T * hd + 2 * T) * 4;
-}
-
-template <int T>
-__global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ kring, const bf16* __restrict__ vring,
-    const int64_t* __restrict__ key_pos, const int64_t* __restrict__ pos, const int* __restrict__ slot32, int heads,
-    int hd, int ring, int window, int64_t slot_stride, float scale, bf16* __restrict__ out, int* status) {
-  extern __shared__ __align__(128) unsigned char rsm[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(rsm);
-  const uint32_t ring_bytes = (uint32_t)ring * hd * 2;
-  bf16* Ks = reinterpret_cast<bf16*>(rsm + 128);
-  bf16* Vs = reinterpret_cast<bf16*>(rsm + 128 + ring_bytes);
-  int64_t* kps = reinterpret_cast<int64_t*>(rsm + 128 + 2 * ring_bytes);  // [ring] key positions
-  float* sc = reinterpret_cast<float*>(kps + ring);                        // [T][ring]
-  float* wred = sc + T * ring;                                              // [warps][T][hd]
-  float* stat = wred + kRingWarps * T * hd;                                 // [T] (max, 1 / sum)
-  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int H = heads * hd;
-  const int s = slot32[b];
-  if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const int64_t off = (int64_t)s * slot_stride + (int64_t)h * ring * hd;
-    mbar_expect_tx(&bar[0], ring_bytes);
-    bulk_g2s(Ks, kring + off, ring_bytes, &bar[0]);
-    mbar_expect_tx(&bar[1], ring_bytes);
-    bulk_g2s(Vs, vring + off, ring_bytes, &bar[1]);
-  }
-  for (int r = tid; r < ring; r += kRingThreads) kps[r] = key_pos[(int64_t)s * ring + r];
-  const int LPR = hd / 8, RPW = 32 / LPR;  // lanes per ring entry, entries per warp step
-  const int c8 = lane % LPR, rsub = lane / LPR;
-  float qr[T][8];
-  int64_t pq[T];
-#pragma unroll
-  for (int t = 0; t < T; ++t) {
-    unpack8(reinterpret_cast<const uint4*>(q + ((int64_t)b * T + t) * H + h * hd)[c8], qr[t]);
-    pq[t] = pos[(int64_t)b * T + t];
-  }
-  const bool kok = mbar_wait(&bar[0], 0, status);
-  if (__syncthreads_or(!kok)) {  // give up: let the V copy land (bounded) before the CTA exits
-    if (tid == 0) mbar_wait(&bar[1], 0, nullptr);
-    __syncthreads();
-    return;
-  }
-  for (int r0 = warp * RPW; r0 < ring; r0 += kRingWarps * RPW) {
-    const int r = r0 + rsub;
-    float kf[8];
-    unpack8(reinterpret_cast<const uint4*>(Ks + r * hd)[c8], kf);
-    float acc[T];
-#pragma unroll
-    for (int t = 0; t < T; ++t) {
-      acc[t] = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[t] = fmaf(qr[t][e], kf[e], acc[t]);
-    }
-    for (int o = LPR / 2; o > 0; o >>= 1)
-#pragma unroll
-      for (int t = 0; t < T; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-    if (c8 == 0) {
-      const int64_t kp = kps[r];
-#pragma unroll
-      for (int t = 0; t < T; ++t) sc[t * ring + r] = (kp <= pq[t] && kp > pq[t] - window) ? acc[t] * scale : -INFINITY;
-    }
-  }
-  __syncthreads();
-  if (warp < T) {
-    float mx = -INFINITY;
-    for (int r = lane; r < ring; r += 32) mx = fmaxf(mx, sc[warp * ring + r]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    for (int r = lane; r < ring; r += 32) {
-      const float v = sc[warp * ring + r];
-      sum += v == -INFINITY ? 0.f : expf(v - mx);
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) {
-      stat[2 * warp] = mx;
-      stat[2 * warp + 1] = sum > 0.f ? 1.f / sum : 0.f;
-    }
-  }
-  const bool vok = mbar_wait(&bar[1], 0, status);
-  if (__syncthreads_or(!vok)) return;
-  float o[T][8];
-#pragma unroll
-  for (int t = 0; t < T; ++t)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[t][e] = 0.f;
-  for (int r0 = warp * RPW; r0 < ring; r0 += kRingWarps * RPW) {
-    const int r = r0 + rsub;
-    float vf[8];
-    unpack8(reinterpret_cast<const uint4*>(Vs + r * hd)[c8], vf);
-#pragma unroll
-    for (int t = 0; t < T; ++t) {
-      const float v = sc[t * ring + r];
-      const float pr = v == -INFINITY ? 0.f : expf(v - stat[2 * t]) * stat[2 * t + 1];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[t][e] = fmaf(pr, vf[e], o[t][e]);
-    }
-  }
-  for (int off = LPR; off < 32; off <<= 1)
-#pragma unroll
-    for (int t = 0; t < T; ++t)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[t][e] += __shfl_xor_sync(0xffffffffu, o[t][e], off);
-  if (rsub == 0)
-#pragma unroll
-    for (int t = 0; t < T; ++t)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) wred[(warp * T + t) * hd + c8 * 8 + e] = o[t][e];
-  __syncthreads();
-  for (int i = tid; i < T * hd; i += kRingThreads) {
-    const int t = i / hd, d = i % hd;
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < kRingWarps; ++w) v += wred[(w * T + t) * hd + d];
-    out[((int64_t)b * T + t) * H + h * hd + d] = to_bf(v);
-  }
-}
-
-// Tensor-core form of the ring attention for head dims 32 and 64 (the decode attention's design, without splits):
+// On the tensor cores for head dims 32 and 64 (the decode attention's design, without splits):
 // one CTA of 4 warps per (row, head); the ring is cut into 16-entry blocks, warp w takes blocks w, w+4, ... through
 // its own 2-deep TMA ring (tensor maps over kv[layer][k|v] as [slot * heads + head][entry][head_dim]); S = Q K^T with
 // the T queries as mma rows, the key_pos window as the mask, online softmax in exp2, O^T += V^T P^T with P split into
@@ -696,7 +563,6 @@ struct m3_mimi {
   int64_t snap_row = 0;
   void* fws = nullptr;  // repacked transposed-conv weights + the state snapshot
   bf16* snap = nullptr;
-  bool ring_mma = false;                // tensor-core ring attention (head dim 32 or 64, ring a multiple of 16)
   int64_t* pos = nullptr;
   bf16 *a_sem = nullptr, *a_ac = nullptr, *p_sem = nullptr, *p_ac = nullptr, *h = nullptr, *y = nullptr,
        *qkv = nullptr, *q = nullptr, *att = nullptr, *ob = nullptr, *ff = nullptr, *act0 = nullptr, *act1 = nullptr,
@@ -884,9 +750,11 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   const int hd = c.hidden / c.heads;
   M3_REQUIRE(c.hidden % c.heads == 0 && hd % 8 == 0 && hd <= 128 && c.heads <= 32, M3_ERR_UNSUPPORTED, "head dim");
   M3_REQUIRE(c.ring >= c.window + c.upsample_stride, M3_ERR_ARG, "ring %d", c.ring);
-  M3_REQUIRE((hd & (hd - 1)) == 0 && c.ring % (256 / hd) == 0 &&
-                 ring_attn_smem(c.upsample_stride, c.ring, hd) <= 227 * 1024,
-             M3_ERR_UNSUPPORTED, "ring %d x head dim %d unsupported by the ring attention", c.ring, hd);
+  M3_REQUIRE((hd == 32 || hd == 64) && c.ring % kRingBlk == 0 &&
+                 (c.upsample_stride == 1 || c.upsample_stride == 2 || c.upsample_stride == 4),
+             M3_ERR_UNSUPPORTED,
+             "ring attention: head dim %d (32 or 64), ring %d (a multiple of %d), %d tokens per frame (1, 2 or 4)", hd,
+             c.ring, kRingBlk, c.upsample_stride);
   M3_REQUIRE(c.upsample_stride <= 4 && c.upsample_stride <= 8 && c.kernel - 1 <= 8 && c.res_kernel - 1 <= 8 &&
                  c.last_kernel - 1 <= 8,
              M3_ERR_UNSUPPORTED, "kernel sizes");
@@ -972,8 +840,7 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   m->tmp = carve<bf16>(p, act);
   m->z = carve<float>(p, zf);
   cudaMemset(m->status, 0, 256);
-  m->ring_mma = (hd == 32 || hd == 64) && c.ring % kRingBlk == 0 && c.upsample_stride <= 8;
-  if (m->ring_mma) {
+  {
     EncodeTiled enc;
     if (tensor_map_encoder(&enc) != M3_OK) {
       cudaFree(m->ws);
@@ -1008,13 +875,6 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
     cudaFuncSetAttribute(ring_mma_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
     cudaFuncSetAttribute(ring_mma_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
     cudaFuncSetAttribute(ring_mma_kernel<64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, rs);
-  }
-  {
-    const int sm = (int)ring_attn_smem(c.upsample_stride, c.ring, hd);
-    cudaFuncSetAttribute(ring_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    cudaFuncSetAttribute(ring_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    cudaFuncSetAttribute(ring_attn_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   }
   if (const int rc = setup_fused_seanet(m); rc != M3_OK) {
     m3_mimi_destroy(m);
@@ -1123,7 +983,7 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
                                                    m->q, kr, kr + kv_half, slot_stride);
     M3_LAUNCHED();
-    if (m->ring_mma && (T == 1 || T == 2 || T == 4)) {
+    {
       const dim3 grid(R, c.heads);
       const float qs = 1.4426950408889634f / sqrtf((float)hd);
 #define M3_RING_MMA(HDD, TT)                                                                                      \
@@ -1136,21 +996,6 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
         if (T == 1) M3_RING_MMA(32, 1); else if (T == 2) M3_RING_MMA(32, 2); else M3_RING_MMA(32, 4);
       }
 #undef M3_RING_MMA
-    } else {
-      const dim3 grid(R, c.heads);
-      const size_t sm = ring_attn_smem(T, c.ring, hd);
-      const float sc = 1.f / sqrtf((float)hd);
-#define M3_RING(TT)                                                                                              \
-  ring_attn_kernel<TT><<<grid, kRingThreads, sm, s>>>(m->q, kr, kr + kv_half, m->key_pos, m->pos, m->slot32,    \
-                                                      c.heads, hd, c.ring, c.window, slot_stride, sc, m->att,    \
-                                                      m->status)
-      switch (T) {
-        case 1: M3_RING(1); break;
-        case 2: M3_RING(2); break;
-        case 3: M3_RING(3); break;
-        default: M3_RING(4); break;
-      }
-#undef M3_RING
     }
     M3_LAUNCHED();
     M3_TRY(gemm({m->att, H, m->wo[li], H, m->ob, H, R * T, H, H, false}, s));

@@ -211,13 +211,13 @@ TICK_GEMMS = [("bb.qkv", 256, 4096, 1024), ("bb.o", 256, 1024, 2048), ("bb.gu", 
 
 @torch.inference_mode()
 def gemm(a):
-    """Time each implementation of m3_gemm_bf16 on the tick's linear-layer shapes (bf16 out; CUDA events over graph
-    replays).  --cold cycles through enough weight copies (> 2x L2) that every launch streams its weights from HBM,
-    as the tick's 28 layers do."""
+    """Time m3_gemm_bf16 (GEMV for M <= 8, cuBLAS above) on the tick's linear-layer shapes (bf16 out; CUDA events
+    over graph replays).  --cold cycles through enough weight copies (> 2x L2) that every launch streams its weights
+    from HBM, as the tick's 28 layers do."""
     from maya2_native_b200 import _lib as L
     dev = torch.device("cuda", 0)
     lib = L.load()
-    print(f"{'layer':16s} {'M':>7s} {'N':>5s} {'K':>5s}   cublas us  tcgen05 us  small us   TF/s(best own)")
+    print(f"{'layer':16s} {'M':>7s} {'N':>5s} {'K':>5s}        us     TF/s")
     for name, M, N, K in TICK_GEMMS:
         if a.shape and name != a.shape:
             continue
@@ -226,37 +226,29 @@ def gemm(a):
         ws = [torch.randn(N, K, device=dev).to(torch.bfloat16) for _ in range(min(copies, 64))]
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         reps = 64 if a.cold else 20
-        res = []
-        for impl in (2, 3, 5):
-            if impl == 5 and M > 256:
-                res.append(float("nan"))
-                continue
 
-            def call(i):
-                w = ws[i % len(ws)]
-                L.check(lib.m3_gemm_bf16_impl(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K, 0, impl,
-                                              L.stream_ptr()))
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                for i in range(3):
-                    call(i)
-            torch.cuda.current_stream().wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):      # launches replayed without host overhead, as in the tick graph
-                for i in range(reps):
-                    call(i)
+        def call(i):
+            w = ws[i % len(ws)]
+            L.check(lib.m3_gemm_bf16(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K, 0, L.stream_ptr()))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(3):
+                call(i)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):      # launches replayed without host overhead, as in the tick graph
+            for i in range(reps):
+                call(i)
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
             graph.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(5):
-                graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            res.append(e0.elapsed_time(e1) / (5 * reps) * 1e3)
-        own = min(v for v in res[1:] if v == v)
-        print(f"{name:16s} {M:7d} {N:5d} {K:5d}   {res[0]:9.2f}  {res[1]:10.2f}  {res[2]:8.2f}   "
-              f"{2 * M * N * K / own / 1e6:8.1f}", flush=True)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / (5 * reps) * 1e3
+        print(f"{name:16s} {M:7d} {N:5d} {K:5d}  {us:8.2f} {2 * M * N * K / us / 1e6:8.1f}", flush=True)
 
 
 @torch.inference_mode()
