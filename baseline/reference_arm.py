@@ -154,11 +154,11 @@ def build_depth(geom, device, seed=0, audio_dtype=None):
 
 
 # ------------------------------------------------------------------------------------------------ GPU arm
-def _engine(model, mimi, device, seats, capacity, depth_dtype, **cfg):
-    """A reference ``Engine`` built by its own ``_build_fast`` around the given models (``Engine.__init__`` would load
-    a checkpoint, a tokenizer and a voice registry, none of which the decode path uses).  The fp32 depth stack is kept
-    after FastDepth copies it (``free_reference_depth=False``) so further engines can be built from the same models;
-    it is not read by the tick."""
+def engine(model, mimi, device, seats, capacity, depth_dtype, build=None, **cfg):
+    """A reference ``Engine`` built by its own ``_build_fast`` (or by `build(engine)` in its place) around the given
+    models (``Engine.__init__`` would load a checkpoint, a tokenizer and a voice registry, none of which the decode
+    path uses).  The fp32 depth stack is kept after FastDepth copies it (``free_reference_depth=False``) so further
+    engines can be built from the same models; it is not read by the tick."""
     import torch
     from maya3 import engine as ME
     from maya3 import guards as G
@@ -171,7 +171,10 @@ def _engine(model, mimi, device, seats, capacity, depth_dtype, **cfg):
     E.log = lambda *a, **k: None
     E.model = model
     E.mimi = mimi
-    E._build_fast()
+    if build is None:
+        E._build_fast()
+    else:
+        build(E)
     E._pending = collections.deque()
     E._calls = collections.deque()
     E._cv = threading.Condition()
@@ -194,7 +197,7 @@ def _engine(model, mimi, device, seats, capacity, depth_dtype, **cfg):
     return E
 
 
-def _voice(model, device):
+def voice(model, device):
     """A plain voice (no prefix, null speaker memory): the fields Engine._admit/_bind read."""
     import torch
     return types.SimpleNamespace(ts=0, kv=None, builder=None,
@@ -209,8 +212,8 @@ def _tick_run(model, mimi, device, wl, seats, capacity, steps, warmup, depth_dty
     from maya3 import engine as ME
     t_build = time.perf_counter()
     with torch.inference_mode():
-        E = _engine(model, mimi, device, seats, capacity, depth_dtype)
-        voice = _voice(model, device)
+        E = engine(model, mimi, device, seats, capacity, depth_dtype)
+        vc = voice(model, device)
     delivered = [0]
 
     def on_event(kind, payload):
@@ -218,7 +221,7 @@ def _tick_run(model, mimi, device, wl, seats, capacity, steps, warmup, depth_dty
             delivered[0] += 1
 
     def request(ids, frames):
-        r = ME.Request(["-"], "en", voice, on_event)
+        r = ME.Request(["-"], "en", vc, on_event)
         r.ids, r.target = ids, frames
         return r
 
@@ -302,12 +305,12 @@ def _ttfa_run(model, mimi, device, vocab, n_req, warm, prompt_len=300, capacity=
     import torch
     from maya3 import engine as ME
     with torch.inference_mode():
-        E = _engine(model, mimi, device, 1, capacity, "bf16", temp=0.8, top_k=50, cb0_temp=0.8, cb0_top_k=50)
-        voice = _voice(model, device)
+        E = engine(model, mimi, device, 1, capacity, "bf16", temp=0.8, top_k=50, cb0_temp=0.8, cb0_top_k=50)
+        vc = voice(model, device)
     out = []
     for i in range(warm + n_req):
         first = []
-        r = ME.Request(["-"], "en", voice, lambda k, p: first.append(time.perf_counter()) if k == "audio" else None)
+        r = ME.Request(["-"], "en", vc, lambda k, p: first.append(time.perf_counter()) if k == "audio" else None)
         r.ids, r.target = np.random.default_rng(i).integers(0, vocab, prompt_len), 2
         t0 = time.perf_counter()
         E._pending.append(r)

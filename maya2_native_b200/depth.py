@@ -7,6 +7,7 @@ replayed from a CUDA graph per batch bucket (serve/fast_depth.py:205-227).
 """
 from __future__ import annotations
 
+import sys
 from collections.abc import Mapping
 
 import torch
@@ -31,10 +32,14 @@ class FastDepth:
             raise ValueError("this build serves the depth stack in bf16 only")
         sd = _named(model)
         if geom is None:
+            # the reference keeps the depth head count and the level -> weight-group map as globals of the module
+            # that defines DepthV2 (tts/model/depth_v2.py:45-47), which its own FastDepth imports
             d = model.depth
-            geom = DepthGeom(layers=len(d.groups[0]), d=d.in_proj.out_features, heads=getattr(d, "heads", 8),
+            mod = sys.modules.get(type(d).__module__)
+            gol = tuple(getattr(mod, "GROUP_OF_LEVEL", ())[:d.n_q])
+            geom = DepthGeom(layers=len(d.groups[0]), d=d.in_proj.out_features, heads=int(getattr(mod, "H", 8)),
                              ffn=d.groups[0][0].f1.out_features, n_q=d.n_q, n_codes=d.n_codes,
-                             rank=d.code_up.in_features, d_backbone=d.in_proj.in_features)
+                             rank=d.code_up.in_features, d_backbone=d.in_proj.in_features, group_of_level=gol)
         self.geom = g = geom
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dtype = torch.bfloat16

@@ -235,3 +235,39 @@ def test_voice_prefix_store(cuda):
         sb.save_prefix(3, 5)                                       # slot 3 holds no positions
     torch.cuda.synchronize()
     assert sb.device_status() == 0
+
+
+def test_load_slot_from_an_hf_cache(cuda):
+    """StaticBackbone.load_slot(slot, hf_cache, length) (serve/fast_backbone.py:157-165, the engine's eager-fallback
+    entry, maya3/engine.py:497-507): a prompt prefilled by the HF Qwen3 model itself into a DynamicCache, installed
+    into a slot, then decoded -- against the same prompt prefilled inline by this backbone (step_mixed); the two decode
+    outputs agree to bf16 accuracy, and the slot's length is the prompt's."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    g = TINY.backbone
+    W = WG.backbone_weights(g)
+    cfg = Qwen3Config(hidden_size=g.hidden, num_hidden_layers=g.layers, num_attention_heads=g.heads,
+                      num_key_value_heads=g.kv_heads, head_dim=g.head_dim, intermediate_size=g.ffn,
+                      vocab_size=g.vocab, rms_norm_eps=g.eps, tie_word_embeddings=True,
+                      rope_parameters={"rope_theta": g.rope_theta, "rope_type": "default"})
+    lm = Qwen3ForCausalLM(cfg)
+    lm.load_state_dict({k: v for k, v in W.items() if k != "cb0_head.weight"}, strict=False)
+    lm = lm.to(cuda, torch.bfloat16).eval()
+    n = 23
+    x = (torch.randn(1, n, g.hidden, generator=torch.Generator().manual_seed(3)) * 0.5).to(cuda, torch.bfloat16)
+    with torch.inference_mode():
+        cache = lm.model(inputs_embeds=x, use_cache=True).past_key_values
+        a = StaticBackbone(W, 2, capacity=64, ctx_buckets=(64,), batch_buckets=(1, 32), geom=g, device=cuda)
+        b = StaticBackbone(W, 2, capacity=64, ctx_buckets=(64,), batch_buckets=(1, 32), geom=g, device=cuda)
+        a.load_slot(1, cache, n)
+        assert a.lengths_cpu[1] == n and int(a.lengths[1]) == n
+        b.step_mixed([], None, [(1, x[0])])
+        x1 = torch.randn(1, g.hidden, generator=torch.Generator().manual_seed(4)).to(cuda, torch.bfloat16)
+        ya = a.step([1], x1).float()
+        yb = b.step([1], x1).float()
+    err = float((ya - yb).abs().max() / max(1.0, float(yb.abs().max())))
+    assert err < 2e-2, err
+    assert a.device_status() == 0
+    with pytest.raises(IndexError):
+        a.load_slot(2, cache, n)          # slot max_slots is the padding slot
+    with pytest.raises(ValueError):
+        a.load_slot(0, cache, 65)         # beyond the capacity

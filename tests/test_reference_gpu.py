@@ -62,3 +62,92 @@ def test_depth_greedy_against_reference_noise_floor(cuda):
     assert nat.device_status() == 0
     assert native >= floor - 0.05, (native, floor)
     assert first >= 0.97, first
+
+
+class _DepthSpy:
+    """Wraps an engine's depth object and records the codes of every call (slot lists and codes per tick)."""
+
+    def __init__(self, inner):
+        self.inner, self.log = inner, []
+
+    def __getattr__(self, name):
+        return getattr(self.inner, name)
+
+    def __call__(self, slots, h, cb0):
+        codes, fb = self.inner(slots, h, cb0)
+        self.log.append((list(slots), codes.cpu().numpy().copy()))
+        return codes, fb
+
+
+def _run_engine(E, ME, vc, prompts, frames, ticks=12):
+    """Submit one request per prompt to a reference Engine and tick it; returns per-request event lists and, per
+    slot, the codes of each frame."""
+    events = [[] for _ in prompts]
+    reqs = []
+    E.depth = _DepthSpy(E.depth)
+    for i, ids in enumerate(prompts):
+        r = ME.Request(["-"], "en", vc, lambda k, p, i=i: events[i].append((k, p)))
+        r.ids, r.target = ids, frames
+        E._pending.append(r)
+        reqs.append(r)
+    for _ in range(ticks):
+        E._tick()
+        if all(r.done for r in reqs):
+            break
+    codes = {}
+    for slots, c in E.depth.log:
+        for j, slot in enumerate(slots):
+            codes.setdefault(slot, []).append(c[j])
+    return events, codes
+
+
+def test_native_objects_inside_the_reference_engine(cuda):
+    """The swap of INTEGRATION.md: the reference's own Engine (maya3/engine.py) with Engine._build_fast replaced by
+    maya2_native_b200.integration.build_fast -- the native StaticBackbone, FastDepth, StaticMimi and Cb0Sampler --
+    runs its unmodified _admit / _bind / _tick / _release / _finish_piece: two requests with inline prefill, six
+    frames each, the one readout per tick, the 'audio' and 'end' events.  Beside it the same Engine with the
+    reference's own serve objects on the same weights and seeds, top-1 decoding (deterministic).  A bf16 near-tie
+    can flip a decision between two correct implementations (about 1.5% of decisions on this random-init model), after
+    which that stream follows another trajectory; up to a stream's first differing code the two engines must give the
+    same audio (PCM SNR over 30 dB per frame), and the first frame must agree for at least one of the streams."""
+    import dataclasses
+    RA.use_reference()
+    from maya3 import engine as ME
+
+    from maya2_native_b200.integration import build_fast
+    geom = dataclasses.replace(BASELINE, backbone=dataclasses.replace(BASELINE.backbone, layers=4, vocab=4096))
+    with torch.inference_mode():
+        model, mimi = RA.build_models(geom, cuda)
+    prompts = [np.random.default_rng(i).integers(0, 4096, 40 + 30 * i) for i in range(2)]
+    out = {}
+    for native in (False, True):
+        with torch.inference_mode():
+            E = RA.engine(model, mimi, cuda, 2, 512, "bf16", build=build_fast if native else None, top_k=1,
+                          cb0_top_k=1, cb0_rep=0.0)
+            vc = RA.voice(model, cuda)
+        out[native] = _run_engine(E, ME, vc, prompts, 6)
+        if native:
+            assert E.backbone.device_status() == 0 and E.sampler.device_status() == 0
+        del E
+        torch.cuda.empty_cache()
+    matched, report = 0, []
+    for i in range(2):                      # request i holds slot i in both engines (same free list)
+        ev_ref, ev_nat = out[False][0][i], out[True][0][i]
+        assert [k for k, _ in ev_nat] == [k for k, _ in ev_ref] == ["audio"] * 6 + ["end"]
+        end = ev_nat[-1][1]
+        assert end["reason"] == "cap" and end["frames"] == 6, end
+        c_ref, c_nat = out[False][1][i], out[True][1][i]
+        same = 0
+        while same < 6 and np.array_equal(c_ref[same], c_nat[same]):
+            same += 1
+        for f in range(6):
+            a, b = ev_ref[f][1], ev_nat[f][1]
+            assert a.dtype == np.int16 and b.shape == a.shape == (1920,)
+            a64, b64 = a.astype(np.float64), b.astype(np.float64)
+            snr = 10 * np.log10((a64 ** 2).sum() / max(((a64 - b64) ** 2).sum(), 1e-30))
+            report.append((i, f, f < same, round(float(snr), 1)))
+            if f < same:
+                assert snr > 30, (i, f, snr)
+        matched += same > 0
+    print("native objects inside the reference Engine: (request, frame, codes identical so far, PCM SNR dB):", report)
+    assert matched >= 1, report
