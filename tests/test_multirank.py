@@ -77,7 +77,8 @@ def _box_worker(rank, world, port, out):
 
 def test_box_router_shares_and_summary_gloo():
     """configs[4] across two replicas: the round-robin shares partition the arrival stream, and the box summary sums
-    the frames over replicas, divides by the longest window and takes TTFA percentiles over all arrivals."""
+    the frames over replicas, divides by the longest window and takes TTFA percentiles over all the window's
+    arrivals (those still without audio at its end included, with their wait so far)."""
     world = 2
     port = _free_port()
     with mp.Manager() as m:
@@ -91,7 +92,7 @@ def test_box_router_shares_and_summary_gloo():
         assert res[r][2] == summ
     assert summ["audio_s_per_s"] == pytest.approx(3000 * 0.08 / 7.0, abs=0.05)
     assert summ["offered_audio_s_per_s"] == pytest.approx(0.9 * 2500.0 * 2)
-    assert summ["first_frames"] == 3 and summ["arrivals"] == n and summ["queued_at_end"] == 1
+    assert summ["window_arrivals"] == 3 and summ["arrivals"] == n and summ["without_audio_at_end"] == 1
     assert summ["ttfa_p50_ms"] == pytest.approx(20.0)
     assert summ["mean_busy_seats_per_gpu"] == pytest.approx(229.5)
 
