@@ -357,20 +357,50 @@ def gpu_arm(device, wl, seats=256, capacity=2048, steps=50, warmup=10, seed=0, g
 
 
 # ------------------------------------------------------------------------------------------------ CPU arm
+_CPU_MODELS = {}
+
+
+def _cpu_models(geom, seed):
+    """The reference's model objects on the CPU in fp32, built once per (geometry, seed) in this process."""
+    import torch
+    key = (geom, seed)
+    if key not in _CPU_MODELS:
+        _CPU_MODELS[key] = build_models(geom, torch.device("cpu"), seed)
+    return _CPU_MODELS[key]
+
+
+def _cb0_state(model, seats, top_k=64, rep=0.8):
+    """The engine's per-slot sampler tensors (maya3/engine.py:210-223) for `seats` seats on the CPU."""
+    import torch
+    from maya3 import engine as ME
+    m = seats + 1
+    return types.SimpleNamespace(
+        model=model, cfg=ME.EngineConfig(max_seats=seats, cb0_rep=rep), _any_rep=False, _any_top_p=False,
+        temp_t=torch.full((m,), 0.9), topk_t=torch.full((m,), top_k, dtype=torch.long),
+        topp_t=torch.ones(m), rep_t=torch.full((m,), rep), aeos_bias=torch.zeros(m),
+        seed_t=torch.arange(m, dtype=torch.int32) + 17, ctr_t=torch.zeros(m, dtype=torch.int32),
+        hist_t=torch.full((m, 12), -1, dtype=torch.long), frames_t=torch.zeros(m, dtype=torch.long),
+        min_t=torch.full((m,), NO_STOP, dtype=torch.long), hazard_t=torch.zeros(m))
+
+
+def _cpu_setup():
+    os.environ["TRITON_INTERPRET"] = "1"        # Engine._cb0's row_exponential is a Triton kernel: run it on the host
+    import torch
+    use_reference()
+    torch.set_num_threads(os.cpu_count())
+
+
 def cpu_tick(geom, wl, seats, capacity=2048, ticks=2, warmup=1, seed=0):
     """Seconds of each of `ticks` decode ticks (after `warmup` untimed ones) of `seats` seats through the reference's
     eager CPU path in fp32, and the threads used.  KV lengths follow wl's steady state; caches hold noise."""
-    os.environ["TRITON_INTERPRET"] = "1"        # Engine._cb0's row_exponential is a Triton kernel: run it on the host
+    _cpu_setup()
     import torch
-    _use_reference()
-    torch.set_num_threads(os.cpu_count())
     from maya3 import engine as ME
     from serve.fast_backbone import StaticBackbone
     from serve.fast_codec import StaticMimi
     from serve.fast_depth import FastDepth
-    cpu = torch.device("cpu")
     with torch.inference_mode():
-        model, mimi = build_models(geom, cpu, seed)
+        model, mimi = _cpu_models(geom, seed)
         sb = StaticBackbone(model.backbone, seats, capacity=capacity, ctx_buckets=(capacity,), attention="gather",
                             use_graphs=False)
         fd = FastDepth(model, seats, dtype=torch.float32, batch_buckets=(seats,), seed=seed + 1, fused=False)
@@ -386,14 +416,7 @@ def cpu_tick(geom, wl, seats, capacity=2048, ticks=2, warmup=1, seed=0):
         for s, (P, T, age) in enumerate(lens):
             sb.lengths[s] = P + age
             sb.lengths_cpu[s] = P + age
-        m = seats + 1
-        st = types.SimpleNamespace(                               # the per-slot tensors of maya3/engine.py:210-223
-            model=model, cfg=ME.EngineConfig(max_seats=seats), _any_rep=False, _any_top_p=False,
-            temp_t=torch.full((m,), 0.9), topk_t=torch.full((m,), 64, dtype=torch.long),
-            topp_t=torch.ones(m), rep_t=torch.full((m,), 0.8), aeos_bias=torch.zeros(m),
-            seed_t=torch.arange(m, dtype=torch.int32) + 17, ctr_t=torch.zeros(m, dtype=torch.int32),
-            hist_t=torch.full((m, 12), -1, dtype=torch.long), frames_t=torch.zeros(m, dtype=torch.long),
-            min_t=torch.full((m,), NO_STOP, dtype=torch.long), hazard_t=torch.zeros(m))
+        st = _cb0_state(model, seats)
         slots = torch.arange(seats)
         x = torch.randn(seats, geom.backbone.hidden, generator=gen) * 0.02
         times = []
@@ -406,3 +429,50 @@ def cpu_tick(geom, wl, seats, capacity=2048, ticks=2, warmup=1, seed=0):
             times.append(time.perf_counter() - t0)
             x = fb
     return times[warmup:], torch.get_num_threads()
+
+
+def cpu_config0(geom, frames=50, seats=4, capacity=512, prompt_len=200, seed=0):
+    """configs[0] on the reference's eager CPU path in fp32: B = 4 seats, KV capacity 512, prompts
+    torch.randint(0, vocab, (4, 200)) from generator seed 0 prefilled by the HF model itself into DynamicCaches
+    installed with StaticBackbone.load_slot (the engine's eager fallback, maya3/engine.py:497-507), then `frames`
+    greedy frames (cb0 at top-k 1 without penalty, FastDepth greedy) with each frame's feedback fed back
+    (maya3/engine.py:544-556).  Returns the timings."""
+    _cpu_setup()
+    import torch
+    from maya3 import engine as ME
+    from serve.fast_backbone import StaticBackbone
+    from serve.fast_codec import StaticMimi
+    from serve.fast_depth import FastDepth
+    with torch.inference_mode():
+        model, mimi = _cpu_models(geom, seed)
+        sb = StaticBackbone(model.backbone, seats, capacity=capacity, ctx_buckets=(capacity,), attention="gather",
+                            use_graphs=False)
+        fd = FastDepth(model, seats, dtype=torch.float32, batch_buckets=(seats,), seed=seed + 1, greedy=True,
+                       fused=False)
+        sm = StaticMimi(mimi, seats, batch_buckets=(seats,), ring=geom.mimi.ring)
+        mem = model.depth.spk_memory(torch.zeros(1, 1, 192), "ecapa", null_mask=torch.tensor([True]))
+        for s in range(seats):
+            fd.set_speaker(s, mem, torch.ones(1, 1, dtype=torch.bool))
+        st = _cb0_state(model, seats, top_k=1, rep=0.0)
+        prompts = torch.randint(0, geom.backbone.vocab, (seats, prompt_len), generator=torch.Generator().manual_seed(0))
+        slots = torch.arange(seats)
+        t0 = time.perf_counter()
+        emb = model.backbone.embed_text(prompts)
+        h = torch.empty(seats, geom.backbone.hidden)
+        for s in range(seats):
+            hs, cache = model.backbone(emb[s:s + 1], use_cache=True)
+            sb.load_slot(s, cache, prompt_len)
+            h[s] = hs[0, -1]
+        t1 = time.perf_counter()
+        for f in range(frames):
+            if f:
+                h = sb._forward(slots, fb, torch.ones(seats, dtype=torch.long), capacity)
+            _, cb0 = ME.Engine._cb0(st, h, slots)
+            codes, fb = fd._compute(slots, h, cb0)
+            sm._forward(slots, codes[:, :, None])
+        t2 = time.perf_counter()
+    dec = t2 - t1
+    return {"seats": seats, "frames": frames, "prefill_s": round(t1 - t0, 3), "s_per_frame": round(dec / frames, 4),
+            "audio_s_per_s": round(seats * frames * FRAME_S / dec, 4), "cores": torch.get_num_threads(),
+            "workload": f"configs[0]: B={seats}, capacity {capacity}, {prompt_len}-token prompts (HF eager prefill "
+                        f"-> load_slot), {frames} greedy frames with feedback, fp32, the reference's own eager CPU path"}

@@ -660,6 +660,7 @@ def run_reference(a, rank, world):
         wl = Workload(BASELINE.backbone.vocab, a.seed * 7919)
         times, cores = RA.cpu_tick(BASELINE, wl, seats, a.capacity, ticks=max(1, a.steps), warmup=a.warmup,
                                    seed=a.seed)
+        config0 = RA.cpu_config0(BASELINE, seed=a.seed)
         kind = "reference"
         sample = (f"one decode tick of {seats} seats at the configs[2] KV-length distribution through the "
                   "reference's own eager CPU path (fp32)")
@@ -669,10 +670,12 @@ def run_reference(a, rank, world):
             sec, cores = cpu_tick_sample(seats, a.seed, reps=1)
             times.append(sec)
         kind = "port"
+        config0 = None
         sample = f"one decode tick of {seats} seats at the configs[2] KV-length distribution, fp32 numpy port ({why})"
     sec = float(np.mean(times))
     v = seats * FRAME_S / sec
-    return {"metric": METRIC, "value": round(v, 4), "unit": "audio-s/s", "n_gpus": world, "steps": len(times),
+    extra = {"configs0": config0} if config0 else {}
+    return {**extra, "metric": METRIC, "value": round(v, 4), "unit": "audio-s/s", "n_gpus": world, "steps": len(times),
             "warmup": a.warmup if kind == "reference" else 0, "ms_per_step": round(sec * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
