@@ -12,8 +12,10 @@ KV positions are staggered up to 2011.  Weights are random-init at the benchmark
 Numbers (one JSON line on rank 0):
   value       audio-seconds per second over all GPUs, device-timed: the K ticks' plans are staged in HBM before the
               timed region and replayed back to back (CUDA events on the tick stream, max over ranks);
-  e2e         the same metric through the engine's public tick (TickEngine.tick): per tick the plan is copied
-              host->device and the packed (stop, cb0, PCM) readout device->host, with one sync, wall-clocked;
+  e2e         the same metric through the engine's public loop, wall-clocked: per tick the plan is copied
+              host->device and the packed (stop, cb0, PCM) readout device->host, with one sync.  The headline runs
+              TickEngine.tick_pipelined (tick t+1 launched before tick t is read and delivered); `synchronous` beside
+              it runs TickEngine.tick (one tick at a time, as the reference's Engine._tick);
   roofline    the split-KV decode attention (the dominant kernel) re-timed on the live cache after the run;
   reference_gpu the reference's own serving engine (its Engine._tick over its Triton + CUDA-graph StaticBackbone,
               FastDepth and StaticMimi, installed in baseline/_ref) on the same GPU, same seat mix, wall-clocked;
@@ -274,23 +276,38 @@ def run_native(a, rank, world, local):
     for cb in eng.ctx_buckets[-2:]:
         for rb in (r for r in eng.row_buckets if r >= eng.buckets[-1]):
             eng.graph_for(rb, eng.buckets[-1], cb)
-    for _ in range(a.warmup):
-        eng.tick()
-        top_up(eng, wl)
-    n_graphs = len(eng.graphs)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e2e_frames, d2h = 0, 0
-    t0 = time.perf_counter()
-    for _ in range(a.steps):
-        out = eng.tick()
-        e2e_frames += len(out)
-        d2h += len(out) * (2 + eng.spf // 4) * 8      # the packed readout rows copied back
-        top_up(eng, wl)
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    e2e_graphs = len(eng.graphs) - n_graphs
+    def public_run(pipelined):
+        """K ticks through the public loop, wall-clocked: tick() (plan, launch, read back, deliver, one tick at a
+        time) or tick_pipelined() (tick t+1 launched before tick t is read; the pipeline starts empty and the last
+        tick is flushed inside the window, so the window holds exactly K launched and delivered ticks)."""
+        step = eng.tick_pipelined if pipelined else eng.tick
+        for _ in range(a.warmup):
+            step()
+            top_up(eng, wl)
+        if pipelined:
+            eng.flush()
+        n_graphs = len(eng.graphs)
+        adm0, rows0 = eng.stats["admitted"], eng.stats["prefill_rows"]
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        frames_out = 0
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            out = step()
+            frames_out += len(out)
+            top_up(eng, wl)
+        if pipelined:
+            frames_out += len(eng.flush())
+        torch.cuda.synchronize()
+        mix = {"admitted": eng.stats["admitted"] - adm0, "prefill_rows": eng.stats["prefill_rows"] - rows0,
+               "graphs_captured_in_window": len(eng.graphs) - n_graphs}
+        return time.perf_counter() - t0, frames_out, mix
+
+    row_bytes = (2 + eng.spf // 4) * 8                    # one packed readout row copied back per frame
+    sync_s, sync_frames, sync_mix = public_run(False)
+    e2e_s, e2e_frames, e2e_mix = public_run(True)
+    d2h = e2e_frames * row_bytes
     h2d = int(np.mean([len(tp.plan) * 8 for tp in plans]))   # the tick plan (slots, offsets, prompt token ids)
 
     # ---- roofline of the decode attention on the live cache (the last tick's rows)
@@ -317,8 +334,10 @@ def run_native(a, rank, world, local):
     # ---- reduce over ranks
     clocks = clk.summary()
     dev_ms, e2e_ms, frames, e2e_frames = reduce_over_ranks(dev_ms, e2e_s * 1e3, frames, e2e_frames, world, dev)
+    _, sync_ms, _, sync_frames = reduce_over_ranks(0.0, sync_s * 1e3, 0, sync_frames, world, dev)
     value = frames * FRAME_S / (dev_ms / 1e3)
     e2e = e2e_frames * FRAME_S / (e2e_ms / 1e3)
+    e2e_sync = sync_frames * FRAME_S / (sync_ms / 1e3)
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
@@ -338,7 +357,12 @@ def run_native(a, rank, world, local):
                    "(8 codebooks), Mimi 8 codebooks", "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (KV cache ~60 GB per replica)"},
         "e2e": {"value": round(e2e, 2), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": int(d2h / max(a.steps, 1)), "graphs_captured_in_window": e2e_graphs},
+                "d2h_bytes_per_step": int(d2h / max(a.steps, 1)), **e2e_mix,
+                "loop": "TickEngine.tick_pipelined (tick t+1 launched before tick t is read)",
+                "synchronous": {"value": round(e2e_sync, 2), "loop": "TickEngine.tick (one tick at a time, as the "
+                                "reference's Engine._tick)", **sync_mix},
+                "note": "each loop runs its own K ticks of the live workload after the device-timed ones; admissions "
+                        "(inline prefill rows) make a tick slower, so the windows differ by their mix"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": int(attn_bytes * ATTN_TRAFFIC_RATIO),
                      "traffic_source": "ncu DRAM bytes of the same kernel at 256 seats x 1 layer, scaled by keys",
@@ -349,6 +373,8 @@ def run_native(a, rank, world, local):
         "tick_ms_p50": round(float(np.percentile(tick_ms, 50)), 4),
         "tick_ms_p99": round(float(np.percentile(tick_ms, 99)), 4),
         "frames_timed": int(frames), "device_status": status,
+        "value_window": {"admitted": int(sum(len(tp.new) for tp in plans)),
+                         "prefill_rows": int(sum(len(s.inline) for tp in plans for s in tp.new))},
         "clocks": clocks,
         "gpu_launches": int(launches),
     }

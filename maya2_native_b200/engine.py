@@ -212,8 +212,13 @@ class TickEngine:
         self._ids = itertools.count()
         self.graphs = {}
         self.pool = None
-        self._host = torch.empty(self.buckets[-1], 2 + self.spf // 4, dtype=torch.int64).pin_memory()
-        self._evt = torch.cuda.Event()
+        # two pinned readout buffers, used in turn: a tick's PCM views stay valid while the next tick is in flight
+        self._hosts = [torch.empty(self.buckets[-1], 2 + self.spf // 4, dtype=torch.int64).pin_memory()
+                       for _ in range(2)]
+        self._flip = 0
+        self._inflight = None       # (plan, host rows, event) of the pipelined tick not yet delivered
+        self._early = set()         # ids of seats whose slots were released before their last tick was read
+        self._readout = None
         self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0,
                       "eager_prefill_rows": 0}
 
@@ -412,15 +417,10 @@ class TickEngine:
             self._launch(g, rb, sb, cb)
 
     # ---------------------------------------------------------------- tick
-    @torch.inference_mode()
-    def tick(self):
-        """One engine tick through the public path: admit, copy the plan host->device, replay, read the packed
-        (stop code, cb0, PCM) rows back with one device->host copy and one sync (maya3/engine.py:557-563).
-        Returns [(seat, stop code, cb0, int16 PCM or None)] for the seats that ran."""
-        new = self._admit()
-        dec = list(self.active)
-        if not dec and not new:
-            return []
+    def _launch_tick(self, dec, new):
+        """Plan one tick, copy its plan host->device, replay its graph and queue the device->host copy of its packed
+        readout into the next pinned buffer; the host mirror of the KV lengths moves at once.  Returns the tick's
+        (plan, host rows, event recorded after the readout copy)."""
         tp = self.make_plan(dec, new)
         g = self.graph_for(tp.rows, tp.seats, tp.ctx)
         if g.evt is not None:
@@ -431,12 +431,88 @@ class TickEngine:
         g.evt.record()
         self.replay(g, tp.rows, tp.seats, tp.ctx)
         B = len(dec) + len(new)
-        host = self._host[:B]
+        host = self._hosts[self._flip][:B]
+        self._flip ^= 1
         host.copy_(g.packed[:B], non_blocking=True)
-        self._evt.record()
-        self._evt.synchronize()
+        evt = torch.cuda.Event()
+        evt.record()
         self.commit(tp)
-        return self._deliver(tp.dec + tp.new, host.numpy())
+        return tp, host, evt
+
+    @torch.inference_mode()
+    def tick(self):
+        """One engine tick through the public path: admit, copy the plan host->device, replay, read the packed
+        (stop code, cb0, PCM) rows back with one device->host copy and one sync (maya3/engine.py:557-563).
+        Returns [(seat, stop code, cb0, int16 PCM or None)] for the seats that ran; the PCM views stay valid until
+        the second tick after this one."""
+        if self._inflight is not None:
+            raise RuntimeError("a pipelined tick is in flight: flush() it before a synchronous tick")
+        new = self._admit()
+        dec = list(self.active)
+        if not dec and not new:
+            return []
+        tp, host, evt = self._launch_tick(dec, new)
+        evt.synchronize()
+        self._readout = host.numpy()
+        return self._deliver(tp.dec + tp.new, self._readout)
+
+    @torch.inference_mode()
+    def tick_pipelined(self):
+        """The engine loop two ticks deep: launch tick t+1, then read back and deliver tick t, so the host's planning
+        and delivery overlap the device's work instead of standing between ticks (the reference's loop,
+        maya3/engine.py:514-630, waits on each tick's readout before planning the next).
+
+        Tick t+1 carries every seat of tick t except those tick t is known to finish (its frame exhausts their
+        budget); their slots are released before the plan, so admissions refill them in tick t+1 as the synchronous
+        loop does.  A seat that tick t's stop code or guard verdict finishes has also run in tick t+1: that frame is
+        dropped, and its slot takes admissions from tick t+2 on.  Per seat the frames delivered are the ones
+        tick() delivers, one call later.  Returns tick t's [(seat, stop code, cb0, int16 PCM or None)] (empty on the
+        first call); flush() delivers the tick still in flight."""
+        prev, self._inflight = self._inflight, None
+        if prev is not None:
+            carried = []
+            for s in prev[0].dec + prev[0].new:
+                if s.stop is not None:
+                    continue                    # finished by an earlier readout: ran speculatively in tick t
+                if s.frames + 1 >= s.max_frames:
+                    self._release(s)            # every outcome of tick t finishes it; stream order keeps the
+                    self._early.add(id(s))      # slot's reset for a new seat behind tick t
+                else:
+                    carried.append(s)
+            self.active = carried
+        new = self._admit()
+        if self.active or new:
+            self._inflight = self._launch_tick(list(self.active), new)
+        out = self._deliver_inflight(prev) if prev is not None else []
+        if self._inflight is not None:
+            tp = self._inflight[0]
+            self.active = [s for s in tp.dec + tp.new if s.stop is None]
+        return out
+
+    @torch.inference_mode()
+    def flush(self):
+        """Deliver the pipelined tick in flight, if any, without launching another; afterwards tick() may run."""
+        prev, self._inflight = self._inflight, None
+        return self._deliver_inflight(prev) if prev is not None else []
+
+    def _deliver_inflight(self, rec):
+        """Wait for a launched tick's readout and deliver it to the seats still live (a seat finished by the
+        readout of the tick before ran in this one speculatively; its row is dropped)."""
+        tp, host, evt = rec
+        evt.synchronize()
+        seats = tp.dec + tp.new
+        hv = host.numpy()
+        live = [i for i, s in enumerate(seats) if s.stop is None]
+        if len(live) < len(seats):
+            hv = hv[live]
+            seats = [seats[i] for i in live]
+        self._readout = hv
+        return self._deliver(seats, hv)
+
+    def last_readout(self):
+        """The packed readout rows of the last tick delivered, one per seat it delivered, in its order: int64
+        [stop | guard verdict << 8 | n_boost << 16, cb0, PCM as int16 pairs...] (a view of pinned host memory)."""
+        return self._readout
 
     @torch.inference_mode()
     def last_outputs(self, n):
@@ -524,7 +600,10 @@ class TickEngine:
         if finished:
             gone = {id(s) for s in finished}
             for s in finished:
-                self._release(s)
+                if id(s) in self._early:
+                    self._early.discard(id(s))      # its slot was released when the next tick was planned
+                else:
+                    self._release(s)
                 self.stats["completed"] += 1
             self.active = [s for s in self.active if id(s) not in gone]
         self.stats["ticks"] += 1

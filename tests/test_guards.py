@@ -114,6 +114,7 @@ def test_engine_delivery_decodes_guard_verdicts():
     eng.guards = types.SimpleNamespace(cfg=eng.cfg.guards)
     eng.stats = {"frames": 0, "completed": 0, "ticks": 0}
     eng.active = []
+    eng._early = set()
     released = []
     eng._release = released.append
     seats = [Seat(rid=i, prompt=np.zeros(3, np.int64), max_frames=50, seed=1, slot=i) for i in range(6)]
