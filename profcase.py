@@ -13,7 +13,8 @@ attention: the backbone step over `seats` decode rows at the configs[2] KV-lengt
 tick:      the full engine tick at the benchmark geometry with fewer seats.
 mimi:      StaticMimi.decode at the benchmark geometry over `seats` streams.
 gaps:      per-node cost of a CUDA graph of dependent tiny kernels.
-overlap:   backbone step and Mimi decode timed back to back and concurrently on two streams.
+overlap:   backbone step and Mimi decode (or the depth loop: --with depth) timed back to back and concurrently on
+           two streams.
 guard:     the loop guard (m3_guard_step) over `seats` seats on due frames, alone and as a graph node.
 """
 from __future__ import annotations
@@ -127,19 +128,29 @@ def gaps(a):
 
 @torch.inference_mode()
 def overlap(a):
-    """Could the Mimi decode of one frame hide under the next frame's backbone step?  Graph-captured backbone step
-    (decode rows of `seats` seats, configs[2] KV-length distribution, benchmark width, all layers) and Mimi decode
-    (`seats` streams), timed back to back on one stream and concurrently on two."""
+    """Could another stage hide under the backbone step?  Graph-captured backbone step (decode rows of `seats` seats,
+    configs[2] KV-length distribution, benchmark width, all layers) and, with `--with mimi`, the Mimi decode of
+    `seats` streams or, with `--with depth`, the depth loop of `seats` seats, timed back to back on one stream and
+    concurrently on two."""
     from maya2_native_b200 import weights as WG
     from maya2_native_b200.backbone import StaticBackbone
     from maya2_native_b200.codec import StaticMimi
     from maya2_native_b200.config import BASELINE
+    from maya2_native_b200.depth import FastDepth
     dev = torch.device("cuda", 0)
     g = BASELINE
     W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
     sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats,), ctx_buckets=(2048,), use_graphs=True,
                         geom=g.backbone, device=dev)
-    codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
+    if a.with_ == "depth":
+        fd = FastDepth(W, a.seats, batch_buckets=(a.seats,), geom=g.depth, device=dev)
+        hd = torch.randn(a.seats, g.depth.d_backbone, device=dev, dtype=torch.bfloat16)
+        cb0 = torch.randint(0, 2048, (a.seats,), device=dev)
+        dslots = list(range(a.seats))
+        other = lambda: fd(dslots, hd, cb0)
+    else:
+        codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
+        other = lambda: codec.decode(idx, codes)
     for k, v in zip(sb.k, sb.v):
         k.normal_()
         v.normal_()
@@ -153,7 +164,7 @@ def overlap(a):
     codes = torch.randint(0, 2048, (a.seats, g.mimi.n_q), device=dev)
     idx = torch.arange(a.seats, device=dev)
     sb.step(slots, x)
-    codec.decode(idx, codes)
+    other()
     torch.cuda.synchronize()
     s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
 
@@ -168,7 +179,7 @@ def overlap(a):
             with torch.cuda.stream(s1):
                 sb.step(slots, x)
             with torch.cuda.stream(s2 if concurrent else s1):
-                codec.decode(idx, codes)
+                other()
             cur.wait_stream(s1)
             cur.wait_stream(s2)
         e1.record()
@@ -192,8 +203,8 @@ def overlap(a):
     sb.lengths[:a.seats] -= 10
     for s in range(a.seats):
         sb.lengths_cpu[s] -= 10
-    t_mimi = alone(lambda: codec.decode(idx, codes))
-    print(f"backbone step {t_bb:.3f} ms, mimi decode {t_mimi:.3f} ms, sequential {run(False):.3f} ms, "
+    t_other = alone(other)
+    print(f"seats {a.seats}: backbone step {t_bb:.3f} ms, {a.with_} {t_other:.3f} ms, sequential {run(False):.3f} ms, "
           f"concurrent {run(True):.3f} ms")
 
 
@@ -306,6 +317,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     ap.add_argument("--cold", action="store_true", help="gemm: stream the weights from HBM on every launch")
+    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth"),
+                    help="overlap: the stage run beside the backbone step")
     a = ap.parse_args()
     {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap,
      "guard": guard}[a.case](a)
