@@ -83,6 +83,7 @@ class Seat:
     suspend: tuple = ()                   # inclusive frame windows with no loop action (_Seat.suspend)
     n_boost: int = 0                      # EOS boosts the loop guard applied (_Seat.n_boost)
     voice: Optional[Voice] = None         # prefix KV installed at bind; the prompt follows it
+    sampling: dict = dataclasses.field(default_factory=dict)   # per-request cb0 sampling (check_sampling)
 
 
 @dataclasses.dataclass
@@ -120,6 +121,29 @@ def frame_budget(prompt_len: int, max_frames: int, capacity: int) -> int:
         if max_frames < 8:
             raise ValueError(f"prompt of {prompt_len} tokens leaves no room in KV capacity {capacity}")
     return max_frames
+
+
+SAMPLING_KEYS = ("seed", "temperature", "top_k", "top_p", "repetition_penalty")
+
+
+def check_sampling(sp) -> dict:
+    """A request's cb0 sampling overrides (maya3/engine.py:110-125): only the keys of SAMPLING_KEYS, None values
+    dropped, each inside the reference's range; ValueError otherwise."""
+    if not sp:
+        return {}
+    unknown = set(sp) - set(SAMPLING_KEYS)
+    if unknown:
+        raise ValueError(f"unknown sampling keys {sorted(unknown)}; allowed {sorted(SAMPLING_KEYS)}")
+    out = {k: v for k, v in sp.items() if v is not None}
+    limits = {"temperature": (0.05, 2.0), "top_k": (1, 2049), "repetition_penalty": (0.0, 5.0)}
+    for k, (lo, hi) in limits.items():
+        if k in out and not lo <= float(out[k]) <= hi:
+            raise ValueError(f"{k} must be in [{lo}, {hi}]")
+    if "top_p" in out and not 0.0 < float(out["top_p"]) <= 1.0:
+        raise ValueError("top_p must be in (0, 1]")
+    if "seed" in out and (isinstance(out["seed"], bool) or int(out["seed"]) < 0):
+        raise ValueError("seed must be a non-negative integer")
+    return out
 
 
 def plan_layout(dec, new, lengths, row_buckets, seat_buckets, ctx_buckets, dummy):
@@ -219,6 +243,7 @@ class TickEngine:
         self._inflight = None       # (plan, host rows, event) of the pipelined tick not yet delivered
         self._early = set()         # ids of seats whose slots were released before their last tick was read
         self._readout = None
+        self._custom = set()        # slots whose cb0 sampling values a request overrode
         self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0,
                       "eager_prefill_rows": 0}
 
@@ -251,19 +276,27 @@ class TickEngine:
         return Voice(ids, store, len(ids))
 
     def submit(self, prompt_ids, max_frames, rid=None, seed=None, cap=None, loose_cap=None, suspend=(),
-               voice: Optional[Voice] = None) -> Seat:
+               voice: Optional[Voice] = None, sampling=None) -> Seat:
         """Queue a request: backbone token ids of its prompt and a frame budget (its length when stops=False), clipped
         to the KV capacity as the reference does (a budget below 8 frames rejects the request).  With guards on,
         `cap` is the piece's frame cap from the caller's duration prior and `loose_cap` its prior-free cap
         (maya3/engine.py:405-411, Engine._plan; both default to the budget), `suspend` its loop-guard suspend windows.
-        With a `voice` (prepare_voice), the prompt is what follows the voice prefix."""
+        With a `voice` (prepare_voice), the prompt is what follows the voice prefix.  `sampling` holds the request's
+        cb0 overrides (check_sampling; the depth levels keep the engine's temperature and top-k); its "seed" derives
+        the request's sampler streams as the reference's bind does for a one-piece request (maya3/engine.py:430-433),
+        where `seed` is the stream seed itself."""
         prompt = np.asarray(prompt_ids, np.int64)
         if prompt.ndim != 1 or len(prompt) == 0:
             raise ValueError("prompt must be a non-empty 1-D array of token ids")
+        sp = check_sampling(sampling)
         pre = voice.length if voice is not None else 0
         frames = frame_budget(pre + len(prompt), int(max_frames), self.cfg.capacity)
-        seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
+        if "seed" in sp:
+            seed = (int(sp.pop("seed")) * 1000003) % (2 ** 31 - 1)
+        else:
+            seed = int(seed) if seed is not None else int(self._rng.integers(1, 2 ** 31 - 1))
         s = Seat(rid if rid is not None else next(self._ids), prompt, frames, seed)
+        s.sampling = sp
         s.loose_cap = frames if loose_cap is None else min(int(loose_cap), frames)
         s.cap = min(s.loose_cap if cap is None else int(cap), frames)
         s.suspend = tuple(suspend)
@@ -295,6 +328,18 @@ class TickEngine:
         c.seed_t[slot] = s.seed
         c.ctr_t[slot] = 0
         c.hist_t[slot] = -1
+        if s.sampling or slot in self._custom:     # maya3/engine.py:438-446; default slots keep the create values
+            sp, cfg = s.sampling, self.cfg
+            c.temp_t[slot] = float(sp.get("temperature") or cfg.cb0_temp)
+            c.topk_t[slot] = int(sp.get("top_k") or cfg.cb0_top_k)
+            c.topp_t[slot] = float(sp.get("top_p") or cfg.cb0_top_p)
+            c.rep_t[slot] = float(sp["repetition_penalty"] if sp.get("repetition_penalty") is not None
+                                  else cfg.cb0_rep)
+            if float(sp.get("top_p") or 1.0) < 1.0:
+                c.any_top_p = True
+            if sp.get("repetition_penalty"):
+                c.any_rep = True
+            (self._custom.add if sp else self._custom.discard)(slot)
         self.depth.row_seed[slot] = (s.seed * 69069 + 1) % (2 ** 31 - 1)
         self.depth.row_ctr[slot] = 0
         self.depth.cross_const[slot] = self.voice_const
@@ -309,6 +354,22 @@ class TickEngine:
         """maya3/engine.py:632-635."""
         self.backbone.free(s.slot)
         self.free.append(s.slot)
+
+    def cancel(self, s: Seat) -> bool:
+        """End a request between ticks (Request.cancel, maya3/engine.py:105-106, acted on at the next tick): a
+        waiting request leaves the queue, a decoding one its slot, released at once -- a pipelined tick still in
+        flight that carries it runs on and its frame for it is dropped, and the slot's next bind is stream-ordered
+        behind that tick.  Returns False when the request had already finished."""
+        if s.stop is not None:
+            return False
+        s.stop = "cancelled"
+        if any(p is s for p in self.pending):
+            self.pending = [p for p in self.pending if p is not s]
+        else:
+            self.active = [a for a in self.active if a is not s]
+            self._release(s)
+        self.stats["cancelled"] = self.stats.get("cancelled", 0) + 1
+        return True
 
     def _admit(self, device=True):
         """maya3/engine.py:449-510 without prompt building: pending requests enter free slots while the tick's row
@@ -368,7 +429,7 @@ class TickEngine:
 
     # ---------------------------------------------------------------- graphs
     def graph_for(self, rb, sb, cb) -> _Graph:
-        key = (rb, sb, cb)
+        key = (rb, sb, cb) + self.cb0.flags()   # the penalty / top-p switches are arguments baked into a capture
         g = self.graphs.get(key)
         if g is not None:
             return g
@@ -610,5 +671,5 @@ class TickEngine:
         return out
 
 
-__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "Voice", "FRAME", "FROM_FEEDBACK", "admission_cap", "frame_budget",
-           "plan_layout"]
+__all__ = ["TickEngine", "TickConfig", "TickPlan", "Seat", "Voice", "FRAME", "FROM_FEEDBACK", "SAMPLING_KEYS",
+           "admission_cap", "check_sampling", "frame_budget", "plan_layout"]

@@ -74,3 +74,36 @@ def test_pipelined_loop_delivers_the_synchronous_streams(cuda):
     assert sync[0][-1][0] != 0 and sync[0][-1][2] is None and pipe[0][-1] == sync[0][-1]
     # the pipelined run delivered every frame it counted (the dropped speculative frame is not one of them)
     assert pstats["frames"] == sum(sum(p is not None for _, _, p in v) for v in pipe.values())
+
+
+def stream_of(eng, seat, step):
+    out = []
+    while seat.stop is None:
+        for s, code, cb0, pcm in step():
+            if s is seat:
+                out.append((code, cb0, None if pcm is None else pcm.tobytes()))
+    return out
+
+
+def test_cancel_with_a_tick_in_flight_hands_a_clean_slot_to_the_next_request(cuda):
+    """cancel() of a decoding request while its next tick is in flight (TickEngine.cancel): the slot is released at
+    once and the request admitted into it next decodes exactly as on a fresh engine -- the slot's reset is
+    stream-ordered behind the speculative tick that still wrote to it."""
+    W = {k: v.to(cuda) for k, v in WG.generate(WG.all_shapes(TINY), seed=9).items()}
+    cfg = TickConfig(max_seats=1, capacity=64, max_inline_rows=8, stops=False)
+    rng = np.random.default_rng(2)
+    pa, pb = rng.integers(0, TINY.backbone.vocab, 5), rng.integers(0, TINY.backbone.vocab, 4)
+    ref = TickEngine(TINY, W, cfg, device=cuda)
+    want = stream_of(ref, ref.submit(pb, 8, sampling={"seed": 5}), ref.tick)
+    ref.close()
+    eng = TickEngine(TINY, W, cfg, device=cuda)
+    a = eng.submit(pa, 40, sampling={"seed": 4})
+    for _ in range(4):
+        eng.tick_pipelined()
+    assert eng.cancel(a) and a.stop == "cancelled" and not eng.cancel(a)
+    b = eng.submit(pb, 8, sampling={"seed": 5})
+    got = stream_of(eng, b, eng.tick_pipelined)
+    eng.flush()
+    assert got == want
+    assert eng.stats["cancelled"] == 1 and eng.device_status() == 0
+    eng.close()
