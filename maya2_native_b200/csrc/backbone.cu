@@ -31,10 +31,9 @@ __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_
                                  int sort, int* status) {
   __shared__ uint64_t key[kSortRows];
   __shared__ int slot_of[kSortRows];
-  __shared__ int first_of[kSortRows];
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   int64_t p = 0;
-  int sl = 0, first = 0;  // first: the slot's first position this step writes (its length before the step)
+  int sl = 0;
   if (r < rows) {
     int64_t s = slots[r];
     if (s < 0 || s > max_slots) {
@@ -49,20 +48,18 @@ __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_
     sl = (int)s;
     slot32[r] = sl;
     pos32[r] = (int)p;
-    first = (int)(p - (offsets ? offsets[r] : 0));
   }
   if (!sort) {
-    if (r < rows) visit[r] = make_int4(r, sl, (int)p, first);
+    if (r < rows) visit[r] = make_int4(r, sl, (int)p, 0);
     return;
   }
   // one CTA, n = blockDim.x: keys (position << 32 | 0x7FFFFFFF - row) sorted descending; padding keys are 0
   const int t = threadIdx.x, n = blockDim.x;
   key[t] = t < rows ? ((uint64_t)(uint32_t)p << 32) | (uint32_t)(0x7FFFFFFF - t) : 0ull;
   slot_of[t] = sl;
-  first_of[t] = first;
   __syncthreads();
   if (__syncthreads_and(t + 1 >= rows || key[t] > key[t + 1])) {  // already in order (keys are distinct)
-    if (t < rows) visit[t] = make_int4(t, sl, (int)p, first);
+    if (t < rows) visit[t] = make_int4(t, sl, (int)p, 0);
     return;
   }
   for (int k = 2; k <= n; k <<= 1)
@@ -79,7 +76,7 @@ __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_
     }
   if (t < rows) {
     const int o = 0x7FFFFFFF - (int)(uint32_t)key[t];
-    visit[t] = make_int4(o, slot_of[o], (int)(key[t] >> 32), first_of[o]);
+    visit[t] = make_int4(o, slot_of[o], (int)(key[t] >> 32), 0);
   }
 }
 
@@ -169,7 +166,6 @@ __global__ void qk_rope_cache_kernel(const bf16* __restrict__ qkv, bf16* __restr
                                      const bf16* __restrict__ cos, const bf16* __restrict__ sin,
                                      const bf16* __restrict__ wq, const bf16* __restrict__ wk, float eps, int H,
                                      int KV) {
-  grid_dep_release();  // the attention after this kernel may start streaming the K/V this kernel does not write
   const int row = blockIdx.x;
   const int head = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (head >= H + KV) return;
@@ -321,7 +317,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
   extern __shared__ unsigned char smem_raw[];
   MmaAttnSmem& sm =
       *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int4 vis = visit[blockIdx.z];  // {row, slot, position, first position written this step}
+  const int4 vis = visit[blockIdx.z];  // {row, slot, position}
   const int split = blockIdx.x, kvh = blockIdx.y, row = vis.x;
   const int KV = gridDim.y;
   const int pos = vis.z;
@@ -350,17 +346,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     tma_load_3d(st + 2 * kBoxBytes, &vmap, 0, y, zc, bar);
     tma_load_3d(st + 3 * kBoxBytes, &vmap, 64, y, zc, bar);
   };
-  // Launched as a programmatic dependent of qk_rope_cache_kernel, which writes q and this step's K/V rows: the
-  // blocks that end at or below the slot's first new position hold only keys of earlier steps and are requested
-  // before the wait; q and the other blocks after it.
-  auto before = [&](int i) { return t0 + (warp + 4 * i + 1) * kBlkTok <= vis.w; };
   if (lane == 0)
-    for (int i = 0; i < min(kMmaStages, nmine); ++i)
-      if (before(i)) issue(i);
-  grid_dep_wait();
-  if (lane == 0)
-    for (int i = 0; i < min(kMmaStages, nmine); ++i)
-      if (!before(i)) issue(i);
+    for (int i = 0; i < min(kMmaStages, nmine); ++i) issue(i);
 
   // A fragments of Q (rows = query heads): a0 = Q[g][16ks + 2t, +1], a2 = Q[g][16ks + 8 + 2t, +1]; rows >= G zero
   uint32_t qa[8][2];
@@ -524,7 +511,7 @@ struct m3_backbone {
   void* ws = nullptr;
   int* slot32 = nullptr;
   int* pos32 = nullptr;
-  int4* visit = nullptr;   // [max_rows] the attention's rows in visiting order (longest first): {row, slot, pos, first new pos}
+  int4* visit = nullptr;   // [max_rows] the attention's rows in visiting order (longest first): {row, slot, pos, 0}
   int rows_written = 0;     // rows of slot32/pos32/visit some step has written (bounds the measurement hook)
   int* status = nullptr;
   bf16 *h = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *o = nullptr, *a = nullptr, *gu = nullptr,
@@ -707,29 +694,26 @@ extern "C" int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clea
   return M3_OK;
 }
 
-static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s, bool after_rope) {
+static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s) {
   const m3_backbone_config& c = bb->c;
   const int G = c.heads / c.kv_heads;
   const int chunk = choose_chunk(rows, ctx, c.kv_heads, bb->max_split);
   const int nsplit = cdiv(ctx, chunk);
   const float qscale = (1.f / sqrtf((float)c.head_dim)) * 1.4426950408889634f;
-  // In a step, a programmatic dependent of qk_rope_cache_kernel: it starts streaming the keys of earlier steps
-  // while that kernel runs and waits for it (grid_dep_wait) before reading q and new keys.  The measurement hook
-  // launches it plainly, so back-to-back launches there do not overlap one another.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nsplit, c.kv_heads, rows);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = kMmaAttnSmemBytes;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = after_rope ? 1 : 0;
-  auto kernel = G == 1 ? attn_mma_kernel<1> : G == 2 ? attn_mma_kernel<2> : attn_mma_kernel<4>;
-  M3_CUDA(cudaLaunchKernelEx(&cfg, kernel, bb->kmap[layer], bb->vmap[layer], (const bf16*)bb->q,
-                             (const int4*)bb->visit, bb->part_o, bb->part_ml, bb->tickets, bb->o, nsplit, chunk,
-                             (int)c.heads, qscale, bb->status));
+  dim3 grid(nsplit, c.kv_heads, rows);
+#define M3_ATTN(GG)                                                                                          \
+  attn_mma_kernel<GG><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                         \
+      bb->kmap[layer], bb->vmap[layer], bb->q, bb->visit, bb->part_o, bb->part_ml,    \
+      bb->tickets,                                                                                             \
+      bb->o, nsplit, chunk, c.heads, qscale, bb->status);
+  if (G == 1) {
+    M3_ATTN(1)
+  } else if (G == 2) {
+    M3_ATTN(2)
+  } else {
+    M3_ATTN(4)
+  }
+#undef M3_ATTN
   M3_LAUNCHED();
   return M3_OK;
 }
@@ -761,7 +745,7 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
         (int64_t)c.capacity * c.head_dim, bb->slot32, bb->pos32, bb->cos, bb->sin, bb->q_norm[i], bb->k_norm[i],
         c.eps, c.heads, c.kv_heads);
     M3_LAUNCHED();
-    M3_TRY(attention(bb, i, rows, ctx, s, true));
+    M3_TRY(attention(bb, i, rows, ctx, s));
     M3_TRY(gemm({bb->o, c.heads * c.head_dim, bb->wo[i], c.heads * c.head_dim, bb->a, Hd, rows, Hd,
                  c.heads * c.head_dim, false},
                 s));
@@ -785,7 +769,7 @@ extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t row
              M3_ERR_RANGE, "m3_backbone_attention: layer %d rows %d ctx %d out of range", layer, rows, ctx);
   M3_REQUIRE(rows <= bb->rows_written, M3_ERR_RANGE,
              "m3_backbone_attention: rows %d beyond the %d rows a backbone step has set up", rows, bb->rows_written);
-  return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream), false);
+  return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
 }
 
 static int prefix_copy(m3_backbone* bb, int32_t slot, void* store, int32_t length, int save, m3_stream stream) {
