@@ -142,13 +142,16 @@ def overlap(a):
     W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
     sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats,), ctx_buckets=(2048,), use_graphs=True,
                         geom=g.backbone, device=dev)
-    if a.with_ == "depth":
+    if a.with_ in ("depth", "depth+mimi"):
         fd = FastDepth(W, a.seats, batch_buckets=(a.seats,), geom=g.depth, device=dev)
         hd = torch.randn(a.seats, g.depth.d_backbone, device=dev, dtype=torch.bfloat16)
         cb0 = torch.randint(0, 2048, (a.seats,), device=dev)
         dslots = list(range(a.seats))
         other = lambda: fd(dslots, hd, cb0)
-    else:
+    if a.with_ == "depth+mimi":
+        codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
+        first, other = other, (lambda: codec.decode(idx, codes))
+    elif a.with_ == "mimi":
         codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
         other = lambda: codec.decode(idx, codes)
     for k, v in zip(sb.k, sb.v):
@@ -163,7 +166,9 @@ def overlap(a):
     x = torch.randn(a.seats, g.backbone.hidden, device=dev, dtype=torch.bfloat16)
     codes = torch.randint(0, 2048, (a.seats, g.mimi.n_q), device=dev)
     idx = torch.arange(a.seats, device=dev)
-    sb.step(slots, x)
+    if a.with_ != "depth+mimi":
+        first = lambda: sb.step(slots, x)
+    first()
     other()
     torch.cuda.synchronize()
     s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
@@ -177,16 +182,17 @@ def overlap(a):
             s1.wait_stream(cur)
             s2.wait_stream(cur)
             with torch.cuda.stream(s1):
-                sb.step(slots, x)
+                first()
             with torch.cuda.stream(s2 if concurrent else s1):
                 other()
             cur.wait_stream(s1)
             cur.wait_stream(s2)
         e1.record()
         torch.cuda.synchronize()
-        for s in range(a.seats):
-            sb.lengths_cpu[s] -= reps
-        sb.lengths[:a.seats] -= reps
+        if a.with_ != "depth+mimi":       # the backbone steps advanced every slot's length
+            for s in range(a.seats):
+                sb.lengths_cpu[s] -= reps
+            sb.lengths[:a.seats] -= reps
         return e0.elapsed_time(e1) / reps
 
     def alone(fn, reps=10):
@@ -199,13 +205,15 @@ def overlap(a):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
-    t_bb = alone(lambda: sb.step(slots, x))
-    sb.lengths[:a.seats] -= 10
-    for s in range(a.seats):
-        sb.lengths_cpu[s] -= 10
+    t_bb = alone(first)
+    if a.with_ != "depth+mimi":
+        sb.lengths[:a.seats] -= 10
+        for s in range(a.seats):
+            sb.lengths_cpu[s] -= 10
     t_other = alone(other)
-    print(f"seats {a.seats}: backbone step {t_bb:.3f} ms, {a.with_} {t_other:.3f} ms, sequential {run(False):.3f} ms, "
-          f"concurrent {run(True):.3f} ms")
+    name = "depth" if a.with_ == "depth+mimi" else "backbone step"
+    print(f"seats {a.seats}: {name} {t_bb:.3f} ms, {a.with_.split('+')[-1]} {t_other:.3f} ms, sequential "
+          f"{run(False):.3f} ms, concurrent {run(True):.3f} ms")
 
 
 # (label, M, N, K) of the linear layers of one configs[2] tick
@@ -317,8 +325,9 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     ap.add_argument("--cold", action="store_true", help="gemm: stream the weights from HBM on every launch")
-    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth"),
-                    help="overlap: the stage run beside the backbone step")
+    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth", "depth+mimi"),
+                    help="overlap: the stage run beside the backbone step (depth+mimi: the Mimi decode beside the "
+                         "depth loop, no backbone)")
     a = ap.parse_args()
     {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap,
      "guard": guard}[a.case](a)
