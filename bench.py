@@ -124,11 +124,12 @@ def init_steady_state(eng, wl, n_seats):
             eng.cb0.hist_t[s.slot] = torch.from_numpy(wl.rng.integers(0, 2048, eng.cfg.cb0_rep_win))
             eng.depth.row_ctr[s.slot] = age
             tok = 2 * age
-            eng.codec.tokens[s.slot] = tok
             pos = np.arange(max(0, tok - ring), tok)
             kp = np.full(ring, -(1 << 40), np.int64)
             kp[pos % ring] = pos
-            eng.codec.key_pos[s.slot] = torch.from_numpy(kp)
+            with torch.cuda.stream(eng.codec_stream):    # after the slot's codec reset, which runs on that stream
+                eng.codec.tokens[s.slot] = tok
+                eng.codec.key_pos[s.slot] = torch.from_numpy(kp)
             eng.active.append(s)
     torch.cuda.synchronize()
 
@@ -233,6 +234,8 @@ def run_native(a, rank, world, local):
         plans.append(tp)
     for tp in plans:
         eng.graph_for(tp.rows, tp.seats, tp.ctx)
+        for k in (0, 1):
+            eng.codec_for(tp.seats, k)
     staged = torch.from_numpy(np.concatenate([tp.plan for tp in plans])).to(dev)
     offs = np.cumsum([0] + [len(tp.plan) for tp in plans])
     frames = sum(len(tp.dec) + len(tp.new) for tp in plans)
@@ -252,12 +255,15 @@ def run_native(a, rank, world, local):
                 eng.reset_slot(s)
             gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
             gr.plan.copy_(staged[offs[k]:offs[k + 1]], non_blocking=True)
-            eng.replay(gr, tp.rows, tp.seats, tp.ctx)
-            launches += gr.launches
+            cg = eng.replay_tick(gr, tp)      # main part here, codec part on the codec stream beside the next tick
+            launches += gr.launches + cg.launches
             ev[k + 1].record(stream)
+        stream.wait_stream(eng.codec_stream)  # the window ends with the last tick's codec part
+        ev_end = torch.cuda.Event(enable_timing=True)
+        ev_end.record(stream)
         torch.cuda.synchronize()
         launches += lib.m3_launch_count() - c0          # eager launches in the region (slot resets)
-    dev_ms = ev[0].elapsed_time(ev[-1])
+    dev_ms = ev[0].elapsed_time(ev_end)
     tick_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(len(plans))]
     if a.tick_breakdown:
         adm = [k for k, tp in enumerate(plans) if tp.new]
@@ -276,6 +282,8 @@ def run_native(a, rank, world, local):
     for cb in eng.ctx_buckets[-2:]:
         for rb in (r for r in eng.row_buckets if r >= eng.buckets[-1]):
             eng.graph_for(rb, eng.buckets[-1], cb)
+    for k in (0, 1):
+        eng.codec_for(eng.buckets[-1], k)
     def public_run(pipelined):
         """K ticks through the public loop, wall-clocked: tick() (plan, launch, read back, deliver, one tick at a
         time) or tick_pipelined() (tick t+1 launched before tick t is read; the pipeline starts empty and the last
@@ -286,7 +294,7 @@ def run_native(a, rank, world, local):
             top_up(eng, wl)
         if pipelined:
             eng.flush()
-        n_graphs = len(eng.graphs)
+        n_graphs = len(eng.graphs) + len(eng.codec_graphs)
         adm0, rows0 = eng.stats["admitted"], eng.stats["prefill_rows"]
         torch.cuda.synchronize()
         if world > 1:
@@ -301,7 +309,7 @@ def run_native(a, rank, world, local):
             frames_out += len(eng.flush())
         torch.cuda.synchronize()
         mix = {"admitted": eng.stats["admitted"] - adm0, "prefill_rows": eng.stats["prefill_rows"] - rows0,
-               "graphs_captured_in_window": len(eng.graphs) - n_graphs}
+               "graphs_captured_in_window": len(eng.graphs) + len(eng.codec_graphs) - n_graphs}
         return time.perf_counter() - t0, frames_out, mix
 
     row_bytes = (2 + eng.spf // 4) * 8                    # one packed readout row copied back per frame
@@ -314,7 +322,7 @@ def run_native(a, rank, world, local):
     tp = eng.make_plan(list(eng.active), [])
     gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
     gr.plan.copy_(torch.from_numpy(tp.plan).to(dev))
-    eng.replay(gr, tp.rows, tp.seats, tp.ctx)     # leaves this step's q / slots / positions in the scratch
+    eng.replay_tick(gr, tp)     # leaves this step's q / slots / positions in the scratch
     eng.commit(tp)
     eng.deliver_forced(tp.dec)
     bg = g.backbone
@@ -422,6 +430,9 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=12.0, warm=10.0):
         for sb in eng.buckets:
             for rb in (r for r in eng.row_buckets if r >= sb):
                 eng.graph_for(rb, sb, cb)
+    for sb in eng.buckets:
+        for k in (0, 1):
+            eng.codec_for(sb, k)
     torch.cuda.synchronize()
     print(f"box: rank {rank} captured {len(eng.graphs)} graphs in {time.perf_counter() - tc:.2f} s", file=sys.stderr)
     torch.cuda.synchronize()
@@ -430,13 +441,13 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=12.0, warm=10.0):
     t0 = time.perf_counter()
     k, arrived, ttfa, frames, occ = 0, {}, [], 0, []
     t_start = None
-    n_graphs = len(eng.graphs)
+    n_graphs = len(eng.graphs) + len(eng.codec_graphs)
     while True:
         now = time.perf_counter() - t0
         if now >= warm + duration:
             break
         if t_start is None and now >= warm:
-            t_start, frames, occ, n_graphs = now, 0, [], len(eng.graphs)
+            t_start, frames, occ, n_graphs = now, 0, [], len(eng.graphs) + len(eng.codec_graphs)
         while k < len(mine) and mine[k].t <= now:
             r = mine[k]
             s = eng.submit(r.prompt, r.frames)
@@ -455,11 +466,11 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=12.0, warm=10.0):
     t_end = time.perf_counter() - t0
     window = t_end - t_start
     waiting = [(t_end - ta) * 1e3 for ta, _ in arrived.values() if ta >= warm]   # no audio yet: wait so far
-    if len(eng.graphs) > n_graphs:
-        print(f"box: rank {rank} captured {len(eng.graphs) - n_graphs} graphs in the window: "
-              f"{list(eng.graphs)[n_graphs:]}", file=sys.stderr)
+    if len(eng.graphs) + len(eng.codec_graphs) > n_graphs:
+        print(f"box: rank {rank} captured {len(eng.graphs) + len(eng.codec_graphs) - n_graphs} graphs in the window: "
+              f"{list(eng.graphs)[-3:]}", file=sys.stderr)
     local = (ttfa + waiting, frames, window, float(np.mean(occ)) if occ else 0.0, len(waiting), len(mine),
-             len(eng.graphs) - n_graphs)
+             len(eng.graphs) + len(eng.codec_graphs) - n_graphs)
     return summarize_box(local, world, a.seats, cap_per_gpu)
 
 

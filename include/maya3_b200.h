@@ -340,6 +340,18 @@ M3_API int m3_tick_destroy(m3_tick* t);
  * packed receives [seats, 2 + spf / 4] int64 (stop code, cb0, int16 PCM). */
 M3_API int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx, int32_t apply_rep,
                        int32_t apply_top_p, int64_t* packed, m3_stream stream);
+/* m3_tick_run in three parts, so that the codec part of one tick can run on a second stream beside the next tick's
+ * main part.  run_main: the backbone through the feedback write-back (the next tick's input); stage_codec: copies
+ * this tick's stop codes, cb0, codes and seat slots (plan as for run_main) into codec input set `set` (0 or 1);
+ * run_codec: the Mimi frame and the packed readout from set `set`.  The caller orders them: stage_codec after
+ * run_main on its stream; run_codec after stage_codec; stage_codec into a set only after the run_codec that last
+ * read it; Mimi slot resets (m3_mimi_reset) on the codec part's stream.  The codec part's library GEMMs use the
+ * Mimi handle's own workspace.  m3_tick_run = run_main, stage_codec(set 0), run_codec(set 0) on one stream. */
+M3_API int m3_tick_run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
+                            int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
+M3_API int m3_tick_stage_codec(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t set,
+                               m3_stream stream);
+M3_API int m3_tick_run_codec(m3_tick* t, int32_t seats, int32_t set, int64_t* packed, m3_stream stream);
 /* Device pointers of the last tick's per-seat hidden states [max_seats, hidden] bf16, codes [max_seats, n_q] and
  * fp32 PCM [max_seats, spf] (any may be NULL). */
 M3_API int m3_tick_outputs(m3_tick* t, void** h, int64_t** codes, float** pcm);

@@ -128,6 +128,9 @@ SIGNATURES = {
     "m3_tick_create": (C.c_int, [P(TickConfig), P(vp)]),
     "m3_tick_destroy": (C.c_int, [vp]),
     "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
+    "m3_tick_run_main": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp]),
+    "m3_tick_stage_codec": (C.c_int, [vp, vp, i32, i32, i32, vp]),
+    "m3_tick_run_codec": (C.c_int, [vp, i32, i32, vp, vp]),
     "m3_tick_outputs": (C.c_int, [vp, P(vp), P(vp), P(vp)]),
     "m3_tick_status": (C.c_int, [vp, P(i32), i32]),
     "m3_backbone_save_prefix": (C.c_int, [vp, i32, vp, i32, vp]),

@@ -122,7 +122,7 @@ int blas_for_current_device(Blas** out) {
       return M3_ERR_CUDA;
     }
     // A fixed workspace lets cuBLAS calls be captured into CUDA graphs (no allocation at launch).
-    b.ws_bytes = 32u << 20;
+    b.ws_bytes = kBlasWorkspace;
     M3_CUDA(cudaMalloc(&b.ws, b.ws_bytes));
     cublasSetMathMode(b.h, CUBLAS_DEFAULT_MATH);
   }
@@ -135,7 +135,7 @@ static int launch_cublas(const GemmDesc& g, cudaStream_t s) {
   Blas* b = nullptr;
   M3_TRY(blas_for_current_device(&b));
   if (cublasSetStream(b->h, s) != CUBLAS_STATUS_SUCCESS ||
-      cublasSetWorkspace(b->h, b->ws, b->ws_bytes) != CUBLAS_STATUS_SUCCESS) {
+      cublasSetWorkspace(b->h, g.ws ? g.ws : b->ws, g.ws ? g.ws_bytes : b->ws_bytes) != CUBLAS_STATUS_SUCCESS) {
     set_error("cublasSetStream/Workspace failed");
     return M3_ERR_CUDA;
   }

@@ -3,6 +3,8 @@
 
 namespace m3 {
 
+constexpr size_t kBlasWorkspace = 32u << 20;  // cuBLAS workspace per device, and per handle that brings its own
+
 // Y[M,N] = X[M,K] . W[N,K]^T (row-major, leading dimensions in elements), fp32 accumulation.
 struct GemmDesc {
   const bf16* X;
@@ -13,6 +15,10 @@ struct GemmDesc {
   int64_t ldy;
   int M, N, K;
   bool y_f32;  // Y stored as fp32 instead of bf16
+  // cuBLAS workspace for this call (nullptr: the device's shared one).  GEMMs that may run concurrently with others
+  // on a second stream bring their own, so that no two running library kernels share scratch.
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
 };
 
 int gemm(const GemmDesc& g, cudaStream_t s);

@@ -551,6 +551,8 @@ struct m3_mimi {
   int64_t state_row = 0, up_off = 0, conv0_off = 0, final_off = 0;
   std::vector<StageDims> stages;
   void* ws = nullptr;
+  // the decode's own cuBLAS workspace: a tick may run this decode on a second stream beside other library GEMMs
+  unsigned char* blas_ws = nullptr;
   int *slot32 = nullptr, *status = nullptr;
   std::vector<CUtensorMap> kmap, vmap;  // per layer, over kv[layer][k|v] as [slot * heads + head][entry][head_dim]
   // fused SEANet stages (a suffix of the stages: first_fused .. n_ratios-1)
@@ -569,6 +571,13 @@ struct m3_mimi {
        *col = nullptr, *tmp = nullptr;
   float* z = nullptr;
 };
+
+// Every GEMM of the decode runs on the handle's own cuBLAS workspace.
+static int mgemm(const m3_mimi* m, GemmDesc g, cudaStream_t s) {
+  g.ws = m->blas_ws;
+  g.ws_bytes = kBlasWorkspace;
+  return gemm(g, s);
+}
 
 namespace {
 template <class T>
@@ -813,6 +822,7 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   add(R * T * H * 2); add(R * T * H * 2); add(R * T * 3 * H * 2); add(R * T * H * 2); add(R * T * H * 2);
   add(R * T * H * 2); add(R * T * c.ffn * 2);
   add(act * 2); add(act * 2); add(col * 2); add(act * 2); add(zf * 4);
+  add(kBlasWorkspace);
   cudaError_t e = cudaMalloc(&m->ws, bytes);
   if (e != cudaSuccess) {
     delete m;
@@ -839,6 +849,7 @@ extern "C" int m3_mimi_create(const m3_mimi_config* cfg, const m3_mimi_weights* 
   m->col = carve<bf16>(p, col);
   m->tmp = carve<bf16>(p, act);
   m->z = carve<float>(p, zf);
+  m->blas_ws = carve<unsigned char>(p, kBlasWorkspace);
   cudaMemset(m->status, 0, 256);
   {
     EncodeTiled enc;
@@ -964,8 +975,10 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   rvq_gather_kernel<<<R, 128, 0, s>>>(codes, c.n_q, c.n_semantic, c.codebook_size, c.codebook_dim, m->books,
                                       m->a_sem, m->a_ac, m->status);
   M3_LAUNCHED();
-  M3_TRY(gemm({m->a_sem, c.codebook_dim, m->proj_sem, c.codebook_dim, m->p_sem, H, R, H, c.codebook_dim, false}, s));
-  M3_TRY(gemm({m->a_ac, c.codebook_dim, m->proj_ac, c.codebook_dim, m->p_ac, H, R, H, c.codebook_dim, false}, s));
+  M3_TRY(mgemm(m, {m->a_sem, c.codebook_dim, m->proj_sem, c.codebook_dim, m->p_sem, H, R, H, c.codebook_dim, false},
+               s));
+  M3_TRY(mgemm(m, {m->a_ac, c.codebook_dim, m->proj_ac, c.codebook_dim, m->p_ac, H, R, H, c.codebook_dim, false},
+               s));
   upsample_kernel<<<dim3(R, cdiv(H, 128)), 128, 0, s>>>(m->p_sem, m->p_ac, m->upw, T, m->slot32,
                                                          m->state + m->up_off, m->state_row, m->h, H);
   M3_LAUNCHED();
@@ -978,7 +991,7 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   M3_TRY(launch_add_ln(R * T, m->h, 1, H, 0, nullptr, nullptr, 0, nullptr, nullptr, m->y, m->ln1_w[0], m->ln1_b[0],
                 c.norm_eps, H, s));
   for (int li = 0; li < c.layers; ++li) {
-    M3_TRY(gemm({m->y, H, m->wqkv[li], H, m->qkv, 3 * H, R * T, 3 * H, H, false}, s));
+    M3_TRY(mgemm(m, {m->y, H, m->wqkv[li], H, m->qkv, 3 * H, R * T, 3 * H, H, false}, s));
     bf16* kr = m->kv + (int64_t)li * 2 * kv_half;
     mimi_rope_kernel<<<R * T, 32 * c.heads, 0, s>>>(m->qkv, m->pos, m->inv_freq, m->slot32, T, c.heads, hd, c.ring,
                                                    m->q, kr, kr + kv_half, slot_stride);
@@ -998,15 +1011,15 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
 #undef M3_RING_MMA
     }
     M3_LAUNCHED();
-    M3_TRY(gemm({m->att, H, m->wo[li], H, m->ob, H, R * T, H, H, false}, s));
+    M3_TRY(mgemm(m, {m->att, H, m->wo[li], H, m->ob, H, R * T, H, H, false}, s));
     scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls1[li], m->y, m->ln2_w[li], m->ln2_b[li], c.norm_eps,
                                              H);
     M3_LAUNCHED();
-    M3_TRY(gemm({m->y, H, m->fc1[li], H, m->ff, c.ffn, R * T, c.ffn, H, false}, s));
+    M3_TRY(mgemm(m, {m->y, H, m->fc1[li], H, m->ff, c.ffn, R * T, c.ffn, H, false}, s));
     const int64_t n8 = (int64_t)R * T * c.ffn / 8;
     gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(m->ff, n8);
     M3_LAUNCHED();
-    M3_TRY(gemm({m->ff, c.ffn, m->fc2[li], c.ffn, m->ob, H, R * T, H, c.ffn, false}, s));
+    M3_TRY(mgemm(m, {m->ff, c.ffn, m->fc2[li], c.ffn, m->ob, H, R * T, H, c.ffn, false}, s));
     const bool last = li + 1 == c.layers;
     scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls2[li], m->y, last ? nullptr : m->ln1_w[li + 1],
                                              last ? nullptr : m->ln1_b[li + 1], c.norm_eps, H);
@@ -1022,7 +1035,7 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   conv_hist_kernel<<<dim3(R, cdiv(H / 8, 128)), 128, 0, s>>>(m->h, T, H, c.kernel, 0, m->slot32, m->state,
                                                               m->state_row, m->conv0_off);
   M3_LAUNCHED();
-  M3_TRY(gemm({m->col, (int64_t)c.kernel * H, m->conv0_w, (int64_t)c.kernel * H, m->z, C0, R * T, C0, c.kernel * H,
+  M3_TRY(mgemm(m, {m->col, (int64_t)c.kernel * H, m->conv0_w, (int64_t)c.kernel * H, m->z, C0, R * T, C0, c.kernel * H,
                true},
               s));
   int64_t n = (int64_t)R * T * C0 / 8;
@@ -1046,9 +1059,9 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     // ELU -> ConvTranspose1d as X . Wt^T (fp32 contributions) -> fold with the overlap tail
     elu_kernel<<<(unsigned)((Min * sd.cin / 8 + 255) / 256), 256, 0, s>>>(x, m->tmp, Min * sd.cin / 8);
     M3_LAUNCHED();
-    M3_TRY(gemm({m->tmp, sd.cin, m->convt_w[i], sd.cin, m->z, 2 * sd.r * sd.cout, (int)Min, 2 * sd.r * sd.cout, sd.cin,
-                 true},
-                s));
+    M3_TRY(mgemm(m, {m->tmp, sd.cin, m->convt_w[i], sd.cin, m->z, 2 * sd.r * sd.cout, (int)Min, 2 * sd.r * sd.cout,
+                     sd.cin, true},
+                 s));
     convt_fold_kernel<<<dim3(R, cdiv(sd.L * sd.r * sd.cout / 8, 256)), 256, 0, s>>>(
         m->z, m->convt_b[i], sd.L, sd.r, sd.cout, m->slot32, m->state, m->state_row, sd.tail_off, other);
     M3_LAUNCHED();
@@ -1066,14 +1079,14 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     conv_hist_kernel<<<dim3(R, cdiv(sd.cout / 8, 128)), 128, 0, s>>>(x, Lo, sd.cout, c.res_kernel, 1, m->slot32,
                                                                       m->state, m->state_row, sd.hist_off);
     M3_LAUNCHED();
-    M3_TRY(gemm({m->col, (int64_t)c.res_kernel * sd.cout, m->res1_w[i], (int64_t)c.res_kernel * sd.cout, m->z, hid,
+    M3_TRY(mgemm(m, {m->col, (int64_t)c.res_kernel * sd.cout, m->res1_w[i], (int64_t)c.res_kernel * sd.cout, m->z, hid,
                  (int)Mout, hid, c.res_kernel * sd.cout, true},
                 s));
     n = Mout * hid / 8;
     bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res1_b[i], Mout, hid, 1, nullptr,
                                                                      m->tmp);
     M3_LAUNCHED();
-    M3_TRY(gemm({m->tmp, hid, m->res2_w[i], hid, m->z, sd.cout, (int)Mout, sd.cout, hid, true}, s));
+    M3_TRY(mgemm(m, {m->tmp, hid, m->res2_w[i], hid, m->z, sd.cout, (int)Mout, sd.cout, hid, true}, s));
     n = Mout * sd.cout / 8;
     if (i + 1 == first_fused && first_fused < nst) {  // the next stage is fused: hand it e = ELU(y) in act0 (in place when x is act0)
       bias_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m->z, m->res2_b[i], Mout, sd.cout, 3, x,

@@ -1,8 +1,13 @@
-// The engine tick as one native call (replaces the device half of Engine._tick, maya3/engine.py:534-561):
-// gather each row's backbone input (a seat's feedback vector, or a prompt token embedding for inline-prefill rows),
-// the backbone step, each seat's hidden state, the cb0 sampler, the depth loop, the feedback write-back, the Mimi
-// frame and the packed readout.  Everything is enqueued on one stream with no host synchronisation, so the caller
-// captures one CUDA graph per (row bucket, seat bucket, context bucket).
+// The engine tick as native calls (replaces the device half of Engine._tick, maya3/engine.py:534-561): gather each
+// row's backbone input (a seat's feedback vector, or a prompt token embedding for inline-prefill rows), the backbone
+// step, each seat's hidden state, the cb0 sampler, the depth loop, the feedback write-back, the Mimi frame and the
+// packed readout, enqueued with no host synchronisation.
+//
+// The tick has two parts.  The main part (m3_tick_run_main) ends with the feedback write-back, which the next tick
+// reads; the codec part (m3_tick_run_codec: Mimi frame + readout) is off that path, so it may run on a second stream
+// beside the next tick's main part.  m3_tick_stage_codec hands one tick's outputs over: it copies the stop codes,
+// cb0, codes and seat slots into one of two codec input sets, which the main part of the next tick does not touch.
+// m3_tick_run is the three in order on one stream.
 #include <vector>
 
 #include "common.cuh"
@@ -59,6 +64,20 @@ __global__ void scatter_rows_kernel(const bf16* __restrict__ src, const int64_t*
   for (int k = threadIdx.x; k < D / 8; k += blockDim.x) d[k] = s[k];
 }
 
+// The codec inputs of one tick: c_code / c_cb0 / c_slot [seats], c_codes [seats, n_q] (one thread per int64).
+__global__ void stage_codec_kernel(const int64_t* __restrict__ code, const int64_t* __restrict__ cb0,
+                                   const int64_t* __restrict__ codes, const int64_t* __restrict__ s_slot, int seats,
+                                   int n_q, int64_t* __restrict__ c_code, int64_t* __restrict__ c_cb0,
+                                   int64_t* __restrict__ c_codes, int64_t* __restrict__ c_slot) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < seats * n_q) c_codes[i] = codes[i];
+  if (i < seats) {
+    c_code[i] = code[i];
+    c_cb0[i] = cb0[i];
+    c_slot[i] = s_slot[i];
+  }
+}
+
 }  // namespace m3
 
 using namespace m3;
@@ -70,6 +89,7 @@ struct m3_tick {
   int64_t *code = nullptr, *cb0 = nullptr, *codes = nullptr;
   float* pcm = nullptr;
   int* status = nullptr;
+  int64_t *c_code[2] = {}, *c_cb0[2] = {}, *c_codes[2] = {}, *c_slot[2] = {};  // the two codec input sets
   bool guard = false;  // m3_tick_set_guard: run the guards after the cb0 sampler
   m3_guard_config gc{};
   m3_guard_state gs{};
@@ -86,6 +106,9 @@ extern "C" int m3_tick_create(const m3_tick_config* cfg, m3_tick** out) {
   auto add = [&](size_t n) { bytes += (n + 255) / 256 * 256; };
   add(R * D * 2); add(R * D * 2); add(S * D * 2); add(S * D * 2); add(S * 8); add(S * 8); add(S * cfg->n_q * 8);
   add(S * cfg->spf * 4); add(256);
+  for (int k = 0; k < 2; ++k) {
+    add(S * 8); add(S * 8); add(S * cfg->n_q * 8); add(S * 8);
+  }
   cudaError_t e = cudaMalloc(&t->ws, bytes);
   if (e != cudaSuccess) {
     delete t;
@@ -107,6 +130,12 @@ extern "C" int m3_tick_create(const m3_tick_config* cfg, m3_tick** out) {
   t->codes = (int64_t*)carve(S * cfg->n_q * 8);
   t->pcm = (float*)carve(S * cfg->spf * 4);
   t->status = (int*)carve(256);
+  for (int k = 0; k < 2; ++k) {
+    t->c_code[k] = (int64_t*)carve(S * 8);
+    t->c_cb0[k] = (int64_t*)carve(S * 8);
+    t->c_codes[k] = (int64_t*)carve(S * cfg->n_q * 8);
+    t->c_slot[k] = (int64_t*)carve(S * 8);
+  }
   cudaMemset(t->status, 0, 256);
   *out = t;
   return M3_OK;
@@ -133,12 +162,12 @@ extern "C" int m3_tick_status(m3_tick* t, int32_t* status, int32_t clear) {
   return M3_OK;
 }
 
-extern "C" int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
-                           int32_t apply_rep, int32_t apply_top_p, int64_t* packed, m3_stream stream) {
-  M3_REQUIRE(t && plan && packed, M3_ERR_ARG, "m3_tick_run: null argument");
+extern "C" int m3_tick_run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
+                                int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
+  M3_REQUIRE(t && plan, M3_ERR_ARG, "m3_tick_run_main: null argument");
   const m3_tick_config& c = t->c;
   M3_REQUIRE(rows >= 0 && rows <= c.max_rows && seats >= 0 && seats <= c.max_seats, M3_ERR_RANGE,
-             "m3_tick_run: rows %d seats %d outside the configured maxima", rows, seats);
+             "m3_tick_run_main: rows %d seats %d outside the configured maxima", rows, seats);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int D = c.hidden;
   // plan layout (int64): rows x {slot, offset, real, token}, then seats x {slot, row}
@@ -162,9 +191,41 @@ extern "C" int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_
   M3_TRY(m3_depth_step(c.depth, s_slot, t->h, t->cb0, t->codes, t->fb, seats, stream));
   scatter_rows_kernel<<<seats, 128, 0, s>>>(t->fb, s_slot, seats, c.max_slots - 1, (bf16*)c.feedback, D);
   M3_LAUNCHED();
-  M3_TRY(m3_mimi_decode(c.mimi, s_slot, t->codes, t->pcm, seats, stream));
-  M3_TRY(m3_pack_readout(t->code, t->cb0, t->pcm, packed, seats, c.spf, stream));
   return M3_OK;
+}
+
+extern "C" int m3_tick_stage_codec(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t set,
+                                   m3_stream stream) {
+  M3_REQUIRE(t && plan, M3_ERR_ARG, "m3_tick_stage_codec: null argument");
+  const m3_tick_config& c = t->c;
+  M3_REQUIRE(rows >= 0 && rows <= c.max_rows && seats >= 0 && seats <= c.max_seats && (set == 0 || set == 1),
+             M3_ERR_RANGE, "m3_tick_stage_codec: rows %d seats %d set %d out of range", rows, seats, set);
+  if (seats == 0) return M3_OK;
+  const int n = seats * c.n_q;
+  stage_codec_kernel<<<cdiv(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      t->code, t->cb0, t->codes, plan + 4 * rows, seats, c.n_q, t->c_code[set], t->c_cb0[set], t->c_codes[set],
+      t->c_slot[set]);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+extern "C" int m3_tick_run_codec(m3_tick* t, int32_t seats, int32_t set, int64_t* packed, m3_stream stream) {
+  M3_REQUIRE(t && packed, M3_ERR_ARG, "m3_tick_run_codec: null argument");
+  const m3_tick_config& c = t->c;
+  M3_REQUIRE(seats >= 0 && seats <= c.max_seats && (set == 0 || set == 1), M3_ERR_RANGE,
+             "m3_tick_run_codec: seats %d set %d out of range", seats, set);
+  if (seats == 0) return M3_OK;
+  M3_TRY(m3_mimi_decode(c.mimi, t->c_slot[set], t->c_codes[set], t->pcm, seats, stream));
+  M3_TRY(m3_pack_readout(t->c_code[set], t->c_cb0[set], t->pcm, packed, seats, c.spf, stream));
+  return M3_OK;
+}
+
+extern "C" int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
+                           int32_t apply_rep, int32_t apply_top_p, int64_t* packed, m3_stream stream) {
+  M3_REQUIRE(t && plan && packed, M3_ERR_ARG, "m3_tick_run: null argument");
+  M3_TRY(m3_tick_run_main(t, plan, rows, seats, ctx, apply_rep, apply_top_p, stream));
+  M3_TRY(m3_tick_stage_codec(t, plan, rows, seats, 0, stream));
+  return m3_tick_run_codec(t, seats, 0, packed, stream);
 }
 
 extern "C" int m3_tick_set_guard(m3_tick* t, const m3_guard_config* cfg, const m3_guard_state* st) {

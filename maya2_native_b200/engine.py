@@ -188,7 +188,13 @@ def plan_layout(dec, new, lengths, row_buckets, seat_buckets, ctx_buckets, dummy
 
 
 class _Graph:
-    __slots__ = ("graph", "plan", "packed", "staging", "evt", "launches")
+    """The main part of a tick (backbone through the feedback write-back) for one bucket."""
+    __slots__ = ("graph", "plan", "staging", "evt", "launches")
+
+
+class _Codec:
+    """The codec part of a tick (Mimi frame + packed readout) for one seat bucket and codec input set."""
+    __slots__ = ("graph", "packed", "launches")
 
 
 class TickEngine:
@@ -235,7 +241,13 @@ class TickEngine:
         self._rng = np.random.default_rng(cfg.seed)
         self._ids = itertools.count()
         self.graphs = {}
+        self.codec_graphs = {}
         self.pool = None
+        # the codec part of tick t runs on its own stream beside the main part of tick t + 1; its inputs alternate
+        # between two sets, and a set is restaged only after the codec part that last read it has finished
+        self.codec_stream = torch.cuda.Stream(device=dev)
+        self._set = 0
+        self._set_free = [None, None]
         # two pinned readout buffers, used in turn: a tick's PCM views stay valid while the next tick is in flight
         self._hosts = [torch.empty(self.buckets[-1], 2 + self.spf // 4, dtype=torch.int64).pin_memory()
                        for _ in range(2)]
@@ -249,13 +261,16 @@ class TickEngine:
 
     def close(self):
         if getattr(self, "_handle", None):
+            torch.cuda.synchronize(self.device)     # the codec stream may still run the last tick's codec part
             self.graphs.clear()
+            self.codec_graphs.clear()
             L.load().m3_tick_destroy(self._handle)
             self._handle = None
             for c in (self.backbone, self.cb0, self.depth, self.codec):
                 c.close()
 
     def device_status(self, clear=True) -> int:
+        torch.cuda.synchronize(self.device)     # the codec stream's last tick included
         s = L.i32(0)
         L.check(L.load().m3_tick_status(self._handle, s, int(clear)), "m3_tick_status")
         return int(s.value)
@@ -343,7 +358,8 @@ class TickEngine:
         self.depth.row_seed[slot] = (s.seed * 69069 + 1) % (2 ** 31 - 1)
         self.depth.row_ctr[slot] = 0
         self.depth.cross_const[slot] = self.voice_const
-        self.codec._reset_row(slot)
+        with torch.cuda.stream(self.codec_stream):     # ordered between the codec parts of two ticks
+            self.codec._reset_row(slot)
         self.backbone.lengths[slot] = 0
         if s.voice is not None:       # maya3/engine.py:488-491: the prefix KV, then the prompt after it
             self.backbone.load_prefix_store(slot, s.voice.store, s.voice.length)
@@ -442,7 +458,6 @@ class TickEngine:
             idle[3 * rb:4 * rb] = -1
             idle[4 * rb:4 * rb + sb] = dummy
             g.plan = torch.from_numpy(idle).to(self.device)
-            g.packed = torch.zeros(sb, 2 + self.spf // 4, dtype=torch.long, device=self.device)
         g.staging = torch.zeros(n, dtype=torch.long).pin_memory()
         g.evt = None
         g.graph = None
@@ -468,35 +483,113 @@ class TickEngine:
 
     def _launch(self, g, rb, sb, cb, stream=None):
         rep, top_p = self.cb0.flags()
-        L.check(L.load().m3_tick_run(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p, g.packed.data_ptr(),
-                                     L.stream_ptr(stream)), "m3_tick_run")
+        L.check(L.load().m3_tick_run_main(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p,
+                                          L.stream_ptr(stream)), "m3_tick_run_main")
 
-    def replay(self, g, rb, sb, cb):
+    def codec_for(self, sb, k) -> _Codec:
+        """The codec part for seat bucket `sb` reading input set `k`; its warm-up and capture decode only the dummy
+        slot (the set is staged from an all-padding plan first)."""
+        key = (sb, k)
+        cg = self.codec_graphs.get(key)
+        if cg is not None:
+            return cg
+        cg = _Codec()
+        lib = L.load()
+        with torch.inference_mode():
+            cg.packed = torch.zeros(sb, 2 + self.spf // 4, dtype=torch.long, device=self.device)
+            idle = torch.full((2 * sb,), self.cfg.max_seats, dtype=torch.long, device=self.device)
+            idle[sb:] = 0
+        cg.graph = None
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        side.wait_stream(self.codec_stream)
+        with torch.cuda.stream(side):
+            L.check(lib.m3_tick_stage_codec(self._handle, idle.data_ptr(), 0, sb, k, L.stream_ptr(side)),
+                    "m3_tick_stage_codec")
+            for _ in range(2 if self.cfg.use_graphs else 0):
+                self._launch_codec(cg, sb, k, side)
+        torch.cuda.current_stream().wait_stream(side)
+        self.codec_stream.wait_stream(side)
+        if self.cfg.use_graphs:
+            if self.pool is None:
+                self.pool = torch.cuda.graph_pool_handle()
+            cg.graph = torch.cuda.CUDAGraph()
+            before = lib.m3_launch_count()
+            with torch.cuda.graph(cg.graph, pool=self.pool):
+                self._launch_codec(cg, sb, k)
+            cg.launches = lib.m3_launch_count() - before
+            with torch.cuda.stream(self.codec_stream):
+                cg.graph.replay()   # upload; the set still holds the idle staging
+        else:
+            cg.launches = None
+        self.codec_graphs[key] = cg
+        return cg
+
+    def _launch_codec(self, cg, sb, k, stream=None):
+        L.check(L.load().m3_tick_run_codec(self._handle, sb, k, cg.packed.data_ptr(), L.stream_ptr(stream)),
+                "m3_tick_run_codec")
+
+    def replay_tick(self, g, tp, k=None):
+        """Enqueue one planned tick whose plan is already in g.plan: the main part on the current stream, then the
+        hand-off of its outputs into codec input set k (after the codec part that last read that set), then the
+        codec part on the codec stream.  Returns the codec part's record."""
+        A, B = torch.cuda.current_stream(self.device), self.codec_stream
+        if k is None:
+            k = self._set
+            self._set ^= 1
+        cg = self.codec_for(tp.seats, k)
         if g.graph is not None:
             g.graph.replay()
         else:
-            self._launch(g, rb, sb, cb)
+            self._launch(g, tp.rows, tp.seats, tp.ctx)
+        if self._set_free[k] is not None:
+            A.wait_event(self._set_free[k])
+        L.check(L.load().m3_tick_stage_codec(self._handle, g.plan.data_ptr(), tp.rows, tp.seats, k,
+                                             L.stream_ptr(A)), "m3_tick_stage_codec")
+        staged = torch.cuda.Event()
+        staged.record(A)
+        B.wait_event(staged)
+        with torch.cuda.stream(B):
+            if cg.graph is not None:
+                cg.graph.replay()
+            else:
+                self._launch_codec(cg, tp.seats, k)
+        done = torch.cuda.Event()
+        done.record(B)
+        self._set_free[k] = done
+        return cg
+
+    def launches_per_tick(self, g, tp):
+        """This library's kernels one tick launches (main graph + hand-off + codec graph), None without graphs."""
+        cg = self.codec_graphs.get((tp.seats, 0))
+        if g.launches is None or cg is None or cg.launches is None:
+            return None
+        return g.launches + 1 + cg.launches
 
     # ---------------------------------------------------------------- tick
     def _launch_tick(self, dec, new):
-        """Plan one tick, copy its plan host->device, replay its graph and queue the device->host copy of its packed
-        readout into the next pinned buffer; the host mirror of the KV lengths moves at once.  Returns the tick's
-        (plan, host rows, event recorded after the readout copy)."""
+        """Plan one tick, copy its plan host->device, enqueue its main and codec parts (replay_tick) and the
+        device->host copy of its packed readout into the next pinned buffer, on the codec stream; the host mirror of
+        the KV lengths moves at once.  Returns the tick's (plan, host rows, event recorded after the readout copy)."""
         tp = self.make_plan(dec, new)
         g = self.graph_for(tp.rows, tp.seats, tp.ctx)
+        k = self._set
+        self._set ^= 1
+        self.codec_for(tp.seats, k)     # captured before this tick's plan lands in g.plan
         if g.evt is not None:
             g.evt.synchronize()     # the pinned staging row may still feed the previous copy
         g.staging.numpy()[:] = tp.plan
         g.plan.copy_(g.staging, non_blocking=True)
         g.evt = torch.cuda.Event()
         g.evt.record()
-        self.replay(g, tp.rows, tp.seats, tp.ctx)
-        B = len(dec) + len(new)
-        host = self._hosts[self._flip][:B]
+        cg = self.replay_tick(g, tp, k)
+        n = len(dec) + len(new)
+        host = self._hosts[self._flip][:n]
         self._flip ^= 1
-        host.copy_(g.packed[:B], non_blocking=True)
-        evt = torch.cuda.Event()
-        evt.record()
+        with torch.cuda.stream(self.codec_stream):
+            host.copy_(cg.packed[:n], non_blocking=True)
+            evt = torch.cuda.Event()
+            evt.record()
         self.commit(tp)
         return tp, host, evt
 
