@@ -776,7 +776,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     with torch.inference_mode():
         line = run_native(a, rank, world, local)
-    if rank == 0 and world == 1 and not a.no_extra and not a.no_reference_gpu:
+    if rank == 0 and world == 1 and not a.no_extra and not a.no_reference_gpu and "e2e" in line:
         try:
             line["reference_gpu"] = run_reference_gpu(a, torch.device("cuda", local), line)
         except Exception as exc:                      # reported, not fatal: the native line still stands

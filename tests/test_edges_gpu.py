@@ -119,3 +119,47 @@ def test_mimi_empty_and_extreme_codes(cuda):
     snr = 10 * np.log10((ref ** 2).sum() / max(((got - ref) ** 2).sum(), 1e-30))
     assert snr > 30, snr
     assert sm.device_status() == 0
+
+
+def test_single_call_tick_equals_the_two_stream_tick(cuda):
+    """m3_tick_run (main part, codec hand-off and codec part in order on one stream: the C ABI's one-call tick)
+    delivers the same packed readout, bit for bit, as TickEngine's tick with the codec part on its own stream beside
+    the next tick's main part, tick by tick over admissions and decode ticks."""
+    from maya2_native_b200.engine import TickConfig, TickEngine
+    W = {k: v.to(cuda) for k, v in WG.generate(WG.all_shapes(TINY), seed=12).items()}
+    cfg = TickConfig(max_seats=3, capacity=64, max_inline_rows=8, stops=False)
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, TINY.backbone.vocab, n) for n in (5, 3, 4, 6)]
+    engines = [TickEngine(TINY, W, cfg, device=cuda) for _ in range(2)]
+    for e in engines:
+        for i, p in enumerate(prompts):
+            e.submit(p, 6 + i, seed=40 + i)
+    lib = L.load()
+    two, one = engines
+    for _ in range(12):
+        out = two.tick_pipelined()
+        got_two = two.last_readout().copy() if out else None
+        # the same tick through the one-call entry point on the other engine
+        new = one._admit()
+        dec = list(one.active)
+        if not dec and not new:
+            break
+        tp = one.make_plan(dec, new)
+        plan = torch.from_numpy(tp.plan).to(cuda)
+        packed = torch.zeros(tp.seats, 2 + one.spf // 4, dtype=torch.long, device=cuda)
+        rep, top_p = one.cb0.flags()
+        torch.cuda.current_stream().wait_stream(one.codec_stream)   # the admitted slots' codec resets
+        assert lib.m3_tick_run(one._handle, plan.data_ptr(), tp.rows, tp.seats, tp.ctx, rep, top_p,
+                               packed.data_ptr(), L.stream_ptr()) == L.M3_OK
+        one.commit(tp)
+        hv = packed[:len(dec) + len(new)].cpu().numpy()
+        one._deliver(tp.dec + tp.new, hv)
+        if got_two is not None:
+            assert np.array_equal(got_two, ref_prev), "readout of the previous tick differs"
+        ref_prev = hv
+    for s in two.flush():
+        pass
+    assert np.array_equal(two.last_readout(), ref_prev)
+    assert two.device_status() == 0 and one.device_status() == 0
+    for e in engines:
+        e.close()
