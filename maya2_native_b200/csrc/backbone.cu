@@ -17,23 +17,40 @@ constexpr int kHeadDim = 128;
 
 // ------------------------------------------------------------------------------------------------ row setup
 // slot and position of every row, validated once per step (pos = lengths[slot] + offset, read before the step's
-// length update as serve/fast_backbone.py:178-179), and the order in which the attention visits the rows: longest
-// first (position descending, then row), so the CTAs with the most keys start first and the short rows fill the last
-// wave.  The order is written as one record per visited row, visit[i] = {row, slot, position, 0}, so the attention's
-// CTA finds all three with one 16-byte load.  With `sort` the grid is one CTA of a power of two >= rows threads
-// (<= 1024): rows that already come longest first (as the engine plans a tick) keep the identity order after one block
-// vote, others are sorted in shared memory (bitonic); without `sort` the order is the identity.
+// length update as serve/fast_backbone.py:178-179), and the work list of the attention.  A decode row is one entry.
+// The rows of an inline prompt (consecutive rows of one slot at offsets 0..P-1, as the step lays them out) go in
+// groups of `rg` consecutive positions, one entry per group: a group's CTA reads the keys up to its last position once
+// for all of its rows instead of once per row.  Entries are written as visit[i] = {first row, slot, last position,
+// rows}; the rows of a group after its first get {row, slot, 0, 0} (nothing to do).  The attention visits entries
+// longest first (last position descending, then row), so the CTAs with the most keys start first and the short ones
+// fill the last wave.  With `sort` the grid is one CTA of a power of two >= rows threads (<= 1024): entries that
+// already come longest first keep the identity order after one block vote, others are sorted in shared memory
+// (bitonic); without `sort` the order is the identity.
 constexpr int kSortRows = 1024;
 
+// rows of the entry starting at row r (0: r is inside a group) and its last position
+__device__ __forceinline__ int entry_rows(const int64_t* __restrict__ slots, const int64_t* __restrict__ offsets,
+                                          int rows, int r, int rg) {
+  if (!offsets) return 1;
+  const int64_t o = offsets[r];
+  const bool prompt = o > 0 || (r + 1 < rows && offsets[r + 1] == 1 && slots[r + 1] == slots[r]);
+  if (!prompt) return 1;
+  if (o % rg != 0) return 0;
+  int n = 1;
+  while (n < rg && r + n < rows && slots[r + n] == slots[r] && offsets[r + n] == o + n) ++n;
+  return n;
+}
+
 __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_t* __restrict__ offsets,
-                                 const int64_t* __restrict__ lengths, int rows, int max_slots, int capacity,
+                                 const int64_t* __restrict__ lengths, int rows, int max_slots, int capacity, int rg,
                                  int* __restrict__ slot32, int* __restrict__ pos32, int4* __restrict__ visit,
                                  int sort, int* status) {
   __shared__ uint64_t key[kSortRows];
   __shared__ int slot_of[kSortRows];
+  __shared__ int rows_of[kSortRows];
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   int64_t p = 0;
-  int sl = 0;
+  int sl = 0, nr = 0, last = 0;
   if (r < rows) {
     int64_t s = slots[r];
     if (s < 0 || s > max_slots) {
@@ -48,18 +65,22 @@ __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_
     sl = (int)s;
     slot32[r] = sl;
     pos32[r] = (int)p;
+    nr = entry_rows(slots, offsets, rows, r, rg);
+    last = nr > 0 ? (int)min(p + nr - 1, (int64_t)capacity - 1) : 0;
   }
   if (!sort) {
-    if (r < rows) visit[r] = make_int4(r, sl, (int)p, 0);
+    if (r < rows) visit[r] = make_int4(r, sl, last, nr);
     return;
   }
-  // one CTA, n = blockDim.x: keys (position << 32 | 0x7FFFFFFF - row) sorted descending; padding keys are 0
+  // one CTA, n = blockDim.x: keys (last position << 32 | 0x7FFFFFFF - row) sorted descending; group members and
+  // padding keys are 0, so they come last
   const int t = threadIdx.x, n = blockDim.x;
-  key[t] = t < rows ? ((uint64_t)(uint32_t)p << 32) | (uint32_t)(0x7FFFFFFF - t) : 0ull;
+  key[t] = t < rows && nr > 0 ? ((uint64_t)(uint32_t)last << 32) | (uint32_t)(0x7FFFFFFF - t) : 0ull;
   slot_of[t] = sl;
+  rows_of[t] = nr;
   __syncthreads();
-  if (__syncthreads_and(t + 1 >= rows || key[t] > key[t + 1])) {  // already in order (keys are distinct)
-    if (t < rows) visit[t] = make_int4(t, sl, (int)p, 0);
+  if (__syncthreads_and(t + 1 >= rows || key[t] > key[t + 1] || (key[t] == 0 && key[t + 1] == 0))) {
+    if (t < rows) visit[t] = make_int4(t, sl, last, nr);   // already in order
     return;
   }
   for (int k = 2; k <= n; k <<= 1)
@@ -75,20 +96,24 @@ __global__ void prep_rows_kernel(const int64_t* __restrict__ slots, const int64_
       __syncthreads();
     }
   if (t < rows) {
-    const int o = 0x7FFFFFFF - (int)(uint32_t)key[t];
-    visit[t] = make_int4(o, slot_of[o], (int)(key[t] >> 32), 0);
+    if (key[t] == 0) {
+      visit[t] = make_int4(0, 0, 0, 0);                   // a group member or padding: no work
+    } else {
+      const int o = 0x7FFFFFFF - (int)(uint32_t)key[t];
+      visit[t] = make_int4(o, slot_of[o], (int)(key[t] >> 32), rows_of[o]);
+    }
   }
 }
 
 int launch_prep_rows(const int64_t* slots, const int64_t* offsets, const int64_t* lengths, int rows, int max_slots,
-                     int capacity, int* slot32, int* pos32, int4* visit, int* status, cudaStream_t s) {
+                     int capacity, int rg, int* slot32, int* pos32, int4* visit, int* status, cudaStream_t s) {
   if (rows <= kSortRows) {
     int n = 32;
     while (n < rows) n <<= 1;
-    prep_rows_kernel<<<1, n, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, slot32, pos32, visit, 1,
+    prep_rows_kernel<<<1, n, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, rg, slot32, pos32, visit, 1,
                                      status);
   } else {
-    prep_rows_kernel<<<cdiv(rows, 128), 128, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, slot32,
+    prep_rows_kernel<<<cdiv(rows, 128), 128, 0, s>>>(slots, offsets, lengths, rows, max_slots, capacity, rg, slot32,
                                                      pos32, visit, 0, status);
   }
   M3_LAUNCHED();
@@ -289,16 +314,21 @@ __device__ __forceinline__ void split_epilogue(const float (&Og)[G], const float
 // K and V arrive by TMA through per-layer tensor maps over the cache [slot * kv_heads + head][position][128]: a
 // 16-token block is four 2 KB boxes (K and V, dims 0-63 and 64-127), 128-byte swizzled so that ldmatrix reads them
 // without bank conflicts.  Each of the 4 warps owns every 4th block of the CTA's chunk and its own kMmaStages-deep
-// ring (no CTA-wide barrier in the loop).  Per block:
-//   S   = Q K^T       A = Q (16 rows, the G query heads, rest zero), B = K rows via ldmatrix      (16 mma)
-//   P   = 2^(S*scale - m) with the warp's lazily raised running max m, masked past the row's length
-//   O^T += V^T P^T    A = V^T via ldmatrix.trans, B = P^T straight from the S accumulators, P split into bf16
-//                     hi + lo parts so that the weights keep ~16 mantissa bits (the reference keeps them in fp32)
-// V rows past the row's last key are zeroed in shared memory before use (0 * stale data must stay 0).
+// ring (no CTA-wide barrier in the loop).  A CTA serves one work entry: the G query heads of a decode row, or those
+// of `rows` consecutive positions of an inline prompt (rows x G <= 16 query vectors, the 16 rows of the mma tile),
+// whose keys it then reads once for all of them.  Query vector v = j G + h (row j of the entry, head kv_head G + h)
+// sits in mma row v.  Per block:
+//   S   = Q K^T       A = Q (the entry's query vectors, rest zero), B = K rows via ldmatrix           (16 mma)
+//   P   = 2^(S*scale - m) per query vector with its lazily raised running max m, masked past its own position
+//   O^T += V^T P^T    A = V^T via ldmatrix.trans, B = P^T straight from the S accumulators (query vectors 0-7, and
+//                     8-15 in a second tile when the entry has more), P split into bf16 hi + lo parts so that the
+//                     weights keep ~16 mantissa bits (the reference keeps them in fp32)
+// V rows past the entry's last key are zeroed in shared memory before use (0 * stale data must stay 0).
 constexpr int kBlkTok = 16;
 constexpr int kMmaStages = 2;
 constexpr int kBoxBytes = kBlkTok * 128;   // 16 positions x 64 dims x bf16
 constexpr int kBlkBytes = 4 * kBoxBytes;   // K lo, K hi, V lo, V hi
+constexpr int kQueryVectors = 16;          // the mma tile's rows: query vectors per CTA
 
 struct MmaAttnSmem {
   unsigned char stage[4][kMmaStages][kBlkBytes];  // [warp][stage], every box 1024-byte aligned
@@ -306,25 +336,29 @@ struct MmaAttnSmem {
   int last;
 };
 constexpr int kMmaAttnSmemBytes = (int)sizeof(MmaAttnSmem) + 1024;  // + alignment slack
+static_assert(kMmaStages * kBlkBytes >= (kQueryVectors * kHeadDim + 2 * kQueryVectors) * 4,
+              "a warp's partial (O and m, l of 16 query vectors) fits in its stage buffers");
 
-template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
-    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
-    const int4* __restrict__ visit,
-    float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out,
-    int nsplit, int chunk, int H, float qscale, int* status) {
-  static_assert(G <= 8, "the query heads of one kv head fill at most 8 of the 16 mma rows");
-  extern __shared__ unsigned char smem_raw[];
-  MmaAttnSmem& sm =
-      *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int4 vis = visit[blockIdx.z];  // {row, slot, position}
+// One work entry (GROUP: a prompt group of nrows rows; else a decode row, whose arithmetic then has no trace of the
+// group path).
+template <int G, bool GROUP>
+__device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                           const bf16* __restrict__ q, const int4 vis, float* __restrict__ part_o,
+                                           float2* __restrict__ part_ml, int* __restrict__ tickets,
+                                           bf16* __restrict__ out, int nsplit, int chunk, int H, float qscale,
+                                           int* status) {
+  const int nrows = GROUP ? vis.w : 1;
   const int split = blockIdx.x, kvh = blockIdx.y, row = vis.x;
   const int KV = gridDim.y;
   const int pos = vis.z;
-  const int t0 = split * chunk;
+  if (GROUP && split > 0) return;      // a prompt group reads all of its keys in one CTA
+  const int t0 = GROUP ? 0 : split * chunk;
   if (t0 > pos) return;
-  const int ntok = min(chunk, pos + 1 - t0);
+  const int ntok = GROUP ? pos + 1 : min(chunk, pos + 1 - t0);
   const int nblk = cdiv(ntok, kBlkTok);
+  const int QV = nrows * G;
+  const int first = pos - (nrows - 1);  // position of the entry's first row
+  const bool hi = GROUP && QV > 8;      // query vectors 8-15 present (uniform over the CTA)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int zc = vis.y * KV + kvh;
@@ -341,28 +375,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     uint64_t* bar = &sm.bar[warp][i % kMmaStages];
     const int y = t0 + (warp + 4 * i) * kBlkTok;
     mbar_expect_tx(bar, kBlkBytes);
-    tma_load_3d(st, &kmap, 0, y, zc, bar);
-    tma_load_3d(st + kBoxBytes, &kmap, 64, y, zc, bar);
-    tma_load_3d(st + 2 * kBoxBytes, &vmap, 0, y, zc, bar);
-    tma_load_3d(st + 3 * kBoxBytes, &vmap, 64, y, zc, bar);
+    tma_load_3d(st, kmap, 0, y, zc, bar);
+    tma_load_3d(st + kBoxBytes, kmap, 64, y, zc, bar);
+    tma_load_3d(st + 2 * kBoxBytes, vmap, 0, y, zc, bar);
+    tma_load_3d(st + 3 * kBoxBytes, vmap, 64, y, zc, bar);
   };
   if (lane == 0)
     for (int i = 0; i < min(kMmaStages, nmine); ++i) issue(i);
 
-  // A fragments of Q (rows = query heads): a0 = Q[g][16ks + 2t, +1], a2 = Q[g][16ks + 8 + 2t, +1]; rows >= G zero
-  uint32_t qa[8][2];
+  // A fragments of Q: this lane holds mma rows g (a0, a2) and g + 8 (a1, a3), dims 16ks + 2t (+8); rows >= QV zero
+  uint32_t qa[8][4];
   {
-    const uint32_t* qp = reinterpret_cast<const uint32_t*>(q + ((int64_t)row * H + kvh * G + min(g, G - 1)) * kHeadDim);
+    const int v0 = min(g, QV - 1), v1 = min(g + 8, QV - 1);
+    const uint32_t* qp0 =
+        reinterpret_cast<const uint32_t*>(q + ((int64_t)(row + v0 / G) * H + kvh * G + v0 % G) * kHeadDim);
+    const uint32_t* qp1 =
+        reinterpret_cast<const uint32_t*>(q + ((int64_t)(row + v1 / G) * H + kvh * G + v1 % G) * kHeadDim);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = g < G ? qp[8 * ks + t] : 0u;
-      qa[ks][1] = g < G ? qp[8 * ks + 4 + t] : 0u;
+      qa[ks][0] = g < QV ? qp0[8 * ks + t] : 0u;
+      qa[ks][1] = GROUP && g + 8 < QV ? qp1[8 * ks + t] : 0u;
+      qa[ks][2] = g < QV ? qp0[8 * ks + 4 + t] : 0u;
+      qa[ks][3] = GROUP && g + 8 < QV ? qp1[8 * ks + 4 + t] : 0u;
     }
   }
-  float o[8][4];  // O^T tiles: o[mt] = rows (dims) 16mt + g, 16mt + 8 + g; columns (query heads) 2t, 2t + 1
+  // O^T tiles: o[mt] = rows (dims) 16mt + g, 16mt + 8 + g; columns query vectors 2t, 2t + 1 (o2: 8 + 2t, 8 + 2t + 1)
+  float o[8][4], o2[8][4];
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;  // of query head g, identical in the 4 lanes of quad g
+  for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[mt][e] = o2[mt][e] = 0.f;
+  // running max and denominator of query vectors g and g + 8, identical in the 4 lanes of quad g
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int lim0 = first + g / G, lim1 = first + (g + 8) / G;  // the last key each of the two may see
   bool timed_out = false;
   int i = 0;
   for (; i < nmine; ++i) {
@@ -384,60 +429,106 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     const uint32_t kb = smem_u32(st), vb = kb + 2 * kBoxBytes;
     const int j = lane >> 3;                           // ldmatrix: this lane addresses row (lane & 7) of matrix j
     const int lr = ((j >> 1) << 3) + (lane & 7), lc = j & 1;
-    // S = Q K^T over 16 positions: s[nt] = rows g (c0, c1) at positions nt*8 + 2t, +1
+    // S = Q K^T over 16 positions: s[nt] = rows g (c0, c1) and g + 8 (c2, c3) at positions nt*8 + 2t, +1
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t k0, k1, k2, k3;
       ldsm_x4(kb + (ks >> 2) * kBoxBytes + sw128(lr, ((ks & 3) << 1) + lc), k0, k1, k2, k3);
-      mma_bf16(s[0], qa[ks][0], 0u, qa[ks][1], 0u, k0, k1);
-      mma_bf16(s[1], qa[ks][0], 0u, qa[ks][1], 0u, k2, k3);
+      if constexpr (GROUP) {
+        mma_bf16(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], k0, k1);
+        mma_bf16(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], k2, k3);
+      } else {
+        mma_bf16(s[0], qa[ks][0], 0u, qa[ks][2], 0u, k0, k1);
+        mma_bf16(s[1], qa[ks][0], 0u, qa[ks][2], 0u, k2, k3);
+      }
     }
-    float p[2][2];
-    float mx = -INFINITY;
+    float p[2][4];
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const bool valid = g < G && b * kBlkTok + nt * 8 + 2 * t + e < ntok;
-        p[nt][e] = valid ? s[nt][e] * qscale : -INFINITY;
-        mx = fmaxf(mx, p[nt][e]);
+        const int kr = b * kBlkTok + nt * 8 + 2 * t + e;  // key index in the CTA's range
+        const bool in = kr < ntok;
+        const bool ok0 = g < QV && in && (!GROUP || t0 + kr <= lim0);
+        p[nt][e] = ok0 ? s[nt][e] * qscale : -INFINITY;
+        mx0 = fmaxf(mx0, p[nt][e]);
+        if constexpr (GROUP) {
+          const bool ok1 = g + 8 < QV && in && t0 + kr <= lim1;
+          p[nt][2 + e] = ok1 ? s[nt][2 + e] * qscale : -INFINITY;
+          mx1 = fmaxf(mx1, p[nt][2 + e]);
+        }
       }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    float r = 1.f;
-    if (mx > m_run + kLazyRescale) {
-      r = exp2f(m_run - mx);
-      m_run = mx;
-      l_run *= r;
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    float r0 = 1.f, r1 = 1.f;
+    if (mx0 > m_run[0] + kLazyRescale) {
+      r0 = exp2f(m_run[0] - mx0);
+      m_run[0] = mx0;
+      l_run[0] *= r0;
     }
-    if (__any_sync(0xffffffffu, r != 1.f)) {  // O^T column q lives in the lanes with t = q / 2
-      const float r0 = __shfl_sync(0xffffffffu, r, 8 * t), r1 = __shfl_sync(0xffffffffu, r, 8 * t + 4);
+    if constexpr (GROUP) {
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      if (mx1 > m_run[1] + kLazyRescale) {
+        r1 = exp2f(m_run[1] - mx1);
+        m_run[1] = mx1;
+        l_run[1] *= r1;
+      }
+    }
+    if (__any_sync(0xffffffffu, r0 != 1.f)) {  // O^T column v lives in the lanes with t = v / 2
+      const float ra = __shfl_sync(0xffffffffu, r0, 8 * t), rb = __shfl_sync(0xffffffffu, r0, 8 * t + 4);
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
-        o[mt][0] *= r0;
-        o[mt][1] *= r1;
-        o[mt][2] *= r0;
-        o[mt][3] *= r1;
+        o[mt][0] *= ra;
+        o[mt][1] *= rb;
+        o[mt][2] *= ra;
+        o[mt][3] *= rb;
+      }
+    }
+    if (hi && __any_sync(0xffffffffu, r1 != 1.f)) {
+      const float ra = __shfl_sync(0xffffffffu, r1, 8 * t), rb = __shfl_sync(0xffffffffu, r1, 8 * t + 4);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o2[mt][0] *= ra;
+        o2[mt][1] *= rb;
+        o2[mt][2] *= ra;
+        o2[mt][3] *= rb;
       }
     }
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        p[nt][e] = p[nt][e] == -INFINITY ? 0.f : exp2f(p[nt][e] - m_run);
-        l_run += p[nt][e];
+        p[nt][e] = p[nt][e] == -INFINITY ? 0.f : exp2f(p[nt][e] - m_run[0]);
+        l_run[0] += p[nt][e];
+        if constexpr (GROUP) {
+          p[nt][2 + e] = p[nt][2 + e] == -INFINITY ? 0.f : exp2f(p[nt][2 + e] - m_run[1]);
+          l_run[1] += p[nt][2 + e];
+        }
       }
     const uint32_t h0 = pack_bf2(p[0][0], p[0][1]), h1 = pack_bf2(p[1][0], p[1][1]);
     const uint32_t l0 = pack_bf2(p[0][0] - bf_lo_f(h0), p[0][1] - bf_hi_f(h0));
     const uint32_t l1 = pack_bf2(p[1][0] - bf_lo_f(h1), p[1][1] - bf_hi_f(h1));
-    // O^T += V^T P^T: per 16 dims, A = V^T (ldmatrix.trans of the V rows), B = P^T = {p[0], p[1]} of quad g
+    uint32_t h2 = 0u, h3 = 0u, l2 = 0u, l3 = 0u;
+    if constexpr (GROUP) {
+      h2 = pack_bf2(p[0][2], p[0][3]);
+      h3 = pack_bf2(p[1][2], p[1][3]);
+      l2 = pack_bf2(p[0][2] - bf_lo_f(h2), p[0][3] - bf_hi_f(h2));
+      l3 = pack_bf2(p[1][2] - bf_lo_f(h3), p[1][3] - bf_hi_f(h3));
+    }
+    // O^T += V^T P^T: per 16 dims, A = V^T (ldmatrix.trans of the V rows), B = P^T of quad g (rows g, then g + 8)
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       uint32_t a0, a1, a2, a3;
       ldsm_x4_t(vb + (mt >> 2) * kBoxBytes + sw128(lr, ((mt & 3) << 1) + lc), a0, a1, a2, a3);
       mma_bf16(o[mt], a0, a1, a2, a3, h0, h1);
       mma_bf16(o[mt], a0, a1, a2, a3, l0, l1);
+      if (hi) {
+        mma_bf16(o2[mt], a0, a1, a2, a3, h2, h3);
+        mma_bf16(o2[mt], a0, a1, a2, a3, l2, l3);
+      }
     }
     __syncwarp();
     if (lane == 0 && i + kMmaStages < nmine) issue(i + kMmaStages);
@@ -448,48 +539,86 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
         mbar_wait(&sm.bar[warp][k % kMmaStages], (k / kMmaStages) & 1, nullptr);
     __syncwarp();
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    m_run = -INFINITY;
-    l_run = 0.f;
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mt][e] = o2[mt][e] = 0.f;
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.f;
   }
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-  // the warp's partial, in its own (now idle) stage buffers: wo[G][128], wml[G][2]
+#pragma unroll
+  for (int h = 0; h < (GROUP ? 2 : 1); ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+  // the warp's partial, in its own (now idle) stage buffers: wo[16][128], wml[16][2]
   float* wo = reinterpret_cast<float*>(sm.stage[warp][0]);
-  float* wml = wo + G * kHeadDim;
+  float* wml = wo + kQueryVectors * kHeadDim;
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int qh = 2 * t + (e & 1);
-      if (qh < G) wo[qh * kHeadDim + 16 * mt + g + ((e >> 1) << 3)] = o[mt][e];
+      const int v = 2 * t + (e & 1), dim = 16 * mt + g + ((e >> 1) << 3);
+      if (v < QV) wo[v * kHeadDim + dim] = o[mt][e];
+      if (hi && 8 + v < QV) wo[(8 + v) * kHeadDim + dim] = o2[mt][e];
     }
-  if (t == 0 && g < G) {
-    wml[g * 2] = m_run;
-    wml[g * 2 + 1] = l_run;
+  if (t == 0) {
+    if (g < QV) {
+      wml[g * 2] = m_run[0];
+      wml[g * 2 + 1] = l_run[0];
+    }
+    if (GROUP && g + 8 < QV) {
+      wml[(g + 8) * 2] = m_run[1];
+      wml[(g + 8) * 2 + 1] = l_run[1];
+    }
   }
   __syncthreads();
-  float Og[G], Mg[G], Lg[G];
+  auto merged = [&](int v, float& O, float& M, float& L) {  // the 4 warps' partials of query vector v, dim tid
+    M = -INFINITY;
 #pragma unroll
-  for (int gg = 0; gg < G; ++gg) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, reinterpret_cast<const float*>(sm.stage[w][0])[G * kHeadDim + gg * 2]);
-    float O = 0.f, L = 0.f;
+    for (int w = 0; w < 4; ++w)
+      M = fmaxf(M, reinterpret_cast<const float*>(sm.stage[w][0])[kQueryVectors * kHeadDim + v * 2]);
+    O = 0.f;
+    L = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float* ww = reinterpret_cast<const float*>(sm.stage[w][0]);
-      const float mw = ww[G * kHeadDim + gg * 2];
+      const float mw = ww[kQueryVectors * kHeadDim + v * 2];
       const float sc = mw == -INFINITY ? 0.f : exp2f(mw - M);
-      O = fmaf(ww[gg * kHeadDim + tid], sc, O);
-      L = fmaf(ww[G * kHeadDim + gg * 2 + 1], sc, L);
+      O = fmaf(ww[v * kHeadDim + tid], sc, O);
+      L = fmaf(ww[kQueryVectors * kHeadDim + v * 2 + 1], sc, L);
     }
-    Og[gg] = O;
-    Mg[gg] = M;
-    Lg[gg] = L;
+  };
+  if constexpr (!GROUP) {
+    float Og[G], Mg[G], Lg[G];
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) merged(gg, Og[gg], Mg[gg], Lg[gg]);
+    split_epilogue<G>(Og, Mg, Lg, tid, row, kvh, KV, split, nsplit, min(nsplit, pos / chunk + 1), part_o, part_ml,
+                      tickets, out, H, &sm.last);
+  } else {  // one split: every query vector's output directly
+    for (int v = 0; v < QV; ++v) {
+      float O, M, L;
+      merged(v, O, M, L);
+      out[((int64_t)(row + v / G) * H + kvh * G + v % G) * kHeadDim + tid] = to_bf(L > 0.f ? O / L : 0.f);
+    }
   }
-  split_epilogue<G>(Og, Mg, Lg, tid, row, kvh, KV, split, nsplit, min(nsplit, pos / chunk + 1), part_o, part_ml,
-                    tickets, out, H, &sm.last);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
+    const int4* __restrict__ visit,
+    float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out,
+    int nsplit, int chunk, int H, float qscale, int* status) {
+  static_assert(G <= 8 && kQueryVectors % G == 0, "the query heads of one kv head fill at most 8 of the 16 mma rows");
+  extern __shared__ unsigned char smem_raw[];
+  MmaAttnSmem& sm =
+      *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int4 vis = visit[blockIdx.z];  // {first row, slot, last position, rows}
+  if (vis.w == 0) return;              // inside a prompt group: the group's first row carries the work
+  if (vis.w > 1)
+    attn_entry<G, true>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status);
+  else
+    attn_entry<G, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status);
 }
 
 }  // namespace m3
@@ -728,8 +857,8 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
   bb->rows_written = std::max(bb->rows_written, (int)rows);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int Hd = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
-  M3_TRY(launch_prep_rows(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity, bb->slot32, bb->pos32,
-                          bb->visit, bb->status, s));
+  M3_TRY(launch_prep_rows(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity,
+                          kQueryVectors / (c.heads / c.kv_heads), bb->slot32, bb->pos32, bb->visit, bb->status, s));
   const bf16* xin = reinterpret_cast<const bf16*>(x);
   for (int i = 0; i < c.layers; ++i) {
     if (i == 0) {

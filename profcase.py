@@ -140,9 +140,9 @@ def overlap(a):
     dev = torch.device("cuda", 0)
     g = BASELINE
     W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
-    sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats,), ctx_buckets=(2048,), use_graphs=True,
+    sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats, 512), ctx_buckets=(2048,), use_graphs=True,
                         geom=g.backbone, device=dev)
-    if a.with_ in ("depth", "depth+mimi"):
+    if a.with_ in ("depth", "depth+mimi", "prefill+depth"):
         fd = FastDepth(W, a.seats, batch_buckets=(a.seats,), geom=g.depth, device=dev)
         hd = torch.randn(a.seats, g.depth.d_backbone, device=dev, dtype=torch.bfloat16)
         cb0 = torch.randint(0, 2048, (a.seats,), device=dev)
@@ -151,6 +151,13 @@ def overlap(a):
     if a.with_ == "depth+mimi":
         codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
         first, other = other, (lambda: codec.decode(idx, codes))
+    if a.with_ == "prefill+depth":     # slot `seats - 1` is emptied and refilled with the prompt every call
+        xp = torch.randn(a.prompt, g.backbone.hidden, device=dev, dtype=torch.bfloat16)
+
+        def first():
+            sb.free(a.seats - 1)
+            for c0 in range(0, a.prompt, 512):
+                sb.step_mixed([], None, [(a.seats - 1, xp[c0:c0 + 512])])
     elif a.with_ == "mimi":
         codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
         other = lambda: codec.decode(idx, codes)
@@ -166,7 +173,7 @@ def overlap(a):
     x = torch.randn(a.seats, g.backbone.hidden, device=dev, dtype=torch.bfloat16)
     codes = torch.randint(0, 2048, (a.seats, g.mimi.n_q), device=dev)
     idx = torch.arange(a.seats, device=dev)
-    if a.with_ != "depth+mimi":
+    if a.with_ not in ("depth+mimi", "prefill+depth"):
         first = lambda: sb.step(slots, x)
     first()
     other()
@@ -189,7 +196,7 @@ def overlap(a):
             cur.wait_stream(s2)
         e1.record()
         torch.cuda.synchronize()
-        if a.with_ != "depth+mimi":       # the backbone steps advanced every slot's length
+        if a.with_ not in ("depth+mimi", "prefill+depth"):   # the backbone steps advanced every slot's length
             for s in range(a.seats):
                 sb.lengths_cpu[s] -= reps
             sb.lengths[:a.seats] -= reps
@@ -206,12 +213,12 @@ def overlap(a):
         return e0.elapsed_time(e1) / reps
 
     t_bb = alone(first)
-    if a.with_ != "depth+mimi":
+    if a.with_ not in ("depth+mimi", "prefill+depth"):
         sb.lengths[:a.seats] -= 10
         for s in range(a.seats):
             sb.lengths_cpu[s] -= 10
     t_other = alone(other)
-    name = "depth" if a.with_ == "depth+mimi" else "backbone step"
+    name = {"depth+mimi": "depth", "prefill+depth": f"prefill of {a.prompt}"}.get(a.with_, "backbone step")
     print(f"seats {a.seats}: {name} {t_bb:.3f} ms, {a.with_.split('+')[-1]} {t_other:.3f} ms, sequential "
           f"{run(False):.3f} ms, concurrent {run(True):.3f} ms")
 
@@ -325,9 +332,11 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     ap.add_argument("--cold", action="store_true", help="gemm: stream the weights from HBM on every launch")
-    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth", "depth+mimi"),
+    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth", "depth+mimi", "prefill+depth"),
                     help="overlap: the stage run beside the backbone step (depth+mimi: the Mimi decode beside the "
-                         "depth loop, no backbone)")
+                         "depth loop; prefill+depth: a backbone prefill of --prompt positions in one free slot "
+                         "beside the depth loop)")
+    ap.add_argument("--prompt", type=int, default=350, help="overlap prefill+depth: prompt positions prefilled")
     a = ap.parse_args()
     {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap,
      "guard": guard}[a.case](a)
