@@ -421,7 +421,16 @@ struct m3_depth {
   bf16 *prefix = nullptr, *x = nullptr, *x2 = nullptr, *y = nullptr, *qkvb = nullptr, *a = nullptr, *ob = nullptr,
        *ff = nullptr, *logits = nullptr, *proj = nullptr, *kvbuf = nullptr, *spk = nullptr;
   bf16* dbg_logits = nullptr;  // m3_depth_debug_logits: every level's head output kept for inspection
+  // the handle's own cuBLAS workspace: two depth handles may run their level loops on two streams at once
+  unsigned char* blas_ws = nullptr;
 };
+
+// Every GEMM of the level loop runs on the handle's own cuBLAS workspace.
+static int dgemm(const m3_depth* d, GemmDesc g, cudaStream_t s) {
+  g.ws = d->blas_ws;
+  g.ws_bytes = kBlasWorkspace;
+  return gemm(g, s);
+}
 
 namespace {
 template <class T>
@@ -484,6 +493,7 @@ extern "C" int m3_depth_create(const m3_depth_config* cfg, const m3_depth_weight
   add(R * D * 2);               // proj
   add((size_t)c.layers * R * NL * 2 * D * 2);  // kvbuf
   add(4 * D * 2);               // speaker scratch
+  add(kBlasWorkspace);          // the handle's own cuBLAS workspace
   cudaError_t e = cudaMalloc(&d->ws, bytes);
   if (e != cudaSuccess) {
     delete d;
@@ -506,6 +516,7 @@ extern "C" int m3_depth_create(const m3_depth_config* cfg, const m3_depth_weight
   d->proj = carve<bf16>(p, R * D);
   d->kvbuf = carve<bf16>(p, (size_t)c.layers * R * NL * 2 * D);
   d->spk = carve<bf16>(p, 4 * D);
+  d->blas_ws = carve<unsigned char>(p, kBlasWorkspace);
   cudaMemset(d->status, 0, 256);
   *out = d;
   return M3_OK;
@@ -547,8 +558,8 @@ extern "C" int m3_depth_set_speaker(m3_depth* d, int32_t slot, const void* mem, 
       continue;
     }
     // kv = kv(mem) (bf16), v = second half; cross = o(v)   (serve/fast_depth.py:80-82)
-    M3_TRY(gemm({(const bf16*)mem, D, d->cross_kv[li], D, d->spk, 2 * D, 1, 2 * D, D, false}, s));
-    M3_TRY(gemm({d->spk + D, D, d->cross_o[li], D, dst, D, 1, D, D, false}, s));
+    M3_TRY(dgemm(d, {(const bf16*)mem, D, d->cross_kv[li], D, d->spk, 2 * D, 1, 2 * D, D, false}, s));
+    M3_TRY(dgemm(d, {d->spk + D, D, d->cross_o[li], D, dst, D, 1, D, D, false}, s));
   }
   return M3_OK;
 }
@@ -566,7 +577,7 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
   depth_prep_kernel<<<cdiv(R, 128), 128, 0, s>>>(slots, cb0, R, c.max_slots, c.n_codes, d->slot32, d->cb032, codes,
                                                  NL, d->status);
   M3_LAUNCHED();
-  M3_TRY(gemm({(const bf16*)h, c.d_backbone, d->in_proj, c.d_backbone, d->proj, D, R, D, c.d_backbone, false}, s));
+  M3_TRY(dgemm(d, {(const bf16*)h, c.d_backbone, d->in_proj, c.d_backbone, d->proj, D, R, D, c.d_backbone, false}, s));
   prefix_init_kernel<<<R, 128, 0, s>>>(d->proj, d->level0, d->embed, d->cb032, d->prefix, NL, D);
   M3_LAUNCHED();
   const int64_t kv_layer = (int64_t)R * NL * 2 * D;
@@ -586,7 +597,7 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
                            d->x, d->y, d->n1_w[gl], d->n1_b[gl], c.ln_eps, D, s));
     int Tr = T;  // rows per seat in the residual stream
     for (int li = 0; li < L; ++li) {
-      M3_TRY(gemm({d->y, D, d->qkv[gl + li], D, d->qkvb, 3 * D, R * Tr, 3 * D, D, false}, s));
+      M3_TRY(dgemm(d, {d->y, D, d->qkv[gl + li], D, d->qkvb, 3 * D, R * Tr, 3 * D, D, false}, s));
       bf16* kvl = d->kvbuf + li * kv_layer;
       int Tq = Tr, q0 = start;
       KeySrc ks;
@@ -616,7 +627,7 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
       else
         depth_attn_kernel<1><<<ag, 32 * Tq, 0, s>>>(d->qkvb, Tr, q0, Tq, ks, H, scale, d->a);
       M3_LAUNCHED();
-      M3_TRY(gemm({d->a, D, d->o[gl + li], D, d->ob, D, R * Tq, D, D, false}, s));
+      M3_TRY(dgemm(d, {d->a, D, d->o[gl + li], D, d->ob, D, R * Tq, D, D, false}, s));
       if (Tq != Tr) {
         // the last layer keeps only each seat's final position (x = x[:, -1:], serve/fast_depth.py:181): the
         // residual add reads row Tr-1 of each seat's block and writes the compact stream
@@ -629,11 +640,11 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
         M3_TRY(launch_add_ln(R * Tr, d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
                              d->n2_b[gl + li], c.ln_eps, D, s));
       }
-      M3_TRY(gemm({d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
+      M3_TRY(dgemm(d, {d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
       const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
       gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);
       M3_LAUNCHED();
-      M3_TRY(gemm({d->ff, c.ffn, d->f2[gl + li], c.ffn, d->ob, D, R * Tr, D, c.ffn, false}, s));
+      M3_TRY(dgemm(d, {d->ff, c.ffn, d->f2[gl + li], c.ffn, d->ob, D, R * Tr, D, c.ffn, false}, s));
       // x, y = add_ln(x, f, next n1 (or the final norm), cross[slot][li])
       const bf16* nw = li + 1 < L ? d->n1_w[gl + li + 1] : d->norm_w;
       const bf16* nb = li + 1 < L ? d->n1_b[gl + li + 1] : d->norm_b;
@@ -642,7 +653,7 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
     }
     // level head on the final position, then sample and write the next prefix row
     bf16* lg = d->dbg_logits ? d->dbg_logits + (int64_t)(level - 1) * c.max_rows * c.n_codes : d->logits;
-    M3_TRY(gemm({d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, lg, c.n_codes, R,
+    M3_TRY(dgemm(d, {d->y + (int64_t)(Tr - 1) * D, (int64_t)Tr * D, d->heads[level - 1], D, lg, c.n_codes, R,
                  c.n_codes, D, false},
                 s));
     const bool more = n < NL;

@@ -142,12 +142,20 @@ def overlap(a):
     W = WG.generate({k: v for k, v in WG.all_shapes(g).items() if k != "model.embed_tokens.weight"}, device=dev)
     sb = StaticBackbone(W, a.seats, capacity=2048, batch_buckets=(a.seats, 512), ctx_buckets=(2048,), use_graphs=True,
                         geom=g.backbone, device=dev)
-    if a.with_ in ("depth", "depth+mimi", "prefill+depth"):
+    if a.with_ in ("depth", "depth+mimi", "prefill+depth", "depth-halves"):
         fd = FastDepth(W, a.seats, batch_buckets=(a.seats,), geom=g.depth, device=dev)
         hd = torch.randn(a.seats, g.depth.d_backbone, device=dev, dtype=torch.bfloat16)
         cb0 = torch.randint(0, 2048, (a.seats,), device=dev)
         dslots = list(range(a.seats))
         other = lambda: fd(dslots, hd, cb0)
+    if a.with_ == "depth-halves":
+        hs = a.seats // 2
+        fa = FastDepth(W, a.seats, batch_buckets=(hs,), geom=g.depth, device=dev)
+        fb = FastDepth(W, a.seats, batch_buckets=(hs,), geom=g.depth, device=dev)
+        full = other
+        first = lambda: fa(dslots[:hs], hd[:hs], cb0[:hs])
+        other = lambda: fb(dslots[hs:], hd[hs:], cb0[hs:])
+        t_full = None
     if a.with_ == "depth+mimi":
         codec = StaticMimi(W, a.seats, batch_buckets=(a.seats,), geom=g.mimi, device=dev)
         first, other = other, (lambda: codec.decode(idx, codes))
@@ -173,7 +181,7 @@ def overlap(a):
     x = torch.randn(a.seats, g.backbone.hidden, device=dev, dtype=torch.bfloat16)
     codes = torch.randint(0, 2048, (a.seats, g.mimi.n_q), device=dev)
     idx = torch.arange(a.seats, device=dev)
-    if a.with_ not in ("depth+mimi", "prefill+depth"):
+    if a.with_ not in ("depth+mimi", "prefill+depth", "depth-halves"):
         first = lambda: sb.step(slots, x)
     first()
     other()
@@ -196,7 +204,7 @@ def overlap(a):
             cur.wait_stream(s2)
         e1.record()
         torch.cuda.synchronize()
-        if a.with_ not in ("depth+mimi", "prefill+depth"):   # the backbone steps advanced every slot's length
+        if a.with_ not in ("depth+mimi", "prefill+depth", "depth-halves"):   # the backbone steps advanced lengths
             for s in range(a.seats):
                 sb.lengths_cpu[s] -= reps
             sb.lengths[:a.seats] -= reps
@@ -213,12 +221,15 @@ def overlap(a):
         return e0.elapsed_time(e1) / reps
 
     t_bb = alone(first)
-    if a.with_ not in ("depth+mimi", "prefill+depth"):
+    if a.with_ not in ("depth+mimi", "prefill+depth", "depth-halves"):
         sb.lengths[:a.seats] -= 10
         for s in range(a.seats):
             sb.lengths_cpu[s] -= 10
     t_other = alone(other)
-    name = {"depth+mimi": "depth", "prefill+depth": f"prefill of {a.prompt}"}.get(a.with_, "backbone step")
+    name = {"depth+mimi": "depth", "prefill+depth": f"prefill of {a.prompt}",
+            "depth-halves": f"depth of {a.seats // 2}"}.get(a.with_, "backbone step")
+    if a.with_ == "depth-halves":
+        print(f"depth of all {a.seats} seats on one handle: {alone(full):.3f} ms")
     print(f"seats {a.seats}: {name} {t_bb:.3f} ms, {a.with_.split('+')[-1]} {t_other:.3f} ms, sequential "
           f"{run(False):.3f} ms, concurrent {run(True):.3f} ms")
 
@@ -332,10 +343,12 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--shape", default="", help="gemm: only this layer of the table (e.g. 'depth.qkv n8')")
     ap.add_argument("--cold", action="store_true", help="gemm: stream the weights from HBM on every launch")
-    ap.add_argument("--with", dest="with_", default="mimi", choices=("mimi", "depth", "depth+mimi", "prefill+depth"),
+    ap.add_argument("--with", dest="with_", default="mimi",
+                    choices=("mimi", "depth", "depth+mimi", "prefill+depth", "depth-halves"),
                     help="overlap: the stage run beside the backbone step (depth+mimi: the Mimi decode beside the "
                          "depth loop; prefill+depth: a backbone prefill of --prompt positions in one free slot "
-                         "beside the depth loop)")
+                         "beside the depth loop; depth-halves: the depth loops of two seat halves, each on its own "
+                         "FastDepth handle, beside each other)")
     ap.add_argument("--prompt", type=int, default=350, help="overlap prefill+depth: prompt positions prefilled")
     a = ap.parse_args()
     {"attention": attention, "tick": tick, "gemm": gemm, "mimi": mimi, "gaps": gaps, "overlap": overlap,
