@@ -129,6 +129,11 @@ M3_API int m3_backbone_load_prefix(m3_backbone* bb, int32_t slot, const void* st
  * on the live cache (rows beyond any step's are rejected with M3_ERR_RANGE).  Overwrites only the handle's attention
  * output scratch. */
 M3_API int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream);
+/* The attention of m3_backbone_attention with every K/V stage barrier expecting 16 bytes more than its copies bring
+ * (rows <= 8), so that every wait in the launch runs out: a test of the kernel's bounded waits, which here give up
+ * after 1000 polls each.  The launch ends by itself, its output rows are zero, M3_DEV_TIMEOUT is in the handle's
+ * status (m3_backbone_status) and the context stays usable. */
+M3_API int m3_backbone_attention_selftest(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream);
 
 /* ---------------------------------------------------------------------------------------------- cb0 sampler */
 /* Replaces Engine._cb0 + Backbone.cb0_logits + row_exponential (maya3/engine.py:652-694,

@@ -100,6 +100,7 @@ SIGNATURES = {
     "m3_backbone_step": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, vp]),
     "m3_backbone_status": (C.c_int, [vp, P(i32), i32]),
     "m3_backbone_attention": (C.c_int, [vp, i32, i32, i32, vp]),
+    "m3_backbone_attention_selftest": (C.c_int, [vp, i32, i32, i32, vp]),
     "m3_cb0_create": (C.c_int, [P(Cb0Config), P(Cb0State), P(vp)]),
     "m3_cb0_destroy": (C.c_int, [vp]),
     "m3_cb0_step": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),

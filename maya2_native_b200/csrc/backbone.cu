@@ -329,6 +329,7 @@ constexpr int kMmaStages = 2;
 constexpr int kBoxBytes = kBlkTok * 128;   // 16 positions x 64 dims x bf16
 constexpr int kBlkBytes = 4 * kBoxBytes;   // K lo, K hi, V lo, V hi
 constexpr int kQueryVectors = 16;          // the mma tile's rows: query vectors per CTA
+constexpr uint32_t kSelftestPolls = 1000;  // m3_backbone_attention_selftest: polls before a wait gives up
 
 struct MmaAttnSmem {
   unsigned char stage[4][kMmaStages][kBlkBytes];  // [warp][stage], every box 1024-byte aligned
@@ -346,7 +347,7 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
                                            const bf16* __restrict__ q, const int4 vis, float* __restrict__ part_o,
                                            float2* __restrict__ part_ml, int* __restrict__ tickets,
                                            bf16* __restrict__ out, int nsplit, int chunk, int H, float qscale,
-                                           int* status) {
+                                           int* status, int extra_tx) {
   const int nrows = GROUP ? vis.w : 1;
   const int split = blockIdx.x, kvh = blockIdx.y, row = vis.x;
   const int KV = gridDim.y;
@@ -363,6 +364,7 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
   const int g = lane >> 2, t = lane & 3;
   const int zc = vis.y * KV + kvh;
   const int nmine = warp < nblk ? (nblk - 1 - warp) / 4 + 1 : 0;  // blocks warp, warp + 4, ...
+  const uint32_t polls = extra_tx ? kSelftestPolls : kSpinLimit;  // the self-test's waits give up sooner
 
   if (tid == 0) {
     for (int w = 0; w < 4; ++w)
@@ -374,7 +376,7 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
     unsigned char* st = sm.stage[warp][i % kMmaStages];
     uint64_t* bar = &sm.bar[warp][i % kMmaStages];
     const int y = t0 + (warp + 4 * i) * kBlkTok;
-    mbar_expect_tx(bar, kBlkBytes);
+    mbar_expect_tx(bar, kBlkBytes + extra_tx);
     tma_load_3d(st, kmap, 0, y, zc, bar);
     tma_load_3d(st + kBoxBytes, kmap, 64, y, zc, bar);
     tma_load_3d(st + 2 * kBoxBytes, vmap, 0, y, zc, bar);
@@ -412,7 +414,7 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
   int i = 0;
   for (; i < nmine; ++i) {
     const int stg = i % kMmaStages;
-    const bool got = mbar_wait(&sm.bar[warp][stg], (i / kMmaStages) & 1, status);
+    const bool got = mbar_wait(&sm.bar[warp][stg], (i / kMmaStages) & 1, status, polls);
     if (!__all_sync(0xffffffffu, got)) {
       timed_out = true;
       break;
@@ -536,7 +538,7 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
   if (timed_out) {  // drain this warp's copies still in flight (bounded) before its buffers are reused
     if (lane == 0)
       for (int k = i; k < min(nmine, i + kMmaStages); ++k)
-        mbar_wait(&sm.bar[warp][k % kMmaStages], (k / kMmaStages) & 1, nullptr);
+        mbar_wait(&sm.bar[warp][k % kMmaStages], (k / kMmaStages) & 1, nullptr, polls);
     __syncwarp();
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt)
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
     const int4* __restrict__ visit,
     float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out,
-    int nsplit, int chunk, int H, float qscale, int* status) {
+    int nsplit, int chunk, int H, float qscale, int* status, int extra_tx) {
   static_assert(G <= 8 && kQueryVectors % G == 0, "the query heads of one kv head fill at most 8 of the 16 mma rows");
   extern __shared__ unsigned char smem_raw[];
   MmaAttnSmem& sm =
@@ -616,9 +618,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
   const int4 vis = visit[blockIdx.z];  // {first row, slot, last position, rows}
   if (vis.w == 0) return;              // inside a prompt group: the group's first row carries the work
   if (vis.w > 1)
-    attn_entry<G, true>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status);
+    attn_entry<G, true>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status,
+                        extra_tx);
   else
-    attn_entry<G, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status);
+    attn_entry<G, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status,
+                         extra_tx);
 }
 
 }  // namespace m3
@@ -823,7 +827,8 @@ extern "C" int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clea
   return M3_OK;
 }
 
-static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s) {
+// extra_tx: bytes each K/V stage barrier expects beyond its copies; 0 except in m3_backbone_attention_selftest.
+static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s, int extra_tx = 0) {
   const m3_backbone_config& c = bb->c;
   const int G = c.heads / c.kv_heads;
   const int chunk = choose_chunk(rows, ctx, c.kv_heads, bb->max_split);
@@ -834,7 +839,7 @@ static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t
   attn_mma_kernel<GG><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                         \
       bb->kmap[layer], bb->vmap[layer], bb->q, bb->visit, bb->part_o, bb->part_ml,    \
       bb->tickets,                                                                                             \
-      bb->o, nsplit, chunk, c.heads, qscale, bb->status);
+      bb->o, nsplit, chunk, c.heads, qscale, bb->status, extra_tx);
   if (G == 1) {
     M3_ATTN(1)
   } else if (G == 2) {
@@ -899,6 +904,15 @@ extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t row
   M3_REQUIRE(rows <= bb->rows_written, M3_ERR_RANGE,
              "m3_backbone_attention: rows %d beyond the %d rows a backbone step has set up", rows, bb->rows_written);
   return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int m3_backbone_attention_selftest(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx,
+                                              m3_stream stream) {
+  M3_REQUIRE(bb, M3_ERR_ARG, "m3_backbone_attention_selftest: null handle");
+  M3_REQUIRE(layer >= 0 && layer < bb->c.layers && rows > 0 && rows <= bb->rows_written && rows <= 8 && ctx > 0 &&
+                 ctx <= bb->c.capacity,
+             M3_ERR_RANGE, "m3_backbone_attention_selftest: layer %d rows %d ctx %d out of range", layer, rows, ctx);
+  return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream), 16);
 }
 
 static int prefix_copy(m3_backbone* bb, int32_t slot, void* store, int32_t length, int save, m3_stream stream) {

@@ -26,6 +26,29 @@ def test_bounded_wait_gives_up_and_reports(cuda):
     assert float(x.sum()) == 28.0
 
 
+def test_attention_waits_run_out_and_report(cuda):
+    """The decode attention's own bounded waits (m3_backbone_attention_selftest: every K/V stage barrier expects 16
+    bytes more than its copies bring, so every wait runs out): the launch ends by itself, the handle's status reads
+    M3_DEV_TIMEOUT, and the same context then steps exactly as a backbone that never timed out."""
+    g = TINY.backbone
+    W = WG.backbone_weights(g)
+    mk = lambda: StaticBackbone(W, 2, capacity=64, ctx_buckets=(64,), batch_buckets=(1, 2), use_graphs=False, geom=g,
+                                device=cuda)
+    a, b = mk(), mk()
+    x1 = torch.randn(2, g.hidden, device=cuda, dtype=torch.bfloat16)
+    x2 = torch.randn(2, g.hidden, device=cuda, dtype=torch.bfloat16)
+    for sb in (a, b):
+        sb.step([0, 1], x1)
+    L.check(L.load().m3_backbone_attention_selftest(a._handle, 0, 2, 64, L.stream_ptr()),
+            "m3_backbone_attention_selftest")
+    torch.cuda.synchronize()
+    assert a.device_status() == DEV_TIMEOUT
+    assert a.device_status() == 0                       # read and cleared
+    ya, yb = a.step([0, 1], x2), b.step([0, 1], x2)
+    assert torch.equal(ya, yb)
+    assert a.device_status() == 0 and b.device_status() == 0
+
+
 def _raw_step(sb, slots, x, ctx):
     """m3_backbone_step through the C ABI, without the mirror's host-side slot validation."""
     rows = len(slots)
