@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(128) convt_umma_kernel(
 // written).  The bias of the CTA's columns is staged once in shared memory.  Each CTA allocates 2 x 128 TMEM
 // columns: releasing a larger allocation at exit measured several microseconds slower.
 constexpr int kCpEpiWarps = 8;
-constexpr int kCpCtl = 2048;  // barriers, TMEM address and the bias row ahead of the staging blocks
+constexpr int kCpCtl = 2048;  // barriers, TMEM address, the bias row and the tail rows ahead of the staging blocks
+constexpr int kCpTailStage = 1024;  // offset of the epilogue warps' tail rows in the control block
 constexpr int kCpThreads = 64 + 32 * kCpEpiWarps;
 constexpr int kCpStages = 4;
 
@@ -180,6 +181,8 @@ __global__ void __launch_bounds__(kCpThreads, 1) convt_pers_kernel(
   constexpr int kA = kUM * 64 * 2, kBt = BN * 64 * 2, CB = KT / 2;
   constexpr int kCols = 2 * BN;
   static_assert(kCols == 256 || kCols == 512, "two accumulators of 128 or 256 columns");
+  static_assert(256 + BN * 4 <= kCpTailStage && kCpTailStage + kCpEpiWarps * BN <= kCpCtl,
+                "bias row and tail rows fit the control block");
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = align1024(smem_raw);
   unsigned char* bres = base;                       // [KT][BN rows x 128 B] resident weights
@@ -272,14 +275,24 @@ __global__ void __launch_bounds__(kCpThreads, 1) convt_pers_kernel(
   } else {  // epilogue warps: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows, columns of half (w - 2) / 4
     const int lane_base = (warp & 3) * 32, cbeg = ((warp - 2) / 4) * (BN / 2);
     unsigned char* stg = stg_all + (warp - 2) * 4096;
+    // this warp's 64 columns of the previous frame's tail (row 0's addend), staged in the control block
+    bf16* tail_s = reinterpret_cast<bf16*>(ctl + kCpTailStage + (warp - 2) * (BN / 2) * 2);
     int lt = 0, nst = 0;
     for (int j = li; j < tiles; j += cpc, ++lt) {
       const int acc = lt & 1;
+      const int b = j / TT, t0 = (j % TT) * kUM, t = t0 + lane_base + lane;
+      // global reads the epilogue needs are issued before the wait for the accumulator, which hides their latency:
+      // the stream's slot (row L's state write) and, in the warp holding row 0, the previous frame's tail
+      const int slot = slot32[b];
+      const bool row0 = t0 == 0 && lane_base == 0;
+      uint32_t tail2 = 0u;
+      if (row0) tail2 = *reinterpret_cast<const uint32_t*>(tail_in + (int64_t)b * in_row + n0 + cbeg + 2 * lane);
       const bool got = mbar_wait(&tfull[acc], (lt >> 1) & 1, status);
       if (!__all_sync(0xffffffffu, got)) break;
       tmem_fence_after();
-      const int b = j / TT, t0 = (j % TT) * kUM, t = t0 + lane_base + lane;
-      bf16* st = state + (int64_t)slot32[b] * state_row + tail_off;
+      if (row0) reinterpret_cast<uint32_t*>(tail_s)[lane] = tail2;
+      __syncwarp();
+      bf16* st = state + (int64_t)slot * state_row + tail_off;
       // one 32-column chunk: bias, the row-0 tail / row-L state special cases, the swizzled staging block, one TMA
       // store of its 32 rows (the store of the chunk before last must have read its buffer)
       auto chunk = [&](const uint32_t (&v32)[32], int c0) {
@@ -301,7 +314,7 @@ __global__ void __launch_bounds__(kCpThreads, 1) convt_pers_kernel(
             }
             if (t == 0) {  // bf16(bf16(z + b) + previous tail)
               float tv[8];
-              unpack8(*reinterpret_cast<const uint4*>(tail_in + (int64_t)b * in_row + n + q * 8), tv);
+              unpack8(*reinterpret_cast<const uint4*>(tail_s + (c0 - cbeg) + q * 8), tv);
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] = rbf(v[e]) + tv[e];
             }

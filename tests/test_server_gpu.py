@@ -1,5 +1,6 @@
-"""The HTTP / WebSocket front over a real engine replica on the GPU: a request's PCM over HTTP (and over the
-WebSocket) is byte for byte what the same engine configuration delivers to the same request driven directly
+"""The HTTP / WebSocket front over a real engine replica on the GPU (its engine thread on the synchronous or the
+pipelined loop): a request's PCM over HTTP (and over the WebSocket) is byte for byte what the same engine
+configuration delivers to the same request driven directly
 through TickEngine (seeded sampler streams, maya3/engine.py:430-433), with per-request cb0 sampling overrides --
 temperature, top-k and top-p, the last of which switches the captured tick to its top-p form."""
 import asyncio
@@ -38,11 +39,12 @@ def direct(W, cuda, ids, sampling, frames):
     return pcm, s.stop
 
 
-def test_server_streams_the_engine_pcm(cuda):
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_server_streams_the_engine_pcm(cuda, pipelined):
     W = {k: v.to(cuda) for k, v in WG.generate(WG.all_shapes(TINY), seed=5).items()}
     ids = np.random.default_rng(1).integers(0, TINY.backbone.vocab, 9).tolist()
     want = [direct(W, cuda, ids, sp, n) for sp, n in REQS]
-    srv = Maya3Server([Replica(engine(W, cuda), name="gpu0")], vocab=TINY.backbone.vocab)
+    srv = Maya3Server([Replica(engine(W, cuda), name="gpu0", pipelined=pipelined)], vocab=TINY.backbone.vocab)
 
     async def http(c, sp, n):
         r = await c.post("/v1/audio/speech", json={"input_ids": ids, "max_frames": n, "response_format": "pcm", **sp})
