@@ -97,8 +97,16 @@ def test_grouped_levels_incremental_path(cuda):
 
 @pytest.mark.parametrize("greedy", [True, False])
 def test_baseline_geometry_against_oracle(cuda, greedy):
-    acc, err = _oracle_vs_gpu(BASELINE.depth, cuda, B=8, frames=3, greedy=greedy)
-    assert acc >= 0.95 and err < 2e-2
+    """8 seats x 25 frames x 7 levels at the benchmark geometry, each level from the GPU's own prefix (a flip at one
+    level does not carry into the next), greedy and sampled (per-seat Philox streams): at least 98% of the decisions
+    agree with the bf16-emulating oracle, as over 200 frames below; greedy flips are near ties in the oracle's own
+    logits."""
+    res = _oracle_vs_gpu(BASELINE.depth, cuda, B=8, frames=25, greedy=greedy, seed=11, forced=True)
+    acc, err = res[0], res[1]
+    print(f"benchmark-geometry depth agreement ({'greedy' if greedy else 'sampled'}): {acc:.4f}")
+    assert acc >= 0.98 and err < 2e-2, (acc, err)
+    if greedy:
+        assert res[2] <= 2.0 ** -6, res[2]
 
 
 def test_baseline_geometry_greedy_agreement_over_200_frames(cuda):
