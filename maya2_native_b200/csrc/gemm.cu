@@ -1,7 +1,7 @@
 // Linear layers: Y[M,N] = X[M,K] . W[N,K]^T with bf16 operands and fp32 accumulation.
 //
 // Small M (a handful of seats) is weight-bandwidth bound: a GEMV kernel streams each weight row once with 16-byte
-// loads and keeps the few activation rows in shared memory.  Larger M goes to cuBLAS (a plain library GEMM): three
+// loads, several in flight per lane, over enough CTAs to cover every SM.  Larger M goes to cuBLAS (a plain library GEMM): three
 // tcgen05 designs of this library's own were built and measured slower than it on the tick's shapes (a persistent
 // warp-specialised kernel, a cluster split-K kernel for M <= 256, and a swap-AB kernel with 128 weight rows per MMA
 // tile and fused norm / RoPE / SwiGLU epilogues), so the choice is a fixed function of M alone.
@@ -16,62 +16,68 @@
 namespace m3 {
 
 // ------------------------------------------------------------------------------------------------ GEMV
-// One warp produces kCols consecutive output columns for all MT rows.  Lanes split K in 8-element (16 B) chunks.
-constexpr int kGemvWarps = 8;
-constexpr int kCols = 4;
+// One warp produces COLS consecutive output columns for all MT rows; lanes split K in 8-element (16 B) chunks, lane l
+// taking chunks l, l + 32, ...  A CTA is kGemvWarps warps, so even a 1024-wide layer runs 256 CTAs over the 148 SMs,
+// and each lane keeps kGemvUnroll chunks of every column's weight row in flight: the weight stream is bound by HBM,
+// not by the few CTAs a wider column block would give.  The activation rows (at most 8 x K, read by every warp) come
+// through the read-only data cache.  Per output the chunks are accumulated in order and reduced across the warp by
+// the same shuffle tree at any MT or COLS.
+constexpr int kGemvWarps = 4;
+constexpr int kGemvUnroll = 4;
 
-template <int MT, bool OUT_F32>
+template <int MT, int COLS, bool OUT_F32>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __restrict__ X, int64_t ldx,
                                                                const bf16* __restrict__ W, int64_t ldw,
                                                                void* __restrict__ Y, int64_t ldy, int M, int N,
                                                                int K) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MT, K]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kv = K / 8;
-  for (int i = tid; i < MT * kv; i += blockDim.x) {
-    const int r = i / kv, c = i % kv;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < M) v = *reinterpret_cast<const uint4*>(X + r * ldx + c * 8);
-    reinterpret_cast<uint4*>(xs)[i] = v;
-  }
-  __syncthreads();
-  const int n0 = (blockIdx.x * kGemvWarps + warp) * kCols;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * COLS;
   if (n0 >= N) return;
-  float acc[MT][kCols];
+  const int kv = K / 8;
+  float acc[MT][COLS];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < kCols; ++c) acc[m][c] = 0.f;
-  for (int k = lane; k < kv; k += 32) {
-    uint4 wv[kCols];
+    for (int c = 0; c < COLS; ++c) acc[m][c] = 0.f;
+  for (int base = lane; base < kv; base += 32 * kGemvUnroll) {
+    uint4 wv[kGemvUnroll][COLS];
 #pragma unroll
-    for (int c = 0; c < kCols; ++c)
-      wv[c] = (n0 + c < N) ? __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + c) * ldw) + k)
-                           : make_uint4(0, 0, 0, 0);
+    for (int u = 0; u < kGemvUnroll; ++u) {
+      const int k = base + 32 * u;
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      float xf[8];
-      unpack8(reinterpret_cast<const uint4*>(xs)[m * kv + k], xf);
+      for (int c = 0; c < COLS; ++c)
+        wv[u][c] = (k < kv && n0 + c < N) ? __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + c) * ldw) + k)
+                                          : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-      for (int c = 0; c < kCols; ++c) {
-        float wf[8];
-        unpack8(wv[c], wf);
+    for (int u = 0; u < kGemvUnroll; ++u) {
+      const int k = base + 32 * u;
+      if (k >= kv) break;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[m][c] = fmaf(xf[e], wf[e], acc[m][c]);
+      for (int m = 0; m < MT; ++m) {
+        float xf[8];
+        unpack8(m < M ? __ldg(reinterpret_cast<const uint4*>(X + (int64_t)m * ldx) + k) : make_uint4(0, 0, 0, 0),
+                xf);
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) {
+          float wf[8];
+          unpack8(wv[u][c], wf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m][c] = fmaf(xf[e], wf[e], acc[m][c]);
+        }
       }
     }
   }
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < kCols; ++c) acc[m][c] = warp_sum(acc[m][c]);
+    for (int c = 0; c < COLS; ++c) acc[m][c] = warp_sum(acc[m][c]);
   if (lane == 0) {
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m >= M) break;
 #pragma unroll
-      for (int c = 0; c < kCols; ++c) {
+      for (int c = 0; c < COLS; ++c) {
         if (n0 + c >= N) break;
         if (OUT_F32)
           reinterpret_cast<float*>(Y)[m * ldy + n0 + c] = acc[m][c];
@@ -82,20 +88,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
   }
 }
 
+// Two columns per warp at 8 rows, where the activation reads would otherwise outweigh the weight stream in the cache.
 template <int MT>
 static int launch_gemv(const GemmDesc& g, cudaStream_t s) {
-  const int cols_per_block = kGemvWarps * kCols;
-  dim3 grid(cdiv(g.N, cols_per_block));
-  size_t smem = (size_t)MT * g.K * sizeof(bf16);
-  if (g.y_f32) {
-    if (smem > 48 * 1024)
-      M3_CUDA(cudaFuncSetAttribute(gemv_kernel<MT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    gemv_kernel<MT, true><<<grid, kGemvWarps * 32, smem, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
-  } else {
-    if (smem > 48 * 1024)
-      M3_CUDA(cudaFuncSetAttribute(gemv_kernel<MT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    gemv_kernel<MT, false><<<grid, kGemvWarps * 32, smem, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
-  }
+  constexpr int COLS = MT >= 8 ? 2 : 1;
+  dim3 grid(cdiv(g.N, kGemvWarps * COLS));
+  if (g.y_f32)
+    gemv_kernel<MT, COLS, true><<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+  else
+    gemv_kernel<MT, COLS, false><<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
   M3_LAUNCHED();
   return M3_OK;
 }
