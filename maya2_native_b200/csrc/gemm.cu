@@ -18,14 +18,14 @@ namespace m3 {
 // ------------------------------------------------------------------------------------------------ GEMV
 // One warp produces COLS consecutive output columns for all MT rows; lanes split K in 8-element (16 B) chunks, lane l
 // taking chunks l, l + 32, ...  A CTA is kGemvWarps warps, so even a 1024-wide layer runs 256 CTAs over the 148 SMs,
-// and each lane keeps kGemvUnroll chunks of every column's weight row in flight: the weight stream is bound by HBM,
+// and each lane keeps UNROLL chunks of every column's weight row in flight (8 for rows of 2048+ elements, else 4,
+// which is all of a 1024-element row): the weight stream is bound by HBM,
 // not by the few CTAs a wider column block would give.  The activation rows (at most 8 x K, read by every warp) come
 // through the read-only data cache.  Per output the chunks are accumulated in order and reduced across the warp by
 // the same shuffle tree at any MT or COLS.
 constexpr int kGemvWarps = 4;
-constexpr int kGemvUnroll = 4;
 
-template <int MT, int COLS, bool OUT_F32>
+template <int MT, int COLS, int UNROLL, bool OUT_F32>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __restrict__ X, int64_t ldx,
                                                                const bf16* __restrict__ W, int64_t ldw,
                                                                void* __restrict__ Y, int64_t ldy, int M, int N,
@@ -39,10 +39,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int c = 0; c < COLS; ++c) acc[m][c] = 0.f;
-  for (int base = lane; base < kv; base += 32 * kGemvUnroll) {
-    uint4 wv[kGemvUnroll][COLS];
+  for (int base = lane; base < kv; base += 32 * UNROLL) {
+    uint4 wv[UNROLL][COLS];
 #pragma unroll
-    for (int u = 0; u < kGemvUnroll; ++u) {
+    for (int u = 0; u < UNROLL; ++u) {
       const int k = base + 32 * u;
 #pragma unroll
       for (int c = 0; c < COLS; ++c)
@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
                                           : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kGemvUnroll; ++u) {
+    for (int u = 0; u < UNROLL; ++u) {
       const int k = base + 32 * u;
       if (k >= kv) break;
 #pragma unroll
@@ -89,14 +89,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
 }
 
 // Two columns per warp at 8 rows, where the activation reads would otherwise outweigh the weight stream in the cache.
-template <int MT>
-static int launch_gemv(const GemmDesc& g, cudaStream_t s) {
+template <int MT, int UNROLL>
+static void launch_gemv_u(const GemmDesc& g, cudaStream_t s) {
   constexpr int COLS = MT >= 8 ? 2 : 1;
   dim3 grid(cdiv(g.N, kGemvWarps * COLS));
   if (g.y_f32)
-    gemv_kernel<MT, COLS, true><<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+    gemv_kernel<MT, COLS, UNROLL, true>
+        <<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
   else
-    gemv_kernel<MT, COLS, false><<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+    gemv_kernel<MT, COLS, UNROLL, false>
+        <<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+}
+
+template <int MT>
+static int launch_gemv(const GemmDesc& g, cudaStream_t s) {
+  if (g.K >= 2048)
+    launch_gemv_u<MT, 8>(g, s);
+  else
+    launch_gemv_u<MT, 4>(g, s);
   M3_LAUNCHED();
   return M3_OK;
 }
