@@ -408,6 +408,40 @@ M3_API int m3_guard_step(const m3_guard_config* cfg, const m3_guard_state* st, c
  * the readout's stop column carries the packed verdicts.  Call before capturing the tick into a graph. */
 M3_API int m3_tick_set_guard(m3_tick* t, const m3_guard_config* cfg, const m3_guard_state* st);
 
+/* ---------------------------------------------------------------------------------------------- slot reset */
+/* The device half of binding a request to a slot (maya3/engine.py:420-447, Engine._bind) as one launch: the cb0
+ * sampler's per-slot state (frames, minimum frames, hazard, AEOS bias, seed, counter, repetition history set to -1,
+ * temperature, top-k, top-p, repetition penalty), the depth sampler's stream seed and counter, the slot's depth
+ * speaker constant (copied from cross_src) and its backbone length.  The state pointers are the per-slot tensors the
+ * sampler, depth and backbone objects were created with ([max_slots + 1] rows each; hist [max_slots + 1, hist_len],
+ * cross_const [max_slots + 1, cross_elems] bf16 with cross_elems a multiple of 8).  The Mimi state has its own reset
+ * (m3_mimi_reset). */
+typedef struct {
+  int64_t *frames, *min_frames;
+  float *hazard, *aeos_bias;
+  int32_t *seed, *ctr;
+  int64_t* hist;
+  int32_t hist_len;
+  float* temp;
+  int64_t* top_k;
+  float *top_p, *rep;
+  int32_t *row_seed, *row_ctr;
+  void* cross_const;
+  int32_t cross_elems;
+  int64_t* lengths;
+  int32_t max_slots;
+} m3_slot_state;
+
+typedef struct {
+  int32_t slot, seed, row_seed, min_frames;
+  int64_t top_k, length;
+  float temp, top_p, rep;
+  const void* cross_src; /* [cross_elems] bf16 */
+} m3_slot_init;
+
+/* slot must lie in [0, max_slots) (the padding slot is never bound); cross_src and cross_const 16-byte aligned. */
+M3_API int m3_slot_reset(const m3_slot_state* st, const m3_slot_init* init, m3_stream stream);
+
 /* ---------------------------------------------------------------------------------------------- readout */
 /* The engine's per-tick readout (maya3/engine.py:557-561): packed [rows, 2 + spf / 4] int64 rows holding
  * (stop code, cb0, PCM as int16 = round(clamp(pcm, -1, 1) * 32767)). */

@@ -42,6 +42,18 @@ class Cb0State(C.Structure):
                 ("top_k", vp), ("top_p", vp), ("rep", vp), ("seed", vp), ("ctr", vp), ("hist", vp)]
 
 
+class SlotState(C.Structure):
+    _fields_ = [("frames", vp), ("min_frames", vp), ("hazard", vp), ("aeos_bias", vp), ("seed", vp), ("ctr", vp),
+                ("hist", vp), ("hist_len", i32), ("temp", vp), ("top_k", vp), ("top_p", vp), ("rep", vp),
+                ("row_seed", vp), ("row_ctr", vp), ("cross_const", vp), ("cross_elems", i32), ("lengths", vp),
+                ("max_slots", i32)]
+
+
+class SlotInit(C.Structure):
+    _fields_ = [("slot", i32), ("seed", i32), ("row_seed", i32), ("min_frames", i32), ("top_k", i64),
+                ("length", i64), ("temp", f32), ("top_p", f32), ("rep", f32), ("cross_src", vp)]
+
+
 class GuardConfig(C.Structure):
     _fields_ = [("loop", i32), ("stall", i32), ("period_win", i32), ("period_thr", C.c_double), ("pmin", i32),
                 ("pmax", i32), ("start", i32), ("every", i32), ("mode", i32), ("boost", f32), ("backstop", i32),
@@ -129,6 +141,7 @@ SIGNATURES = {
     "m3_tick_create": (C.c_int, [P(TickConfig), P(vp)]),
     "m3_tick_destroy": (C.c_int, [vp]),
     "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
+    "m3_slot_reset": (C.c_int, [P(SlotState), P(SlotInit), vp]),
     "m3_tick_run_main": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp]),
     "m3_tick_stage_codec": (C.c_int, [vp, vp, i32, i32, i32, vp]),
     "m3_tick_run_codec": (C.c_int, [vp, i32, i32, vp, vp]),

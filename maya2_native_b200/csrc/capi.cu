@@ -60,6 +60,30 @@ __global__ void selftest_timeout_kernel(int polls, int* status) {
   mbar_arrive(&bar);  // complete the phase so the barrier is left in a finished state
 }
 
+// One request's slot, every field in one launch (m3_slot_reset).
+__global__ void slot_reset_kernel(const m3_slot_state st, const m3_slot_init in) {
+  const int s = in.slot;
+  if (threadIdx.x == 0) {
+    st.frames[s] = 0;
+    st.min_frames[s] = in.min_frames;
+    st.hazard[s] = 0.f;
+    st.aeos_bias[s] = 0.f;
+    st.seed[s] = in.seed;
+    st.ctr[s] = 0;
+    st.temp[s] = in.temp;
+    st.top_k[s] = in.top_k;
+    st.top_p[s] = in.top_p;
+    st.rep[s] = in.rep;
+    st.row_seed[s] = in.row_seed;
+    st.row_ctr[s] = 0;
+    st.lengths[s] = in.length;
+  }
+  for (int i = threadIdx.x; i < st.hist_len; i += blockDim.x) st.hist[(int64_t)s * st.hist_len + i] = -1;
+  const uint4* src = reinterpret_cast<const uint4*>(in.cross_src);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.cross_const) + (int64_t)s * st.cross_elems);
+  for (int i = threadIdx.x; i < st.cross_elems / 8; i += blockDim.x) dst[i] = src[i];
+}
+
 }  // namespace m3
 
 extern "C" int m3_selftest_timeout(int32_t polls, int32_t* status) {
@@ -87,6 +111,23 @@ extern "C" int m3_pack_readout(const int64_t* code, const int64_t* cb0, const fl
   M3_REQUIRE(spf % 4 == 0 && rows >= 0, M3_ERR_ARG, "m3_pack_readout: spf %d not a multiple of 4", spf);
   if (rows == 0) return M3_OK;
   m3::pack_readout_kernel<<<rows, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(code, cb0, pcm, packed, spf);
+  M3_LAUNCHED();
+  return M3_OK;
+}
+
+extern "C" int m3_slot_reset(const m3_slot_state* st, const m3_slot_init* init, m3_stream stream) {
+  M3_REQUIRE(st && init && st->frames && st->min_frames && st->hazard && st->aeos_bias && st->seed && st->ctr &&
+                 st->hist && st->temp && st->top_k && st->top_p && st->rep && st->row_seed && st->row_ctr &&
+                 st->cross_const && st->lengths && init->cross_src,
+             M3_ERR_ARG, "m3_slot_reset: null argument");
+  M3_REQUIRE(init->slot >= 0 && init->slot < st->max_slots, M3_ERR_RANGE, "m3_slot_reset: slot %d outside [0, %d)",
+             init->slot, st->max_slots);
+  M3_REQUIRE(st->hist_len >= 0 && st->cross_elems >= 0 && st->cross_elems % 8 == 0 &&
+                 (reinterpret_cast<uintptr_t>(st->cross_const) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(init->cross_src) & 15) == 0,
+             M3_ERR_ARG, "m3_slot_reset: speaker constant of %d elements must be 16-byte aligned rows",
+             st->cross_elems);
+  m3::slot_reset_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*st, *init);
   M3_LAUNCHED();
   return M3_OK;
 }

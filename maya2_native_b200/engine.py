@@ -255,7 +255,12 @@ class TickEngine:
         self._inflight = None       # (plan, host rows, event) of the pipelined tick not yet delivered
         self._early = set()         # ids of seats whose slots were released before their last tick was read
         self._readout = None
-        self._custom = set()        # slots whose cb0 sampling values a request overrode
+        c, d = self.cb0, self.depth
+        self._slot_state = L.SlotState(
+            c.frames_t.data_ptr(), c.min_t.data_ptr(), c.hazard_t.data_ptr(), c.aeos_bias.data_ptr(),
+            c.seed_t.data_ptr(), c.ctr_t.data_ptr(), c.hist_t.data_ptr(), c.hist_t.shape[1], c.temp_t.data_ptr(),
+            c.topk_t.data_ptr(), c.topp_t.data_ptr(), c.rep_t.data_ptr(), d.row_seed.data_ptr(), d.row_ctr.data_ptr(),
+            d.cross_const.data_ptr(), d.cross_const[0].numel(), self.backbone.lengths.data_ptr(), n)
         self.stats = {"ticks": 0, "admitted": 0, "completed": 0, "frames": 0, "prefill_rows": 0,
                       "eager_prefill_rows": 0}
 
@@ -335,32 +340,20 @@ class TickEngine:
         """The device half of binding a seat: sampler, depth, codec and backbone state of its slot (stream-ordered,
         no host sync)."""
         slot = s.slot
-        c = self.cb0
-        c.frames_t[slot] = 0
-        c.min_t[slot] = self.cfg.min_frames
-        c.hazard_t[slot] = 0
-        c.aeos_bias[slot] = 0
-        c.seed_t[slot] = s.seed
-        c.ctr_t[slot] = 0
-        c.hist_t[slot] = -1
-        if s.sampling or slot in self._custom:     # maya3/engine.py:438-446; default slots keep the create values
-            sp, cfg = s.sampling, self.cfg
-            c.temp_t[slot] = float(sp.get("temperature") or cfg.cb0_temp)
-            c.topk_t[slot] = int(sp.get("top_k") or cfg.cb0_top_k)
-            c.topp_t[slot] = float(sp.get("top_p") or cfg.cb0_top_p)
-            c.rep_t[slot] = float(sp["repetition_penalty"] if sp.get("repetition_penalty") is not None
-                                  else cfg.cb0_rep)
-            if float(sp.get("top_p") or 1.0) < 1.0:
-                c.any_top_p = True
-            if sp.get("repetition_penalty"):
-                c.any_rep = True
-            (self._custom.add if sp else self._custom.discard)(slot)
-        self.depth.row_seed[slot] = (s.seed * 69069 + 1) % (2 ** 31 - 1)
-        self.depth.row_ctr[slot] = 0
-        self.depth.cross_const[slot] = self.voice_const
+        c, sp, cfg = self.cb0, s.sampling, self.cfg
+        # maya3/engine.py:427-446: sampler, depth stream and backbone state of the slot in one launch; the request's
+        # cb0 sampling overrides (or the engine's values) and the depth stream seed derived from its seed
+        rep = float(sp["repetition_penalty"] if sp.get("repetition_penalty") is not None else cfg.cb0_rep)
+        init = L.SlotInit(slot, s.seed, (s.seed * 69069 + 1) % (2 ** 31 - 1), cfg.min_frames,
+                          int(sp.get("top_k") or cfg.cb0_top_k), 0, float(sp.get("temperature") or cfg.cb0_temp),
+                          float(sp.get("top_p") or cfg.cb0_top_p), rep, self.voice_const.data_ptr())
+        L.check(L.load().m3_slot_reset(self._slot_state, init, L.stream_ptr()), "m3_slot_reset")
+        if float(sp.get("top_p") or 1.0) < 1.0:
+            c.any_top_p = True
+        if sp.get("repetition_penalty"):
+            c.any_rep = True
         with torch.cuda.stream(self.codec_stream):     # ordered between the codec parts of two ticks
             self.codec._reset_row(slot)
-        self.backbone.lengths[slot] = 0
         if s.voice is not None:       # maya3/engine.py:488-491: the prefix KV, then the prompt after it
             self.backbone.load_prefix_store(slot, s.voice.store, s.voice.length)
         if self.guards is not None:
