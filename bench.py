@@ -71,7 +71,7 @@ def args_():
                     help="print the device time of each stage of a decode tick (backbone, cb0, depth, Mimi) at the "
                          "configs[2] steady state, each stage called through its own mirror object, and exit")
     ap.add_argument("--profile-ticks", type=int, default=0,
-                    help="after warm-up, run this many ticks inside cudaProfilerStart/Stop (for ncu "
+                    help="after warm-up, run this many decode-only ticks inside cudaProfilerStart/Stop (for ncu "
                          "--profile-from-start off) and exit")
     return ap.parse_args()
 
@@ -213,14 +213,18 @@ def run_native(a, rank, world, local):
         eng.tick()
         top_up(eng, wl)
     if a.profile_ticks:
+        # decode-only ticks, the common kind (the queue is held back, so nothing is admitted), with their graph
+        # captured by an untimed tick before the profiled region
+        held, eng.pending = eng.pending, []
+        eng.tick()
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStart()
         for _ in range(a.profile_ticks):
             eng.tick()
-            top_up(eng, wl)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
-        return {"profiled_ticks": a.profile_ticks}
+        eng.pending = held
+        return {"profiled_ticks": a.profile_ticks, "kind": "decode-only"}
 
     # ---- device-resident run: plan K ticks on the host, stage them in HBM, replay back to back
     plans = []
@@ -233,7 +237,7 @@ def run_native(a, rank, world, local):
         top_up(eng, wl)
         plans.append(tp)
     for tp in plans:
-        eng.graph_of(tp)
+        eng.graph_for(tp.rows, tp.seats, tp.ctx)
         for k in (0, 1):
             eng.codec_for(tp.seats, k)
     staged = torch.from_numpy(np.concatenate([tp.plan for tp in plans])).to(dev)
@@ -253,7 +257,7 @@ def run_native(a, rank, world, local):
         for k, tp in enumerate(plans):
             for s in tp.new:
                 eng.reset_slot(s)
-            gr = eng.graph_of(tp)
+            gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
             gr.plan.copy_(staged[offs[k]:offs[k + 1]], non_blocking=True)
             cg = eng.replay_tick(gr, tp)      # main part here, codec part on the codec stream beside the next tick
             launches += gr.launches + cg.launches
@@ -280,7 +284,6 @@ def run_native(a, rank, world, local):
     # the buckets these ticks can reach (any admission rows at the full seat bucket, the two largest context buckets)
     # are captured first and W public ticks run untimed, so no graph is captured inside the timed window.
     for cb in eng.ctx_buckets[-2:]:
-        eng.graph_for(eng.buckets[-1], eng.buckets[-1], cb, decode=True)
         for rb in (r for r in eng.row_buckets if r >= eng.buckets[-1]):
             eng.graph_for(rb, eng.buckets[-1], cb)
     for k in (0, 1):
@@ -321,9 +324,9 @@ def run_native(a, rank, world, local):
 
     # ---- roofline of the decode attention on the live cache (the last tick's rows)
     tp = eng.make_plan(list(eng.active), [])
-    gr = eng.graph_of(tp)
+    gr = eng.graph_for(tp.rows, tp.seats, tp.ctx)
     gr.plan.copy_(torch.from_numpy(tp.plan).to(dev))
-    eng.replay_tick(gr, tp)     # leaves this step's slots, positions and q|k|v in the scratch
+    eng.replay_tick(gr, tp)     # leaves this step's q / slots / positions in the scratch
     eng.commit(tp)
     eng.deliver_forced(tp.dec)
     bg = g.backbone
@@ -429,7 +432,6 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=12.0, warm=10.0):
     tc = time.perf_counter()
     for cb in eng.ctx_buckets[-2:]:
         for sb in eng.buckets:
-            eng.graph_for(sb, sb, cb, decode=True)
             for rb in (r for r in eng.row_buckets if r >= sb):
                 eng.graph_for(rb, sb, cb)
     for sb in eng.buckets:

@@ -115,12 +115,6 @@ M3_API int m3_backbone_destroy(m3_backbone* bb);
  * any row attends, so prefill rows form an exact causal prefill (fast_backbone.py:326-333). */
 M3_API int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* offsets, const int64_t* real,
                      const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream);
-/* m3_backbone_step for a step of decode rows only (StaticBackbone.step, serve/fast_backbone.py:289-315): each row is
- * one slot's next position (no inline prompt; each slot at most once, padding rows on the dummy slot).  Each layer's
- * q/k head RMSNorm, RoPE and K/V cache write (fast_backbone.py:62-92) run inside its attention launch, one launch
- * per layer fewer; same results, bit for bit. */
-M3_API int m3_backbone_step_decode(m3_backbone* bb, const int64_t* slots, const int64_t* real, const void* x,
-                                   void* out, int32_t rows, int32_t ctx, m3_stream stream);
 /* Read (and optionally clear) the device status word; synchronises with the device. */
 M3_API int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clear);
 /* Voice prefix KV (maya3/engine.py:276-280, serve/fast_backbone.py:316-322): copy the first `length` positions of
@@ -132,9 +126,8 @@ M3_API int m3_backbone_load_prefix(m3_backbone* bb, int32_t slot, const void* st
                                    m3_stream stream);
 /* Measurement hook: re-run layer `layer`'s decode attention (split-KV pass + combine) on the queries, slots and
  * positions the last m3_backbone_step left in the handle's scratch (rows and ctx as that step), to time the kernel
- * on the live cache (rows beyond any step's are rejected with M3_ERR_RANGE).  After m3_backbone_step_decode it runs
- * that step's form (query heads normed and roped in the launch, from the last layer's q|k|v scratch) without its
- * K/V writes.  Overwrites only the handle's attention output scratch. */
+ * on the live cache (rows beyond any step's are rejected with M3_ERR_RANGE).  Overwrites only the handle's attention
+ * output scratch. */
 M3_API int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream);
 /* The attention of m3_backbone_attention with every K/V stage barrier expecting 16 bytes more than its copies bring
  * (rows <= 8), so that every wait in the launch runs out: a test of the kernel's bounded waits, which here give up
@@ -361,10 +354,6 @@ M3_API int m3_tick_run(m3_tick* t, const int64_t* plan, int32_t rows, int32_t se
  * Mimi handle's own workspace.  m3_tick_run = run_main, stage_codec(set 0), run_codec(set 0) on one stream. */
 M3_API int m3_tick_run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
                             int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
-/* m3_tick_run_main for a plan without inline-prefill rows (every row a decode or padding row, offsets 0): the
- * backbone runs as m3_backbone_step_decode.  Same results as m3_tick_run_main on such a plan. */
-M3_API int m3_tick_run_main_decode(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
-                                   int32_t apply_rep, int32_t apply_top_p, m3_stream stream);
 M3_API int m3_tick_stage_codec(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t set,
                                m3_stream stream);
 M3_API int m3_tick_run_codec(m3_tick* t, int32_t seats, int32_t set, int64_t* packed, m3_stream stream);

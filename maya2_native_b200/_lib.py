@@ -110,7 +110,6 @@ SIGNATURES = {
     "m3_backbone_create": (C.c_int, [P(BackboneConfig), P(BackboneWeights), P(vp)]),
     "m3_backbone_destroy": (C.c_int, [vp]),
     "m3_backbone_step": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, vp]),
-    "m3_backbone_step_decode": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, vp]),
     "m3_backbone_status": (C.c_int, [vp, P(i32), i32]),
     "m3_backbone_attention": (C.c_int, [vp, i32, i32, i32, vp]),
     "m3_backbone_attention_selftest": (C.c_int, [vp, i32, i32, i32, vp]),
@@ -144,7 +143,6 @@ SIGNATURES = {
     "m3_tick_run": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     "m3_slot_reset": (C.c_int, [P(SlotState), P(SlotInit), vp]),
     "m3_tick_run_main": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp]),
-    "m3_tick_run_main_decode": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp]),
     "m3_tick_stage_codec": (C.c_int, [vp, vp, i32, i32, i32, vp]),
     "m3_tick_run_codec": (C.c_int, [vp, i32, i32, vp, vp]),
     "m3_tick_outputs": (C.c_int, [vp, P(vp), P(vp), P(vp)]),

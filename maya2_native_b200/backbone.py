@@ -38,7 +38,7 @@ def rope_tables(head_dim: int, capacity: int, theta: float, dtype: torch.dtype):
 
 class _Graph:
     __slots__ = ("graph", "slots", "slots_cpu", "x", "real", "real_cpu", "out", "last", "offset", "offset_cpu",
-                 "offset_dirty", "evt", "decode")
+                 "offset_dirty", "evt")
 
 
 class StaticBackbone:
@@ -100,9 +100,6 @@ class StaticBackbone:
             self.lengths_cpu = [0] * (self.max_slots + 1)
         self.graphs = {}
         self.pool = None
-        # steps of decode rows only run m3_backbone_step_decode (each layer's q/k norm + RoPE + cache write inside
-        # its attention launch); False runs them as plain steps.  Same results either way.
-        self.decode_form = True
         self.max_rows = max(self.batch_buckets)
         self._handle = self._create()
 
@@ -236,24 +233,14 @@ class StaticBackbone:
         raise ValueError(f"{what} {need} exceeds largest bucket {values[-1]}")
 
     def _launch(self, g, cb, stream=None):
-        if g.decode:
-            L.check(L.load().m3_backbone_step_decode(self._handle, g.slots.data_ptr(), g.real.data_ptr(),
-                                                     g.x.data_ptr(), g.out.data_ptr(), g.slots.shape[0], cb,
-                                                     L.stream_ptr(stream)), "m3_backbone_step_decode")
-        else:
-            L.check(L.load().m3_backbone_step(self._handle, g.slots.data_ptr(), g.offset.data_ptr(),
-                                              g.real.data_ptr(), g.x.data_ptr(), g.out.data_ptr(),
-                                              g.slots.shape[0], cb, L.stream_ptr(stream)), "m3_backbone_step")
-
-    def _graph(self, bb, cb, decode):
-        decode = bool(decode and self.decode_form)
-        return self.graphs.get((bb, cb, decode)) or self._capture(bb, cb, decode)
+        L.check(L.load().m3_backbone_step(self._handle, g.slots.data_ptr(), g.offset.data_ptr(), g.real.data_ptr(),
+                                          g.x.data_ptr(), g.out.data_ptr(), g.slots.shape[0], cb,
+                                          L.stream_ptr(stream)), "m3_backbone_step")
 
     @torch.inference_mode()
-    def _capture(self, bb, cb, decode=False):
+    def _capture(self, bb, cb):
         dev = self.device
         g = _Graph()
-        g.decode = decode
         g.slots = torch.full((bb,), self.dummy, dtype=torch.long, device=dev)
         g.real = torch.zeros(bb, dtype=torch.long, device=dev)
         g.offset = torch.zeros(bb, dtype=torch.long, device=dev)
@@ -278,7 +265,7 @@ class StaticBackbone:
             g.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g.graph, pool=self.pool):
                 self._launch(g, cb)
-        self.graphs[bb, cb, decode] = g
+        self.graphs[bb, cb] = g
         return g
 
     @torch.inference_mode()
@@ -286,9 +273,8 @@ class StaticBackbone:
         for bb in sorted(batch_buckets or self.batch_buckets, reverse=True):
             for cb in sorted(ctx_buckets or self.ctx_buckets, reverse=True):
                 cb = min(cb, self.capacity)
-                for decode in {self.decode_form, False}:     # step's form, and step_mixed's with prefills
-                    if (bb, cb, decode) not in self.graphs:
-                        self._capture(bb, cb, decode)
+                if (bb, cb) not in self.graphs:
+                    self._capture(bb, cb)
         torch.cuda.synchronize()
 
     def _run(self, g, cb):
@@ -314,7 +300,7 @@ class StaticBackbone:
             raise ValueError(f"context {need} exceeds capacity {self.capacity}")
         bb = self._bucket(self.batch_buckets, B, "batch")
         cb = self._bucket(self.ctx_buckets, need, "context")
-        g = self._graph(bb, cb, True)
+        g = self.graphs.get((bb, cb)) or self._capture(bb, cb)
         key = tuple(slots)
         if g.offset_dirty:
             g.offset.zero_()
@@ -359,7 +345,7 @@ class StaticBackbone:
             raise ValueError(f"context {need} exceeds capacity {self.capacity}")
         bb = self._bucket(self.batch_buckets, rows, "batch")
         cb = self._bucket(self.ctx_buckets, need, "context")
-        g = self._graph(bb, cb, not prefills)
+        g = self.graphs.get((bb, cb)) or self._capture(bb, cb)
         if g.evt is not None:
             g.evt.synchronize()
         index = list(slots)

@@ -182,36 +182,9 @@ int launch_add_rms(int rows, const bf16* hin, const bf16* a, bf16* hout, bf16* y
 }
 
 // ------------------------------------------------------------------------------------------------ q/k norm + RoPE
-// One head of one row, by one warp (serve/fast_backbone.py:62-92): head RMSNorm with weight w, then RoPE at the row's
-// position (cos / sin rows cr, sr).  Lane l owns dims (2l, 2l+1) of the first half and (64+2l, 64+2l+1) of the second
-// half (rotate-half pairs); returns them packed as bf16 pairs in lo and hi.  Shared by qk_rope_cache_kernel and the
-// decode attention's own prologue, so that both produce the same bits.
-__device__ __forceinline__ void rope_head(const bf16* __restrict__ src, const bf16* __restrict__ w,
-                                          const bf16* __restrict__ cr, const bf16* __restrict__ sr, float eps,
-                                          int lane, uint32_t& lo, uint32_t& hi) {
-  const int D = kHeadDim, half = D / 2;
-  const int d1 = 2 * lane, d2 = half + 2 * lane;
-  const float2 x1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d1));
-  const float2 x2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d2));
-  float ss = x1.x * x1.x + x1.y * x1.y + x2.x * x2.x + x2.y * x2.y;
-  ss = warp_sum(ss);
-  const float inv = 1.f / sqrtf(ss / (float)D + eps);
-  const float2 w1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + d1));
-  const float2 w2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + d2));
-  const float y1a = rbf(rbf(x1.x * inv) * w1.x), y1b = rbf(rbf(x1.y * inv) * w1.y);
-  const float y2a = rbf(rbf(x2.x * inv) * w2.x), y2b = rbf(rbf(x2.y * inv) * w2.y);
-  const float2 c1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cr + d1));
-  const float2 c2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cr + d2));
-  const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sr + d1));
-  const float2 s2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sr + d2));
-  const float o1a = y1a * c1.x - y2a * s1.x, o1b = y1b * c1.y - y2b * s1.y;
-  const float o2a = y2a * c2.x + y1a * s2.x, o2b = y2b * c2.y + y1b * s2.y;
-  lo = pack2(o1a, o1b);
-  hi = pack2(o2a, o2b);
-}
-
 // One warp per (row, head): heads [0, H) are query heads written to q; heads [H, H + KV) are key heads written to
-// the K cache at (slot, kv head, pos) together with the matching value head.
+// the K cache at (slot, kv head, pos) together with the matching value head (serve/fast_backbone.py:62-92).
+// Lane l owns dims (2l, 2l+1) of the first half and (64+2l, 64+2l+1) of the second half (rotate-half pairs).
 __global__ void qk_rope_cache_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ q, bf16* __restrict__ kc,
                                      bf16* __restrict__ vc, int64_t slot_stride, int64_t head_stride,
                                      const int* __restrict__ slot32, const int* __restrict__ pos32,
@@ -224,10 +197,26 @@ __global__ void qk_rope_cache_kernel(const bf16* __restrict__ qkv, bf16* __restr
   const int pos = pos32[row];
   const int D = kHeadDim, half = D / 2;
   const int64_t width = (int64_t)(H + 2 * KV) * D;
+  const bf16* src = qkv + row * width + (int64_t)head * D;
   const int d1 = 2 * lane, d2 = half + 2 * lane;
-  uint32_t lo, hi;
-  rope_head(qkv + row * width + (int64_t)head * D, head < H ? wq : wk, cos + (int64_t)pos * D,
-            sin + (int64_t)pos * D, eps, lane, lo, hi);
+  const float2 x1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d1));
+  const float2 x2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d2));
+  float ss = x1.x * x1.x + x1.y * x1.y + x2.x * x2.x + x2.y * x2.y;
+  ss = warp_sum(ss);
+  const float inv = 1.f / sqrtf(ss / (float)D + eps);
+  const bf16* w = head < H ? wq : wk;
+  const float2 w1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + d1));
+  const float2 w2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + d2));
+  const float y1a = rbf(rbf(x1.x * inv) * w1.x), y1b = rbf(rbf(x1.y * inv) * w1.y);
+  const float y2a = rbf(rbf(x2.x * inv) * w2.x), y2b = rbf(rbf(x2.y * inv) * w2.y);
+  const bf16* cr = cos + (int64_t)pos * D;
+  const bf16* sr = sin + (int64_t)pos * D;
+  const float2 c1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cr + d1));
+  const float2 c2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cr + d2));
+  const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sr + d1));
+  const float2 s2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sr + d2));
+  const float o1a = y1a * c1.x - y2a * s1.x, o1b = y1b * c1.y - y2b * s1.y;
+  const float o2a = y2a * c2.x + y1a * s2.x, o2b = y2b * c2.y + y1b * s2.y;
   bf16* dst;
   if (head < H) {
     dst = q + ((int64_t)row * H + head) * D;
@@ -239,8 +228,8 @@ __global__ void qk_rope_cache_kernel(const bf16* __restrict__ qkv, bf16* __restr
     *reinterpret_cast<uint32_t*>(vc + off + d1) = *reinterpret_cast<const uint32_t*>(vsrc + d1);
     *reinterpret_cast<uint32_t*>(vc + off + d2) = *reinterpret_cast<const uint32_t*>(vsrc + d2);
   }
-  *reinterpret_cast<uint32_t*>(dst + d1) = lo;
-  *reinterpret_cast<uint32_t*>(dst + d2) = hi;
+  *reinterpret_cast<uint32_t*>(dst + d1) = pack2(o1a, o1b);
+  *reinterpret_cast<uint32_t*>(dst + d2) = pack2(o2a, o2b);
 }
 
 // ------------------------------------------------------------------------------------------------ SwiGLU
@@ -345,39 +334,20 @@ constexpr uint32_t kSelftestPolls = 1000;  // m3_backbone_attention_selftest: po
 struct MmaAttnSmem {
   unsigned char stage[4][kMmaStages][kBlkBytes];  // [warp][stage], every box 1024-byte aligned
   uint64_t bar[4][kMmaStages];
-  uint32_t qs[4][kHeadDim / 2];                   // decode-only form: the G <= 4 query heads, normed and roped
   int last;
-};
-
-// Inputs of the decode-only form, which folds the step's q/k head RMSNorm, RoPE and K/V cache write into the
-// attention: the rows' raw q|k|v (the QKV linear's output), the layer's head norms, the RoPE tables and the layer's
-// caches.  kv_write = 0 leaves the caches alone (the measurement hook's re-run of a step's attention).
-struct RopeIn {
-  const bf16* qkv;
-  const bf16* wq;
-  const bf16* wk;
-  const bf16* cos;
-  const bf16* sin;
-  bf16* kc;
-  bf16* vc;
-  int64_t slot_stride, head_stride;
-  float eps;
-  int kv_write;
 };
 constexpr int kMmaAttnSmemBytes = (int)sizeof(MmaAttnSmem) + 1024;  // + alignment slack
 static_assert(kMmaStages * kBlkBytes >= (kQueryVectors * kHeadDim + 2 * kQueryVectors) * 4,
               "a warp's partial (O and m, l of 16 query vectors) fits in its stage buffers");
 
 // One work entry (GROUP: a prompt group of nrows rows; else a decode row, whose arithmetic then has no trace of the
-// group path).  ROPE (decode rows only): the entry computes its own G query heads from the raw q|k|v and, in the CTA
-// whose key range ends at the row's position, writes the row's K and V to the cache before its copies read them.
-template <int G, bool GROUP, bool ROPE>
+// group path).
+template <int G, bool GROUP>
 __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* kmap, const CUtensorMap* vmap,
                                            const bf16* __restrict__ q, const int4 vis, float* __restrict__ part_o,
                                            float2* __restrict__ part_ml, int* __restrict__ tickets,
                                            bf16* __restrict__ out, int nsplit, int chunk, int H, float qscale,
-                                           int* status, int extra_tx, const RopeIn& ri) {
-  static_assert(!(ROPE && GROUP), "the decode-only form serves decode rows");
+                                           int* status, int extra_tx) {
   const int nrows = GROUP ? vis.w : 1;
   const int split = blockIdx.x, kvh = blockIdx.y, row = vis.x;
   const int KV = gridDim.y;
@@ -412,58 +382,12 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
     tma_load_3d(st + 2 * kBoxBytes, vmap, 0, y, zc, bar);
     tma_load_3d(st + 3 * kBoxBytes, vmap, 64, y, zc, bar);
   };
-  // ROPE: the block holding the row's own position (the CTA's last, owned by warp pos_warp as its pos_i-th) waits
-  // for the K/V write below when it is among the first copies
-  const bool writes = ROPE && ri.kv_write && pos + 1 - t0 <= chunk;
-  const int pos_warp = (nblk - 1) & 3, pos_i = (nblk - 1) >> 2;
-  const bool defer = writes && warp == pos_warp && pos_i < kMmaStages;
   if (lane == 0)
-    for (int i = 0; i < min(kMmaStages, nmine); ++i)
-      if (!(defer && i == pos_i)) issue(i);
-  if constexpr (ROPE) {  // warp w: query head w (and w + 4), then the key head, then the value head
-    const int KVn = gridDim.y;
-    const bf16* src = ri.qkv + (int64_t)row * (H + 2 * KVn) * kHeadDim;
-    const bf16* cr = ri.cos + (int64_t)pos * kHeadDim;
-    const bf16* sr = ri.sin + (int64_t)pos * kHeadDim;
-    for (int job = warp; job < G + 2; job += 4) {
-      uint32_t lo, hi;
-      if (job < G) {
-        rope_head(src + (int64_t)(kvh * G + job) * kHeadDim, ri.wq, cr, sr, ri.eps, lane, lo, hi);
-        sm.qs[job][lane] = lo;
-        sm.qs[job][32 + lane] = hi;
-      } else if (writes) {
-        const int64_t off = (int64_t)vis.y * ri.slot_stride + (int64_t)kvh * ri.head_stride + (int64_t)pos * kHeadDim;
-        bf16* dst;
-        if (job == G) {
-          rope_head(src + (int64_t)(H + kvh) * kHeadDim, ri.wk, cr, sr, ri.eps, lane, lo, hi);
-          dst = ri.kc + off;
-        } else {
-          const uint32_t* v = reinterpret_cast<const uint32_t*>(src + (int64_t)(H + KVn + kvh) * kHeadDim);
-          lo = v[lane];
-          hi = v[32 + lane];
-          dst = ri.vc + off;
-        }
-        reinterpret_cast<uint32_t*>(dst)[lane] = lo;
-        reinterpret_cast<uint32_t*>(dst)[32 + lane] = hi;
-        fence_proxy_async_global();  // the stores, before the async proxy's copy of the same block
-      }
-    }
-    __syncthreads();
-    if (defer && lane == 0) issue(pos_i);
-  }
+    for (int i = 0; i < min(kMmaStages, nmine); ++i) issue(i);
 
   // A fragments of Q: this lane holds mma rows g (a0, a2) and g + 8 (a1, a3), dims 16ks + 2t (+8); rows >= QV zero
   uint32_t qa[8][4];
-  if constexpr (ROPE) {  // a decode row: QV = G query heads, from shared memory
-    const uint32_t* qp0 = sm.qs[min(g, QV - 1)];
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = g < QV ? qp0[8 * ks + t] : 0u;
-      qa[ks][1] = 0u;
-      qa[ks][2] = g < QV ? qp0[8 * ks + 4 + t] : 0u;
-      qa[ks][3] = 0u;
-    }
-  } else {
+  {
     const int v0 = min(g, QV - 1), v1 = min(g + 8, QV - 1);
     const uint32_t* qp0 =
         reinterpret_cast<const uint32_t*>(q + ((int64_t)(row + v0 / G) * H + kvh * G + v0 % G) * kHeadDim);
@@ -681,28 +605,24 @@ __device__ __forceinline__ void attn_entry(MmaAttnSmem& sm, const CUtensorMap* k
   }
 }
 
-template <int G, bool ROPE>
+template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_mma_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
     const int4* __restrict__ visit,
     float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ tickets, bf16* __restrict__ out,
-    int nsplit, int chunk, int H, float qscale, int* status, int extra_tx, const RopeIn ri) {
+    int nsplit, int chunk, int H, float qscale, int* status, int extra_tx) {
   static_assert(G <= 8 && kQueryVectors % G == 0, "the query heads of one kv head fill at most 8 of the 16 mma rows");
   extern __shared__ unsigned char smem_raw[];
   MmaAttnSmem& sm =
       *reinterpret_cast<MmaAttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int4 vis = visit[blockIdx.z];  // {first row, slot, last position, rows}
   if (vis.w == 0) return;              // inside a prompt group: the group's first row carries the work
-  if constexpr (ROPE) {                // work lists of decode-only steps hold one-row entries only
-    attn_entry<G, false, true>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale,
-                               status, extra_tx, ri);
-  } else if (vis.w > 1) {
-    attn_entry<G, true, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale,
-                               status, extra_tx, ri);
-  } else {
-    attn_entry<G, false, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale,
-                                status, extra_tx, ri);
-  }
+  if (vis.w > 1)
+    attn_entry<G, true>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status,
+                        extra_tx);
+  else
+    attn_entry<G, false>(sm, &kmap, &vmap, q, vis, part_o, part_ml, tickets, out, nsplit, chunk, H, qscale, status,
+                         extra_tx);
 }
 
 }  // namespace m3
@@ -726,7 +646,6 @@ struct m3_backbone {
   int* pos32 = nullptr;
   int4* visit = nullptr;   // [max_rows] the attention's rows in visiting order (longest first): {row, slot, pos, 0}
   int rows_written = 0;     // rows of slot32/pos32/visit some step has written (bounds the measurement hook)
-  bool last_decode = false; // the last step was a decode-only step (its attention folded in the q/k norm + RoPE)
   int* status = nullptr;
   bf16 *h = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *o = nullptr, *a = nullptr, *gu = nullptr,
        *act = nullptr;
@@ -887,12 +806,9 @@ extern "C" int m3_backbone_create(const m3_backbone_config* cfg, const m3_backbo
     set_error("m3_backbone_create: memset failed");
     return M3_ERR_CUDA;
   }
-  cudaFuncSetAttribute(attn_mma_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
-  cudaFuncSetAttribute(attn_mma_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
-  cudaFuncSetAttribute(attn_mma_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
-  cudaFuncSetAttribute(attn_mma_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
-  cudaFuncSetAttribute(attn_mma_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
-  cudaFuncSetAttribute(attn_mma_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
+  cudaFuncSetAttribute(attn_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
+  cudaFuncSetAttribute(attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
+  cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmemBytes);
   *out = bb;
   return M3_OK;
 }
@@ -911,82 +827,57 @@ extern "C" int m3_backbone_status(m3_backbone* bb, int32_t* status, int32_t clea
   return M3_OK;
 }
 
-// The decode-only form's inputs for layer `layer` (kv_write: whether it writes the rows' K/V).
-static RopeIn rope_in(const m3_backbone* bb, int layer, int kv_write) {
-  const m3_backbone_config& c = bb->c;
-  return RopeIn{bb->qkv, bb->q_norm[layer], bb->k_norm[layer], bb->cos, bb->sin, bb->kc[layer], bb->vc[layer],
-                (int64_t)c.kv_heads * c.capacity * c.head_dim, (int64_t)c.capacity * c.head_dim, c.eps, kv_write};
-}
-
 // extra_tx: bytes each K/V stage barrier expects beyond its copies; 0 except in m3_backbone_attention_selftest.
-// ri: the decode-only form (q/k norm + RoPE + K/V write folded in) when set; q from the step's q scratch otherwise.
-static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s, int extra_tx = 0,
-                     const RopeIn* ri = nullptr) {
+static int attention(m3_backbone* bb, int layer, int rows, int ctx, cudaStream_t s, int extra_tx = 0) {
   const m3_backbone_config& c = bb->c;
   const int G = c.heads / c.kv_heads;
   const int chunk = choose_chunk(rows, ctx, c.kv_heads, bb->max_split);
   const int nsplit = cdiv(ctx, chunk);
   const float qscale = (1.f / sqrtf((float)c.head_dim)) * 1.4426950408889634f;
   dim3 grid(nsplit, c.kv_heads, rows);
-  const RopeIn rin = ri ? *ri : RopeIn{};
-#define M3_ATTN(GG, R)                                                                                        \
-  attn_mma_kernel<GG, R><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                        \
-      bb->kmap[layer], bb->vmap[layer], bb->q, bb->visit, bb->part_o, bb->part_ml, bb->tickets, bb->o, nsplit,  \
-      chunk, c.heads, qscale, bb->status, extra_tx, rin);
-  if (ri) {
-    if (G == 1) {
-      M3_ATTN(1, true)
-    } else if (G == 2) {
-      M3_ATTN(2, true)
-    } else {
-      M3_ATTN(4, true)
-    }
+#define M3_ATTN(GG)                                                                                          \
+  attn_mma_kernel<GG><<<grid, kAttnThreads, kMmaAttnSmemBytes, s>>>(                                         \
+      bb->kmap[layer], bb->vmap[layer], bb->q, bb->visit, bb->part_o, bb->part_ml,    \
+      bb->tickets,                                                                                             \
+      bb->o, nsplit, chunk, c.heads, qscale, bb->status, extra_tx);
+  if (G == 1) {
+    M3_ATTN(1)
+  } else if (G == 2) {
+    M3_ATTN(2)
   } else {
-    if (G == 1) {
-      M3_ATTN(1, false)
-    } else if (G == 2) {
-      M3_ATTN(2, false)
-    } else {
-      M3_ATTN(4, false)
-    }
+    M3_ATTN(4)
   }
 #undef M3_ATTN
   M3_LAUNCHED();
   return M3_OK;
 }
 
-// One step over `rows` rows.  decode: every row is a decode row (no inline prompt; offsets ignored), and each layer's
-// q/k head norm + RoPE + K/V cache write runs inside its attention instead of as a launch of its own.
-static int backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* offsets, const int64_t* real,
-                         const void* x, void* out, int32_t rows, int32_t ctx, cudaStream_t s, bool decode) {
+extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* offsets, const int64_t* real,
+                                const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream) {
+  M3_REQUIRE(bb && slots && x && out, M3_ERR_ARG, "m3_backbone_step: null argument");
   const m3_backbone_config& c = bb->c;
   M3_REQUIRE(rows >= 0 && rows <= c.max_rows, M3_ERR_RANGE, "rows %d outside [0, %d]", rows, c.max_rows);
   M3_REQUIRE(ctx > 0 && ctx <= c.capacity, M3_ERR_RANGE, "ctx %d outside (0, %d]", ctx, c.capacity);
   if (rows == 0) return M3_OK;
   bb->rows_written = std::max(bb->rows_written, (int)rows);
-  bb->last_decode = decode;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int Hd = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
-  M3_TRY(launch_prep_rows(slots, decode ? nullptr : offsets, bb->lengths, rows, c.max_slots, c.capacity,
+  M3_TRY(launch_prep_rows(slots, offsets, bb->lengths, rows, c.max_slots, c.capacity,
                           kQueryVectors / (c.heads / c.kv_heads), bb->slot32, bb->pos32, bb->visit, bb->status, s));
+  const bf16* xin = reinterpret_cast<const bf16*>(x);
   for (int i = 0; i < c.layers; ++i) {
-    // h = x, y = RMSNorm(x) on the first layer (HF Qwen3RMSNorm module); h += a, y = RMSNorm(h) after
+    // h = x, y = RMSNorm(x) on the first layer (HF Qwen3RMSNorm module, one launch); h += a, y = RMSNorm(h) after
     if (i == 0)
-      M3_TRY(launch_add_rms(rows, reinterpret_cast<const bf16*>(x), nullptr, bb->h, bb->y, bb->in_norm[0], c.eps, Hd,
-                            s));
+      M3_TRY(launch_add_rms(rows, xin, nullptr, bb->h, bb->y, bb->in_norm[0], c.eps, Hd, s));
     else
       M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, bb->y, bb->in_norm[i], c.eps, Hd, s));
     M3_TRY(gemm({bb->y, Hd, bb->wqkv[i], Hd, bb->qkv, qkvw, rows, qkvw, Hd, false}, s));
-    if (decode) {
-      const RopeIn ri = rope_in(bb, i, 1);
-      M3_TRY(attention(bb, i, rows, ctx, s, 0, &ri));
-    } else {
-      qk_rope_cache_kernel<<<dim3(rows, cdiv(c.heads + c.kv_heads, 4)), 128, 0, s>>>(
-          bb->qkv, bb->q, bb->kc[i], bb->vc[i], (int64_t)c.kv_heads * c.capacity * c.head_dim,
-          (int64_t)c.capacity * c.head_dim, bb->slot32, bb->pos32, bb->cos, bb->sin, bb->q_norm[i], bb->k_norm[i],
-          c.eps, c.heads, c.kv_heads);
-      M3_LAUNCHED();
-      M3_TRY(attention(bb, i, rows, ctx, s));
-    }
+    qk_rope_cache_kernel<<<dim3(rows, cdiv(c.heads + c.kv_heads, 4)), 128, 0, s>>>(
+        bb->qkv, bb->q, bb->kc[i], bb->vc[i], (int64_t)c.kv_heads * c.capacity * c.head_dim,
+        (int64_t)c.capacity * c.head_dim, bb->slot32, bb->pos32, bb->cos, bb->sin, bb->q_norm[i], bb->k_norm[i],
+        c.eps, c.heads, c.kv_heads);
+    M3_LAUNCHED();
+    M3_TRY(attention(bb, i, rows, ctx, s));
     M3_TRY(gemm({bb->o, c.heads * c.head_dim, bb->wo[i], c.heads * c.head_dim, bb->a, Hd, rows, Hd,
                  c.heads * c.head_dim, false},
                 s));
@@ -1003,18 +894,6 @@ static int backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* o
   return M3_OK;
 }
 
-extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int64_t* offsets, const int64_t* real,
-                                const void* x, void* out, int32_t rows, int32_t ctx, m3_stream stream) {
-  M3_REQUIRE(bb && slots && x && out, M3_ERR_ARG, "m3_backbone_step: null argument");
-  return backbone_step(bb, slots, offsets, real, x, out, rows, ctx, reinterpret_cast<cudaStream_t>(stream), false);
-}
-
-extern "C" int m3_backbone_step_decode(m3_backbone* bb, const int64_t* slots, const int64_t* real, const void* x,
-                                       void* out, int32_t rows, int32_t ctx, m3_stream stream) {
-  M3_REQUIRE(bb && slots && x && out, M3_ERR_ARG, "m3_backbone_step_decode: null argument");
-  return backbone_step(bb, slots, nullptr, real, x, out, rows, ctx, reinterpret_cast<cudaStream_t>(stream), true);
-}
-
 extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t rows, int32_t ctx, m3_stream stream) {
   M3_REQUIRE(bb, M3_ERR_ARG, "m3_backbone_attention: null handle");
   M3_REQUIRE(layer >= 0 && layer < bb->c.layers && rows > 0 && rows <= bb->c.max_rows && ctx > 0 &&
@@ -1022,10 +901,6 @@ extern "C" int m3_backbone_attention(m3_backbone* bb, int32_t layer, int32_t row
              M3_ERR_RANGE, "m3_backbone_attention: layer %d rows %d ctx %d out of range", layer, rows, ctx);
   M3_REQUIRE(rows <= bb->rows_written, M3_ERR_RANGE,
              "m3_backbone_attention: rows %d beyond the %d rows a backbone step has set up", rows, bb->rows_written);
-  if (bb->last_decode) {  // the decode-only form as the step ran it, minus its K/V writes (the cache stays as is)
-    const RopeIn ri = rope_in(bb, layer, 0);
-    return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream), 0, &ri);
-  }
   return attention(bb, layer, rows, ctx, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -162,8 +162,8 @@ extern "C" int m3_tick_status(m3_tick* t, int32_t* status, int32_t clear) {
   return M3_OK;
 }
 
-static int run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx, int32_t apply_rep,
-                    int32_t apply_top_p, m3_stream stream, bool decode) {
+extern "C" int m3_tick_run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
+                                int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
   M3_REQUIRE(t && plan, M3_ERR_ARG, "m3_tick_run_main: null argument");
   const m3_tick_config& c = t->c;
   M3_REQUIRE(rows >= 0 && rows <= c.max_rows && seats >= 0 && seats <= c.max_seats, M3_ERR_RANGE,
@@ -181,10 +181,7 @@ static int run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats
     gather_inputs_kernel<<<rows, 128, 0, s>>>(r_slot, r_tok, (const bf16*)c.feedback, (const bf16*)c.embed,
                                               c.vocab, t->x, D, c.max_slots, t->status);
     M3_LAUNCHED();
-    if (decode)
-      M3_TRY(m3_backbone_step_decode(c.bb, r_slot, r_real, t->x, t->out, rows, ctx, stream));
-    else
-      M3_TRY(m3_backbone_step(c.bb, r_slot, r_off, r_real, t->x, t->out, rows, ctx, stream));
+    M3_TRY(m3_backbone_step(c.bb, r_slot, r_off, r_real, t->x, t->out, rows, ctx, stream));
   }
   if (seats == 0) return M3_OK;
   gather_rows_kernel<<<seats, 128, 0, s>>>(t->out, s_row, rows > 0 ? rows : 1, t->h, D);
@@ -195,16 +192,6 @@ static int run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats
   scatter_rows_kernel<<<seats, 128, 0, s>>>(t->fb, s_slot, seats, c.max_slots - 1, (bf16*)c.feedback, D);
   M3_LAUNCHED();
   return M3_OK;
-}
-
-extern "C" int m3_tick_run_main(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
-                                int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
-  return run_main(t, plan, rows, seats, ctx, apply_rep, apply_top_p, stream, false);
-}
-
-extern "C" int m3_tick_run_main_decode(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t ctx,
-                                       int32_t apply_rep, int32_t apply_top_p, m3_stream stream) {
-  return run_main(t, plan, rows, seats, ctx, apply_rep, apply_top_p, stream, true);
 }
 
 extern "C" int m3_tick_stage_codec(m3_tick* t, const int64_t* plan, int32_t rows, int32_t seats, int32_t set,

@@ -189,7 +189,7 @@ def plan_layout(dec, new, lengths, row_buckets, seat_buckets, ctx_buckets, dummy
 
 class _Graph:
     """The main part of a tick (backbone through the feedback write-back) for one bucket."""
-    __slots__ = ("graph", "plan", "staging", "evt", "launches", "decode")
+    __slots__ = ("graph", "plan", "staging", "evt", "launches")
 
 
 class _Codec:
@@ -437,19 +437,12 @@ class TickEngine:
             self.stats["prefill_rows"] += len(s.inline)
 
     # ---------------------------------------------------------------- graphs
-    def graph_of(self, tp: TickPlan) -> _Graph:
-        """The main part's graph for a planned tick: the decode-only form when no seat has inline prompt rows."""
-        return self.graph_for(tp.rows, tp.seats, tp.ctx, decode=not tp.new)
-
-    def graph_for(self, rb, sb, cb, decode=False) -> _Graph:
-        """decode: the tick's rows are decode and padding rows only (m3_tick_run_main_decode, whose backbone folds
-        the q/k norm + RoPE + cache write into the attention); a plan with inline prompt rows needs decode=False."""
-        key = (rb, sb, cb, decode) + self.cb0.flags()   # the penalty / top-p switches are baked into a capture
+    def graph_for(self, rb, sb, cb) -> _Graph:
+        key = (rb, sb, cb) + self.cb0.flags()   # the penalty / top-p switches are arguments baked into a capture
         g = self.graphs.get(key)
         if g is not None:
             return g
         g = _Graph()
-        g.decode = decode
         n = 4 * rb + 2 * sb
         dummy = self.cfg.max_seats
         with torch.inference_mode():
@@ -483,8 +476,8 @@ class TickEngine:
 
     def _launch(self, g, rb, sb, cb, stream=None):
         rep, top_p = self.cb0.flags()
-        run = L.load().m3_tick_run_main_decode if g.decode else L.load().m3_tick_run_main
-        L.check(run(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p, L.stream_ptr(stream)), "m3_tick_run_main")
+        L.check(L.load().m3_tick_run_main(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p,
+                                          L.stream_ptr(stream)), "m3_tick_run_main")
 
     def codec_for(self, sb, k) -> _Codec:
         """The codec part for seat bucket `sb` reading input set `k`; its warm-up and capture decode only the dummy
@@ -572,7 +565,7 @@ class TickEngine:
         device->host copy of its packed readout into the next pinned buffer, on the codec stream; the host mirror of
         the KV lengths moves at once.  Returns the tick's (plan, host rows, event recorded after the readout copy)."""
         tp = self.make_plan(dec, new)
-        g = self.graph_of(tp)
+        g = self.graph_for(tp.rows, tp.seats, tp.ctx)
         k = self._set
         self._set ^= 1
         self.codec_for(tp.seats, k)     # captured before this tick's plan lands in g.plan
