@@ -73,6 +73,13 @@ M3_API int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
 /* In place f = bf16(GELU_erf(f)) over n8 groups of 8 bf16 values: the depth and Mimi feed-forward activation
  * (F.gelu on bf16 tensors) as the stages apply it.  For tests. */
 M3_API int m3_gelu_bf16(void* f, int64_t n8, m3_stream stream);
+/* m3_gemm_bf16 with a feed-forward activation in the GEMV kernel's epilogue (m <= 8, 16-byte aligned rows; other
+ * shapes return M3_ERR_UNSUPPORTED): act 1, y = bf16(GELU_erf(bf16(x w^T))) over n columns; act 2, SwiGLU: w holds
+ * n = 2F rows (gate rows, then up rows), y is [m, F] = bf16(bf16(silu(g)) * u) of the bf16 gate and up outputs
+ * (serve/fast_backbone.py:200-202).  Same bits as the unfused layer followed by its activation pass.  The stages
+ * fuse these themselves at small batch; this entry is for tests. */
+M3_API int m3_gemm_bf16_act(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int32_t m,
+                            int32_t n, int32_t k, int32_t act, m3_stream stream);
 
 /* ---------------------------------------------------------------------------------------------- backbone */
 /* Replaces StaticBackbone (serve/fast_backbone.py:111-362): the static-KV Qwen3 decode with per-seat positions. */

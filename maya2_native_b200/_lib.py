@@ -107,6 +107,7 @@ SIGNATURES = {
     "m3_version": (C.c_int, []),
     "m3_launch_count": (i64, []),
     "m3_gemm_bf16": (C.c_int, [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp]),
+    "m3_gemm_bf16_act": (C.c_int, [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp]),
     "m3_backbone_create": (C.c_int, [P(BackboneConfig), P(BackboneWeights), P(vp)]),
     "m3_backbone_destroy": (C.c_int, [vp]),
     "m3_backbone_step": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, vp]),

@@ -243,7 +243,7 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
   unpack8(reinterpret_cast<const uint4*>(gu + r * 2 * F)[c], g);
   unpack8(reinterpret_cast<const uint4*>(gu + r * 2 * F + F)[c], u);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) o[e] = rbf(rbf(g[e] / (1.f + expf(-g[e]))) * u[e]);
+  for (int e = 0; e < 8; ++e) o[e] = rbf(silu_mul1(g[e], u[e]));
   reinterpret_cast<uint4*>(act + r * F)[c] = pack8(o);
 }
 
@@ -882,10 +882,16 @@ extern "C" int m3_backbone_step(m3_backbone* bb, const int64_t* slots, const int
                  c.heads * c.head_dim, false},
                 s));
     M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, bb->y, bb->post_norm[i], c.eps, Hd, s));
-    M3_TRY(gemm({bb->y, Hd, bb->wgu[i], Hd, bb->gu, 2 * c.ffn, rows, 2 * c.ffn, Hd, false}, s));
-    const int64_t nv = (int64_t)rows * (c.ffn / 8);
-    silu_mul_kernel<<<(unsigned)((nv + 255) / 256), 256, 0, s>>>(bb->gu, bb->act, rows, c.ffn);
-    M3_LAUNCHED();
+    GemmDesc gu{bb->y, Hd, bb->wgu[i], Hd, bb->act, c.ffn, rows, 2 * c.ffn, Hd, false};
+    gu.act = kActSwiGLU;
+    if (gemv_path(gu)) {  // a few rows: SwiGLU in the GEMV epilogue
+      M3_TRY(gemm(gu, s));
+    } else {
+      M3_TRY(gemm({bb->y, Hd, bb->wgu[i], Hd, bb->gu, 2 * c.ffn, rows, 2 * c.ffn, Hd, false}, s));
+      const int64_t nv = (int64_t)rows * (c.ffn / 8);
+      silu_mul_kernel<<<(unsigned)((nv + 255) / 256), 256, 0, s>>>(bb->gu, bb->act, rows, c.ffn);
+      M3_LAUNCHED();
+    }
     M3_TRY(gemm({bb->act, c.ffn, bb->wdown[i], c.ffn, bb->a, Hd, rows, Hd, c.ffn, false}, s));
   }
   M3_TRY(launch_add_rms(rows, bb->h, bb->a, bb->h, reinterpret_cast<bf16*>(out), bb->final_norm, c.eps, Hd, s));

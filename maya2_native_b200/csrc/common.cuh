@@ -65,6 +65,13 @@ __device__ __forceinline__ bf16 to_bf(float x) { return __float2bfloat16_rn(x); 
 // Round an fp32 value to the nearest bf16 and return it as fp32 (the reference stores every such intermediate).
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Activations of the feed-forward layers on one value, fp32 in and out (the callers round):
+// GELU, erf form (F.gelu): 0.5 x (1 + erf(x / sqrt 2)); SwiGLU of a bf16 gate / up pair (serve/fast_backbone.py:201-202,
+// F.silu(g) * u in bf16): bf16(silu(g)) * u.  The element-wise kernels and the GEMV epilogues share these, so that
+// a fused and an unfused layer give the same bits.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float silu_mul1(float g, float u) { return rbf(g / (1.f + expf(-g))) * u; }
+
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   f[0] = bf_lo(u.x); f[1] = bf_hi(u.x); f[2] = bf_lo(u.y); f[3] = bf_hi(u.y);
   f[4] = bf_lo(u.z); f[5] = bf_hi(u.z); f[6] = bf_lo(u.w); f[7] = bf_hi(u.w);

@@ -340,7 +340,7 @@ __global__ void gelu_kernel(bf16* __restrict__ f, int64_t n8) {
   float v[8];
   unpack8(reinterpret_cast<const uint4*>(f)[i], v);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = 0.5f * v[e] * (1.f + erff(v[e] * 0.70710678118654752f));
+  for (int e = 0; e < 8; ++e) v[e] = gelu_erf(v[e]);
   reinterpret_cast<uint4*>(f)[i] = pack8(v);
 }
 
@@ -640,10 +640,15 @@ extern "C" int m3_depth_step(m3_depth* d, const int64_t* slots, const void* h, c
         M3_TRY(launch_add_ln(R * Tr, d->x, 1, D, 0, d->ob, nullptr, 0, nullptr, d->x, d->y, d->n2_w[gl + li],
                              d->n2_b[gl + li], c.ln_eps, D, s));
       }
-      M3_TRY(dgemm(d, {d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false}, s));
-      const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
-      gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);
-      M3_LAUNCHED();
+      GemmDesc f1{d->y, D, d->f1[gl + li], D, d->ff, c.ffn, R * Tr, c.ffn, D, false};
+      f1.act = kActGelu;
+      if (!gemv_path(f1)) f1.act = kActNone;  // a few rows: GELU in the GEMV epilogue; else its own pass
+      M3_TRY(dgemm(d, f1, s));
+      if (f1.act == kActNone) {
+        const int64_t n8 = (int64_t)R * Tr * c.ffn / 8;
+        gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(d->ff, n8);
+        M3_LAUNCHED();
+      }
       M3_TRY(dgemm(d, {d->ff, c.ffn, d->f2[gl + li], c.ffn, d->ob, D, R * Tr, D, c.ffn, false}, s));
       // x, y = add_ln(x, f, next n1 (or the final norm), cross[slot][li])
       const bf16* nw = li + 1 < L ? d->n1_w[gl + li + 1] : d->norm_w;

@@ -25,14 +25,19 @@ namespace m3 {
 // the same shuffle tree at any MT or COLS.
 constexpr int kGemvWarps = 4;
 
-template <int MT, int COLS, int UNROLL, bool OUT_F32>
+template <int MT, int COLS, int UNROLL, bool OUT_F32, int ACT>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __restrict__ X, int64_t ldx,
                                                                const bf16* __restrict__ W, int64_t ldw,
                                                                void* __restrict__ Y, int64_t ldy, int M, int N,
                                                                int K) {
+  static_assert(ACT != kActSwiGLU || COLS == 2, "a SwiGLU warp computes one gate and one up column");
+  static_assert(ACT == kActNone || !OUT_F32, "activations write bf16");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kGemvWarps + warp) * COLS;
-  if (n0 >= N) return;
+  // the warp's columns: n0 + c (c < COLS), or with SwiGLU gate row n0 and up row F + n0 of W (F = N / 2)
+  const int wid = blockIdx.x * kGemvWarps + warp;
+  const int n0 = ACT == kActSwiGLU ? wid : wid * COLS;
+  const int cs = ACT == kActSwiGLU ? N / 2 : 1;
+  if (n0 >= (ACT == kActSwiGLU ? N / 2 : N)) return;
   const int kv = K / 8;
   float acc[MT][COLS];
 #pragma unroll
@@ -46,8 +51,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
       const int k = base + 32 * u;
 #pragma unroll
       for (int c = 0; c < COLS; ++c)
-        wv[u][c] = (k < kv && n0 + c < N) ? __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + c) * ldw) + k)
-                                          : make_uint4(0, 0, 0, 0);
+        wv[u][c] = (k < kv && n0 + c * cs < N)
+                       ? __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + c * cs) * ldw) + k)
+                       : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
@@ -76,29 +82,44 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const bf16* __res
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m >= M) break;
+      if constexpr (ACT == kActSwiGLU) {  // the gate and up outputs rounded to bf16 as stored, then combined
+        reinterpret_cast<bf16*>(Y)[m * ldy + n0] = to_bf(silu_mul1(rbf(acc[m][0]), rbf(acc[m][1])));
+      } else {
 #pragma unroll
-      for (int c = 0; c < COLS; ++c) {
-        if (n0 + c >= N) break;
-        if (OUT_F32)
-          reinterpret_cast<float*>(Y)[m * ldy + n0 + c] = acc[m][c];
-        else
-          reinterpret_cast<bf16*>(Y)[m * ldy + n0 + c] = to_bf(acc[m][c]);
+        for (int c = 0; c < COLS; ++c) {
+          if (n0 + c >= N) break;
+          if (OUT_F32)
+            reinterpret_cast<float*>(Y)[m * ldy + n0 + c] = acc[m][c];
+          else if (ACT == kActGelu)
+            reinterpret_cast<bf16*>(Y)[m * ldy + n0 + c] = to_bf(gelu_erf(rbf(acc[m][c])));
+          else
+            reinterpret_cast<bf16*>(Y)[m * ldy + n0 + c] = to_bf(acc[m][c]);
+        }
       }
     }
   }
 }
 
-// Two columns per warp at 8 rows, where the activation reads would otherwise outweigh the weight stream in the cache.
+// Two columns per warp at 8 rows, where the activation reads would otherwise outweigh the weight stream in the cache
+// (and always with SwiGLU: a gate and an up column).
+template <int MT, int UNROLL, int ACT, bool OUT_F32>
+static void launch_gemv_a(const GemmDesc& g, cudaStream_t s) {
+  constexpr int COLS = ACT == kActSwiGLU || MT >= 8 ? 2 : 1;
+  const int warps = ACT == kActSwiGLU ? g.N / 2 : cdiv(g.N, COLS);
+  gemv_kernel<MT, COLS, UNROLL, OUT_F32, ACT>
+      <<<cdiv(warps, kGemvWarps), kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+}
+
 template <int MT, int UNROLL>
 static void launch_gemv_u(const GemmDesc& g, cudaStream_t s) {
-  constexpr int COLS = MT >= 8 ? 2 : 1;
-  dim3 grid(cdiv(g.N, kGemvWarps * COLS));
-  if (g.y_f32)
-    gemv_kernel<MT, COLS, UNROLL, true>
-        <<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+  if (g.act == kActGelu)
+    launch_gemv_a<MT, UNROLL, kActGelu, false>(g, s);
+  else if (g.act == kActSwiGLU)
+    launch_gemv_a<MT, UNROLL, kActSwiGLU, false>(g, s);
+  else if (g.y_f32)
+    launch_gemv_a<MT, UNROLL, kActNone, true>(g, s);
   else
-    gemv_kernel<MT, COLS, UNROLL, false>
-        <<<grid, kGemvWarps * 32, 0, s>>>(g.X, g.ldx, g.W, g.ldw, g.Y, g.ldy, g.M, g.N, g.K);
+    launch_gemv_a<MT, UNROLL, kActNone, false>(g, s);
 }
 
 template <int MT>
@@ -163,12 +184,18 @@ static int launch_cublas(const GemmDesc& g, cudaStream_t s) {
   return M3_OK;
 }
 
-int gemm(const GemmDesc& g, cudaStream_t s) {
-  M3_REQUIRE(g.M >= 0 && g.N > 0 && g.K > 0, M3_ERR_ARG, "gemm: bad shape M=%d N=%d K=%d", g.M, g.N, g.K);
-  if (g.M == 0) return M3_OK;
+bool gemv_path(const GemmDesc& g) {
   const bool vec_ok = g.K % 8 == 0 && g.ldx % 8 == 0 && g.ldw % 8 == 0 &&
                       (reinterpret_cast<uintptr_t>(g.X) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.W) & 15) == 0;
-  if (vec_ok && g.M <= 8 && (size_t)8 * g.K * 2 <= 200 * 1024) {
+  return vec_ok && g.M <= 8 && (size_t)8 * g.K * 2 <= 200 * 1024;
+}
+
+int gemm(const GemmDesc& g, cudaStream_t s) {
+  M3_REQUIRE(g.M >= 0 && g.N > 0 && g.K > 0, M3_ERR_ARG, "gemm: bad shape M=%d N=%d K=%d", g.M, g.N, g.K);
+  M3_REQUIRE(g.act == kActNone || (!g.y_f32 && gemv_path(g) && (g.act != kActSwiGLU || g.N % 2 == 0)),
+             M3_ERR_UNSUPPORTED, "gemm: activation %d needs the GEMV path (M=%d N=%d K=%d)", g.act, g.M, g.N, g.K);
+  if (g.M == 0) return M3_OK;
+  if (gemv_path(g)) {
     if (g.M <= 1) return launch_gemv<1>(g, s);
     if (g.M <= 2) return launch_gemv<2>(g, s);
     if (g.M <= 4) return launch_gemv<4>(g, s);
@@ -186,11 +213,20 @@ extern "C" int m3_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t l
   return m3::gemm(g, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int m3_gemm_bf16_act(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                                int32_t m, int32_t n, int32_t k, int32_t act, m3_stream stream) {
+  M3_REQUIRE(act == m3::kActGelu || act == m3::kActSwiGLU, M3_ERR_ARG, "m3_gemm_bf16_act: activation %d", act);
+  m3::GemmDesc g{reinterpret_cast<const m3::bf16*>(x), ldx, reinterpret_cast<const m3::bf16*>(w), ldw, y, ldy,
+                 m, n, k, false};
+  g.act = act;
+  return m3::gemm(g, reinterpret_cast<cudaStream_t>(stream));
+}
+
 namespace m3 {
 // The GEMV kernel alone (M <= 8), never a library call: for paths that must not allocate (cuBLAS creates its handle
 // and workspace lazily).  Returns M3_ERR_UNSUPPORTED when the shape or alignment does not fit the GEMV kernel.
 int gemv_only(const GemmDesc& g, cudaStream_t s) {
-  const bool ok = g.M >= 0 && g.M <= 8 && g.N > 0 && g.K > 0 && g.K % 8 == 0 && g.ldx % 8 == 0 && g.ldw % 8 == 0 &&
+  const bool ok = g.act == kActNone && g.M >= 0 && g.M <= 8 && g.N > 0 && g.K > 0 && g.K % 8 == 0 && g.ldx % 8 == 0 && g.ldw % 8 == 0 &&
                   (reinterpret_cast<uintptr_t>(g.X) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.W) & 15) == 0 &&
                   (size_t)8 * g.K * 2 <= 48 * 1024;
   M3_REQUIRE(ok, M3_ERR_UNSUPPORTED, "gemv_only: M=%d N=%d K=%d outside the GEMV kernel's range", g.M, g.N, g.K);

@@ -1015,10 +1015,15 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
     scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls1[li], m->y, m->ln2_w[li], m->ln2_b[li], c.norm_eps,
                                              H);
     M3_LAUNCHED();
-    M3_TRY(mgemm(m, {m->y, H, m->fc1[li], H, m->ff, c.ffn, R * T, c.ffn, H, false}, s));
-    const int64_t n8 = (int64_t)R * T * c.ffn / 8;
-    gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(m->ff, n8);
-    M3_LAUNCHED();
+    GemmDesc fc1{m->y, H, m->fc1[li], H, m->ff, c.ffn, R * T, c.ffn, H, false};
+    fc1.act = kActGelu;
+    if (!gemv_path(fc1)) fc1.act = kActNone;  // a few streams: GELU in the GEMV epilogue; else its own pass
+    M3_TRY(mgemm(m, fc1, s));
+    if (fc1.act == kActNone) {
+      const int64_t n8 = (int64_t)R * T * c.ffn / 8;
+      gelu_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(m->ff, n8);
+      M3_LAUNCHED();
+    }
     M3_TRY(mgemm(m, {m->ff, c.ffn, m->fc2[li], c.ffn, m->ob, H, R * T, H, c.ffn, false}, s));
     const bool last = li + 1 == c.layers;
     scale_add_ln_kernel<<<R * T, nb, 0, s>>>(m->h, m->ob, m->ls2[li], m->y, last ? nullptr : m->ln1_w[li + 1],
