@@ -322,6 +322,12 @@ M3_API int m3_mimi_reset(m3_mimi* m, int32_t slot, int32_t zero_kv, m3_stream st
 M3_API int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* codes, float* pcm, int32_t rows,
                    m3_stream stream);
 M3_API int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear);
+/* How many SMs the handle's persistent SEANet kernels (transposed convs and residual blocks of the fused stages)
+ * spread their CTAs over; 0 (the default) or more than the device has: all.  A decoder that runs on a second
+ * stream beside other work (the engine's codec part beside the next tick's main part) leaves the other stream
+ * room this way: its kernels otherwise take every SM for their duration.  Results do not depend on it.  Takes
+ * effect at the next decode; a CUDA graph keeps the grid it was captured with. */
+M3_API int m3_mimi_set_sm_budget(m3_mimi* m, int32_t sms);
 /* Measurement hook: re-run decoder stage `stage`'s fused transposed conv (a stage of the fused SEANet suffix) over
  * `rows` streams on the activation buffers the last decode left, writing the overlap tails to a scratch row instead
  * of the streams' state; *bytes = its algorithmic bytes (bf16 stage input read + stage output written). */

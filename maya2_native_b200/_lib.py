@@ -135,6 +135,7 @@ SIGNATURES = {
     "m3_mimi_reset": (C.c_int, [vp, i32, i32, vp]),
     "m3_mimi_decode": (C.c_int, [vp, vp, vp, vp, i32, vp]),
     "m3_mimi_status": (C.c_int, [vp, P(i32), i32]),
+    "m3_mimi_set_sm_budget": (C.c_int, [vp, i32]),
     "m3_mimi_convt": (C.c_int, [vp, i32, i32, P(C.c_int64), vp]),
     "m3_selftest_timeout": (C.c_int, [i32, P(i32)]),
     "m3_gelu_bf16": (C.c_int, [vp, i64, vp]),

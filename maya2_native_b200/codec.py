@@ -156,6 +156,11 @@ class StaticMimi:
         L.check(L.load().m3_mimi_status(self._handle, s, int(clear)), "m3_mimi_status")
         return int(s.value)
 
+    def set_sm_budget(self, sms: int):
+        """SMs the persistent SEANet kernels spread over (0: all); for a decoder on a second stream beside other
+        work.  Graphs captured afterwards use it; results do not depend on it."""
+        L.check(L.load().m3_mimi_set_sm_budget(self._handle, int(sms)), "m3_mimi_set_sm_budget")
+
     def state_bytes_per_slot(self):
         return {"conv": self.conv_flat[0].numel() * self.conv_flat.element_size(),
                 "attention_kv": self.kv[:, :, 0].numel() * self.kv.element_size(),

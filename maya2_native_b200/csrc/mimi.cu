@@ -562,6 +562,7 @@ struct m3_mimi {
   StateCopy snap_regions{};
   FinalFused fin{};
   bool fin_fused = false;
+  int sm_budget = 0;  // SMs the persistent SEANet kernels spread over (0: all)
   int64_t snap_row = 0;
   void* fws = nullptr;  // repacked transposed-conv weights + the state snapshot
   bf16* snap = nullptr;
@@ -915,7 +916,13 @@ extern "C" int m3_mimi_convt(m3_mimi* m, int32_t stage, int32_t rows, int64_t* b
   ct.state_row = 0;
   ct.tail_off = 0;
   if (bytes) *bytes = ((int64_t)rows * sd.L * sd.cin + (int64_t)rows * sd.L * sd.r * sd.cout) * 2;
-  return launch_convt_fused(ct, rows, reinterpret_cast<cudaStream_t>(stream), m->status);
+  return launch_convt_fused(ct, rows, reinterpret_cast<cudaStream_t>(stream), m->status, m->sm_budget);
+}
+
+extern "C" int m3_mimi_set_sm_budget(m3_mimi* m, int32_t sms) {
+  M3_REQUIRE(m && sms >= 0, M3_ERR_ARG, "m3_mimi_set_sm_budget: null handle or negative budget");
+  m->sm_budget = sms;
+  return M3_OK;
 }
 
 extern "C" int m3_mimi_status(m3_mimi* m, int32_t* status, int32_t clear) {
@@ -1055,8 +1062,8 @@ extern "C" int m3_mimi_decode(m3_mimi* m, const int64_t* slots, const int64_t* c
   for (int i = 0; i < nst; ++i) {
     const StageDims& sd = m->stages[i];
     if (i >= first_fused) {  // e (act0) -> transposed conv -> u (act1) -> residual block -> next e (act0)
-      M3_TRY(launch_convt_fused(m->ct[i - first_fused], R, s, m->status));
-      M3_TRY(launch_res_fused(m->rs[i - first_fused], R, s, m->status));
+      M3_TRY(launch_convt_fused(m->ct[i - first_fused], R, s, m->status, m->sm_budget));
+      M3_TRY(launch_res_fused(m->rs[i - first_fused], R, s, m->status, m->sm_budget));
       x = m->act0;
       continue;
     }

@@ -740,11 +740,12 @@ int seanet_fused_init() {
   return M3_OK;
 }
 
-int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status) {
+int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status, int sms) {
   const int N = p.r * p.cout, BN = convt_bn(N), KT = 2 * p.cin / 64;
+  const int nsm = sms > 0 && sms < g_sms ? sms : g_sms;
   if (convt_persistent_ok(p.cin, p.cout, p.r)) {  // the persistent, weight-resident form (128-column slices)
     const int NC = N / 128, tiles = R * ((p.L + 1 + kUM - 1) / kUM);
-    const int cpc = std::max(1, std::min(tiles, g_sms / NC));
+    const int cpc = std::max(1, std::min(tiles, nsm / NC));
     const dim3 grid(NC * cpc);
     if (KT == 4)
       convt_pers_kernel<128, 4><<<grid, kCpThreads, convt_pers_smem(128, 4), s>>>(
@@ -773,11 +774,12 @@ int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status) 
   return M3_OK;
 }
 
-int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status) {
+int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status, int sms) {
+  const int nsm = sms > 0 && sms < g_sms ? sms : g_sms;
   const int tiles = R * ((p.Lo + kBM - 1) / kBM);
   const size_t smem = res_fused_smem(p.cout, p.hid);
   const int per_sm = std::max(1, p.cout == 64 ? g_res_per_sm[0] : g_res_per_sm[1]);
-  const dim3 grid(std::max(1, std::min(tiles, g_sms * per_sm)));
+  const dim3 grid(std::max(1, std::min(tiles, nsm * per_sm)));
   if (p.cout == 64)
     res_fused_kernel<64, 32><<<grid, kResThreads, smem, s>>>(p.umap, p.w1, p.b1, p.w2, p.b2, p.hist_in, p.in_row, p.state,
                                                      p.state_row, p.hist_off, p.slot32, p.e, p.Lo, R, g_elu_lut, status);

@@ -70,11 +70,12 @@ size_t res_fused_smem(int cout, int hid);
 // Set the kernels' shared-memory limits (once per process and device).
 int seanet_fused_init();
 
-int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status);
+// sms: SMs the persistent forms spread over (0 or above the device's count: all of them).
+int launch_convt_fused(const ConvTFused& p, int R, cudaStream_t s, int* status, int sms = 0);
 // wc[jj*cout + o][k] = k < cin ? wt[(jj + r)*cout + o][k] : wt[jj*cout + o][k - cin], from the transposed conv's
 // [2r * cout][cin] repack (element (j*cout + o, c) = W[c, o, j]).
 int launch_convt_repack(const bf16* wt, int r, int cout, int cin, bf16* wc, cudaStream_t s);
-int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status);
+int launch_res_fused(const ResFused& p, int R, cudaStream_t s, int* status, int sms = 0);
 
 // Snapshot of the stateful rows the fused kernels read (so that they can write the new state in place):
 // for each listed region, dst[b][0 .. len) = state[slot32[b]][off .. off + len).

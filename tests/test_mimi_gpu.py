@@ -77,3 +77,25 @@ def test_many_streams_against_oracle_subset(cuda):
         for i, s in enumerate(pick):
             assert snr_db(got[s], ref[i]) > 30, (f, s, snr_db(got[s], ref[i]))
     assert sm.device_status() == 0
+
+
+def test_sm_budget_changes_no_result(cuda):
+    """The SEANet kernels spread over a few SMs (the engine's codec beside the next tick) give the same PCM, bit for
+    bit, as over all of them: the budget sets the grid of the persistent kernels, not their arithmetic."""
+    g = BASELINE.mimi
+    B = 48
+    W = WG.generate(WG.mimi_shapes(g), seed=4, device=cuda)
+    pcm = {}
+    for sms in (0, 9):
+        sm = StaticMimi(W, B, batch_buckets=(B,), geom=g, device=cuda)
+        sm.set_sm_budget(sms)
+        gen = torch.Generator(device=cuda).manual_seed(9)
+        idx = torch.arange(B, device=cuda)
+        out = []
+        for _ in range(4):
+            codes = torch.randint(0, g.codebook_size, (B, g.n_q), device=cuda, generator=gen)
+            out.append(sm.decode(idx, codes).cpu())
+        assert sm.device_status() == 0
+        pcm[sms] = torch.cat(out)
+        sm.close()
+    assert torch.equal(pcm[0], pcm[9])
