@@ -287,7 +287,8 @@ def run_native(a, rank, world, local):
         for rb in (r for r in eng.row_buckets if r >= eng.buckets[-1]):
             eng.graph_for(rb, eng.buckets[-1], cb)
     for k in (0, 1):
-        eng.codec_for(eng.buckets[-1], k)
+        for beside in (False, True):     # the synchronous and the pipelined loop
+            eng.codec_for(eng.buckets[-1], k, beside)
     def public_run(pipelined):
         """K ticks through the public loop, wall-clocked: tick() (plan, launch, read back, deliver, one tick at a
         time) or tick_pipelined() (tick t+1 launched before tick t is read; the pipeline starts empty and the last
@@ -436,7 +437,7 @@ def run_box(eng, a, rank, world, dev, cap_per_gpu, duration=12.0, warm=10.0):
                 eng.graph_for(rb, sb, cb)
     for sb in eng.buckets:
         for k in (0, 1):
-            eng.codec_for(sb, k)
+            eng.codec_for(sb, k, beside=False)     # the box runs the synchronous loop
     torch.cuda.synchronize()
     print(f"box: rank {rank} captured {len(eng.graphs)} graphs in {time.perf_counter() - tc:.2f} s", file=sys.stderr)
     torch.cuda.synchronize()

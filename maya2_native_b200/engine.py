@@ -55,8 +55,9 @@ class TickConfig:
     min_frames: int = 4
     greedy: bool = False              # depth levels by argmax (FastDepth greedy); cb0 greedy is cb0_top_k = 1
     use_graphs: bool = True
-    # SMs the codec part's persistent SEANet kernels spread over, beside the next tick's main part (None: a quarter
-    # of the device's, 0: all).  Measured on one box: decode ticks 6.82 ms with all SMs, 6.74 ms with a quarter.
+    # SMs the codec part's persistent SEANet kernels spread over when it runs beside the next tick's main part
+    # (tick_pipelined; None: a quarter of the device's, 0: all).  Measured on one box: decode ticks 6.82 ms with all
+    # SMs, 6.74 ms with a quarter.  A synchronous tick runs its codec part alone, on every SM.
     codec_sms: Optional[int] = None
     guards: Optional[GuardConfig] = None   # loop guard + frame cap on the device (maya3/engine.py:69); None = off
 
@@ -197,7 +198,7 @@ class _Graph:
 
 class _Codec:
     """The codec part of a tick (Mimi frame + packed readout) for one seat bucket and codec input set."""
-    __slots__ = ("graph", "packed", "launches")
+    __slots__ = ("graph", "packed", "launches", "beside")
 
 
 class TickEngine:
@@ -220,9 +221,10 @@ class TickEngine:
         self.depth = FastDepth(weights, n, temp=cfg.temp, top_k=cfg.top_k, batch_buckets=self.buckets,
                                seed=cfg.seed + 1, greedy=cfg.greedy, geom=g.depth, device=dev)
         self.codec = StaticMimi(weights, n, batch_buckets=self.buckets, geom=g.mimi, device=dev)
-        sms = cfg.codec_sms if cfg.codec_sms is not None else \
+        # the codec's SM budget when its part runs beside the next tick's main part (pipelined ticks); a synchronous
+        # tick runs it alone, on every SM
+        self._codec_sms = cfg.codec_sms if cfg.codec_sms is not None else \
             torch.cuda.get_device_properties(dev).multi_processor_count // 4
-        self.codec.set_sm_budget(sms)
         D = g.backbone.hidden
         with torch.inference_mode():
             self.embed = weights["model.embed_tokens.weight"].detach().to(dev, torch.bfloat16).contiguous()
@@ -485,14 +487,16 @@ class TickEngine:
         L.check(L.load().m3_tick_run_main(self._handle, g.plan.data_ptr(), rb, sb, cb, rep, top_p,
                                           L.stream_ptr(stream)), "m3_tick_run_main")
 
-    def codec_for(self, sb, k) -> _Codec:
+    def codec_for(self, sb, k, beside=True) -> _Codec:
         """The codec part for seat bucket `sb` reading input set `k`; its warm-up and capture decode only the dummy
-        slot (the set is staged from an all-padding plan first)."""
-        key = (sb, k)
+        slot (the set is staged from an all-padding plan first).  beside: the part runs beside the next tick's main
+        part (pipelined ticks), within the codec's SM budget; else alone (a synchronous tick), on every SM."""
+        key = (sb, k, beside)
         cg = self.codec_graphs.get(key)
         if cg is not None:
             return cg
         cg = _Codec()
+        cg.beside = beside
         lib = L.load()
         with torch.inference_mode():
             cg.packed = torch.zeros(sb, 2 + self.spf // 4, dtype=torch.long, device=self.device)
@@ -525,18 +529,20 @@ class TickEngine:
         return cg
 
     def _launch_codec(self, cg, sb, k, stream=None):
+        self.codec.set_sm_budget(self._codec_sms if cg.beside else 0)     # read when the kernels are launched
         L.check(L.load().m3_tick_run_codec(self._handle, sb, k, cg.packed.data_ptr(), L.stream_ptr(stream)),
                 "m3_tick_run_codec")
 
-    def replay_tick(self, g, tp, k=None):
+    def replay_tick(self, g, tp, k=None, beside=True):
         """Enqueue one planned tick whose plan is already in g.plan: the main part on the current stream, then the
         hand-off of its outputs into codec input set k (after the codec part that last read that set), then the
-        codec part on the codec stream.  Returns the codec part's record."""
+        codec part on the codec stream (beside: within the codec's SM budget, for a part that runs beside the next
+        tick's main part).  Returns the codec part's record."""
         A, B = torch.cuda.current_stream(self.device), self.codec_stream
         if k is None:
             k = self._set
             self._set ^= 1
-        cg = self.codec_for(tp.seats, k)
+        cg = self.codec_for(tp.seats, k, beside)
         if g.graph is not None:
             g.graph.replay()
         else:
@@ -560,13 +566,13 @@ class TickEngine:
 
     def launches_per_tick(self, g, tp):
         """This library's kernels one tick launches (main graph + hand-off + codec graph), None without graphs."""
-        cg = self.codec_graphs.get((tp.seats, 0))
+        cg = self.codec_graphs.get((tp.seats, 0, True)) or self.codec_graphs.get((tp.seats, 0, False))
         if g.launches is None or cg is None or cg.launches is None:
             return None
         return g.launches + 1 + cg.launches
 
     # ---------------------------------------------------------------- tick
-    def _launch_tick(self, dec, new):
+    def _launch_tick(self, dec, new, beside):
         """Plan one tick, copy its plan host->device, enqueue its main and codec parts (replay_tick) and the
         device->host copy of its packed readout into the next pinned buffer, on the codec stream; the host mirror of
         the KV lengths moves at once.  Returns the tick's (plan, host rows, event recorded after the readout copy)."""
@@ -574,14 +580,14 @@ class TickEngine:
         g = self.graph_for(tp.rows, tp.seats, tp.ctx)
         k = self._set
         self._set ^= 1
-        self.codec_for(tp.seats, k)     # captured before this tick's plan lands in g.plan
+        self.codec_for(tp.seats, k, beside)     # captured before this tick's plan lands in g.plan
         if g.evt is not None:
             g.evt.synchronize()     # the pinned staging row may still feed the previous copy
         g.staging.numpy()[:] = tp.plan
         g.plan.copy_(g.staging, non_blocking=True)
         g.evt = torch.cuda.Event()
         g.evt.record()
-        cg = self.replay_tick(g, tp, k)
+        cg = self.replay_tick(g, tp, k, beside)
         n = len(dec) + len(new)
         host = self._hosts[self._flip][:n]
         self._flip ^= 1
@@ -604,7 +610,7 @@ class TickEngine:
         dec = list(self.active)
         if not dec and not new:
             return []
-        tp, host, evt = self._launch_tick(dec, new)
+        tp, host, evt = self._launch_tick(dec, new, beside=False)
         evt.synchronize()
         self._readout = host.numpy()
         return self._deliver(tp.dec + tp.new, self._readout)
@@ -635,7 +641,7 @@ class TickEngine:
             self.active = carried
         new = self._admit()
         if self.active or new:
-            self._inflight = self._launch_tick(list(self.active), new)
+            self._inflight = self._launch_tick(list(self.active), new, beside=True)
         out = self._deliver_inflight(prev) if prev is not None else []
         if self._inflight is not None:
             tp = self._inflight[0]

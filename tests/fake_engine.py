@@ -35,7 +35,7 @@ class FakeDevice:
         self.count[s.slot] = 0
         self.owner[s.slot] = id(s)
 
-    def launch(self, dec, new):
+    def launch(self, dec, new, beside=True):
         eng = self.eng
         tp = eng.make_plan(dec, new)
         seats = dec + new
