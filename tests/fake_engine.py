@@ -29,6 +29,7 @@ class FakeDevice:
         self.count = {}                       # slot -> frames produced since the slot's last bind
         self.owner = {}                       # slot -> id of the seat bound there
         self.ticks = []                       # the seat count of every launched tick
+        self.beside = []                      # per launched tick: its codec part runs beside the next tick's main part
 
     def bind(self, s):
         self.eng._claim(s)
@@ -40,6 +41,7 @@ class FakeDevice:
         tp = eng.make_plan(dec, new)
         seats = dec + new
         self.ticks.append(len(seats))
+        self.beside.append(beside)
         if self.delay:
             time.sleep(self.delay)
         hv = np.zeros((len(seats), 2 + PCM_COLS), np.int64)

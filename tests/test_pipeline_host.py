@@ -59,3 +59,18 @@ def test_synchronous_tick_refuses_while_a_pipelined_tick_is_in_flight():
         eng.tick()
     eng.flush()
     eng.tick()
+
+
+def test_codec_budget_only_for_pipelined_ticks():
+    """A pipelined tick's codec part runs beside the next tick's main part, so it is launched within the codec's SM
+    budget; a synchronous tick's codec part runs alone and keeps every SM."""
+    eng, dev, _ = fake_engine(4)
+    for i in range(3):
+        eng.submit(np.arange(3) + i, 10)
+    eng.tick()
+    eng.tick()
+    eng.tick_pipelined()
+    eng.tick_pipelined()
+    eng.flush()
+    eng.tick()
+    assert dev.beside == [False, False, True, True, False]
