@@ -84,6 +84,12 @@ def test_bad_arguments_map_to_reference_exceptions(lib):
         L.check(lib.m3_tick_create(None, L.vp()), "m3_tick_create")
     with pytest.raises(ValueError):
         L.check(lib.m3_backbone_step(None, None, None, None, None, None, 1, 1, None), "m3_backbone_step")
+    with pytest.raises(ValueError, match="null handle"):
+        L.check(lib.m3_mimi_set_sm_budget(None, 37), "m3_mimi_set_sm_budget")
+    with pytest.raises(ValueError, match="null argument"):
+        L.check(lib.m3_slot_reset(None, None, None), "m3_slot_reset")
+    with pytest.raises(ValueError, match="activation"):
+        L.check(lib.m3_gemm_bf16_act(None, 8, None, 8, None, 8, 1, 8, 8, 3, None), "m3_gemm_bf16_act")
 
 
 def test_unsupported_geometries_are_rejected(lib):
